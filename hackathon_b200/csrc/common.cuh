@@ -1,0 +1,115 @@
+// Shared helpers for the c3b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <string>
+
+#include "c3b200.h"
+
+namespace c3b {
+
+// Thread-local last error (c3b_last_error).
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+
+#define C3B_CHECK_CUDA(expr)                                                    \
+  do {                                                                          \
+    cudaError_t _e = (expr);                                                    \
+    if (_e != cudaSuccess)                                                      \
+      return ::c3b::fail(C3B_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+#define C3B_REQUIRE(cond, msg)                                                  \
+  do {                                                                          \
+    if (!(cond)) return ::c3b::fail(C3B_E_INVALID, msg);                        \
+  } while (0)
+
+inline int64_t numel(const c3b_tensor& t) {
+  int64_t n = 1;
+  for (int i = 0; i < t.ndim; ++i) n *= t.shape[i];
+  return n;
+}
+
+inline size_t dtype_size(int dt) {
+  switch (dt) {
+    case C3B_F32: case C3B_I32: return 4;
+    case C3B_BF16: case C3B_F16: return 2;
+    case C3B_I64: return 8;
+    case C3B_U8: return 1;
+  }
+  return 0;
+}
+
+// Device-side status word: set by kernels whose bounded waits expire.
+extern __device__ int g_status;
+
+__device__ __forceinline__ float load_as_f32(const void* p, int dt, int64_t i) {
+  switch (dt) {
+    case C3B_F32: return static_cast<const float*>(p)[i];
+    case C3B_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    case C3B_F16: return __half2float(static_cast<const __half*>(p)[i]);
+    case C3B_I64: return (float)static_cast<const long long*>(p)[i];
+    case C3B_I32: return (float)static_cast<const int*>(p)[i];
+    default: return static_cast<const unsigned char*>(p)[i];
+  }
+}
+
+__device__ __forceinline__ void store_from_f32(void* p, int dt, int64_t i, float v) {
+  switch (dt) {
+    case C3B_F32: static_cast<float*>(p)[i] = v; break;
+    case C3B_BF16: static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v); break;
+    case C3B_F16: static_cast<__half*>(p)[i] = __float2half_rn(v); break;
+    case C3B_I64: static_cast<long long*>(p)[i] = (long long)v; break;
+    case C3B_I32: static_cast<int*>(p)[i] = (int)v; break;
+    default: static_cast<unsigned char*>(p)[i] = (unsigned char)v; break;
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Exact-erf GELU, the 5-op chain x * 0.5 * (1 + erf(x / sqrt(2))).
+__device__ __forceinline__ float gelu_erf(float x) {
+  return (x * (1.0f + erff(x * 0.70710678118654752f))) * 0.5f;
+}
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == C3B_ACT_RELU) return fmaxf(v, 0.0f);
+  if (act == C3B_ACT_GELU) return gelu_erf(v);
+  return v;
+}
+
+// ---- kernel entry points implemented in the .cu files (host launchers)
+int launch_ew(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_ew_params& p, cudaStream_t s);
+int launch_copy(const c3b_tensor& in, const c3b_tensor& out, const c3b_copy_params& p, cudaStream_t s);
+int launch_im2col(const c3b_tensor& in, const c3b_tensor& out, const c3b_conv_geom& g, cudaStream_t s);
+int launch_reduce(const c3b_tensor& in, const c3b_tensor& out, const c3b_reduce_params& p, cudaStream_t s);
+int launch_layernorm(const c3b_tensor* in, int n_in, const c3b_tensor* out, int n_out,
+                     const c3b_layernorm_params& p, cudaStream_t s);
+int launch_softmax(const c3b_tensor& in, const c3b_tensor& out, const c3b_softmax_params& p, cudaStream_t s);
+int launch_attn_scores(const c3b_tensor* in, const c3b_tensor& out, const c3b_attn_scores_params& p, cudaStream_t s);
+int launch_gather(const c3b_tensor& data, const c3b_tensor& idx, const c3b_tensor& out,
+                  const c3b_gather_params& p, cudaStream_t s);
+int launch_embed(const c3b_tensor* in, const c3b_tensor& out, const c3b_embed_params& p, cudaStream_t s);
+int launch_stem_im2col(const c3b_tensor& in, const c3b_tensor& out, const c3b_stem_params& p, cudaStream_t s);
+int launch_gap_nhwc(const c3b_tensor& in, const c3b_tensor& out, const c3b_gap_params& p, cudaStream_t s);
+int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_params& p, cudaStream_t s);
+int launch_conv_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_params& p, cudaStream_t s);
+int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p, cudaStream_t s);
+int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_tc_params& p, cudaStream_t s);
+int launch_flash_attn(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_flash_params& p, cudaStream_t s);
+
+int sm_count();
+
+}  // namespace c3b

@@ -1,0 +1,252 @@
+// FP32-math SIMT GEMM and implicit-GEMM convolution with fused epilogues.
+//
+// This is the fp32 precision profile's contraction (the reference executes every
+// contraction in FP32: c3_gemm_epilogue at c35/engine.py:798-843, cuBLAS SGEMM via
+// cp.dot at c32/kernel_registry.py:318-358 and c35/engine.py:412).  TF32 tensor
+// cores cannot meet the 1e-4 relative gate against an FP32 reference, so the
+// fp32 profile keeps IEEE FP32 FMAs; the bf16 profile runs on tcgen05
+// (gemm_tc.cu).
+//
+// Tiling: 128x128 CTA tile, BK=16, 256 threads, 8x8 outputs per thread, shared
+// memory double buffer filled from registers.  Operand loaders and the output
+// mapper are template functors, so the same core serves plain/batched GEMM
+// (transA/transB/broadcast batch) and NCHW / NHWC implicit-GEMM convolution (the
+// im2col_f32 -> matmul_f32 -> conv_reshape_f32 -> add_bias_f32 -> relu chain of
+// c32/decompositions.py:301-378 in one launch, with no patch matrix in memory).
+#include "common.cuh"
+
+namespace c3b {
+
+constexpr int BM = 128, BN = 128, BK = 16, NT = 256;
+
+// ---- operand loaders: value(m_or_n, k) as float; KCONTIG says which index is
+// contiguous in memory (drives the thread->element mapping for coalescing).
+
+struct MatLoad {  // A (rows=m) or B^T (rows=n) view of a dense matrix
+  const void* p;
+  int dt;
+  int64_t rows, K, batch_stride;
+  bool trans;  // false: element (r,k) at r*K + k ; true: at k*rows + r
+  __device__ __forceinline__ float get(int b, int64_t r, int64_t k) const {
+    if (r >= rows || k >= K) return 0.f;
+    int64_t off = (int64_t)b * batch_stride + (trans ? k * rows + r : r * K + k);
+    return load_as_f32(p, dt, off);
+  }
+  __device__ __forceinline__ bool kcontig() const { return !trans; }
+};
+
+struct ConvALoad {  // im2col view of the activation, K ordered (c,r,s) for NCHW, (r,s,c) for NHWC
+  const float* x;
+  int n, c, h, w, ho, wo, layout;
+  c3b_conv_geom g;
+  int64_t rows, K;
+  __device__ __forceinline__ float get(int, int64_t m, int64_t k) const {
+    if (m >= rows || k >= K) return 0.f;
+    int ow = (int)(m % wo);
+    int oh = (int)((m / wo) % ho);
+    int img = (int)(m / ((int64_t)wo * ho));
+    int ci, r, s;
+    if (layout == 0) {
+      s = (int)(k % g.kw); r = (int)((k / g.kw) % g.kh); ci = (int)(k / (g.kw * g.kh));
+    } else {
+      ci = (int)(k % c); s = (int)((k / c) % g.kw); r = (int)(k / ((int64_t)c * g.kw));
+    }
+    int ih = oh * g.sh - g.ph0 + r * g.dh;
+    int iw = ow * g.sw - g.pw0 + s * g.dw;
+    if (ih < 0 || ih >= h || iw < 0 || iw >= w) return 0.f;
+    if (layout == 0) return x[(((int64_t)img * c + ci) * h + ih) * w + iw];
+    return x[(((int64_t)img * h + ih) * w + iw) * c + ci];
+  }
+  __device__ __forceinline__ bool kcontig() const { return layout == 1; }
+};
+
+// ---- epilogue / output mapping
+struct Epi {
+  void* out;
+  int dt_out;
+  const float* bias;
+  int bias_mode;
+  const void* res;
+  int dt_res;
+  float alpha, beta;
+  int act;
+  int64_t M, N, batch_stride;
+  // conv output mapping: 0 = row-major [M,N]; 1 = NCHW with HoWo pixels per image
+  int conv_nchw;
+  int64_t hw;
+  __device__ __forceinline__ void put(int b, int64_t m, int64_t n, float acc) const {
+    if (m >= M || n >= N) return;
+    float v = alpha * acc;
+    if (bias_mode == C3B_BIAS_COL) v += beta * bias[n];
+    else if (bias_mode == C3B_BIAS_ROW) v += beta * bias[m];
+    else if (bias_mode == C3B_BIAS_FULL) v += beta * bias[m * N + n];
+    else if (bias_mode == C3B_BIAS_SCALAR) v += beta * bias[0];
+    int64_t off;
+    if (conv_nchw) {
+      int64_t img = m / hw, pix = m - img * hw;
+      off = (img * N + n) * hw + pix;
+    } else {
+      off = (int64_t)b * batch_stride + m * N + n;
+    }
+    if (res) v += load_as_f32(res, dt_res, off);
+    v = apply_act(v, act);
+    store_from_f32(out, dt_out, off, v);
+  }
+};
+
+template <class AL, class BL>
+__global__ void __launch_bounds__(NT) simt_gemm_kernel(AL A, BL B, Epi E, int64_t M, int64_t N, int64_t K) {
+  __shared__ float As[2][BK][BM + 4];
+  __shared__ float Bs[2][BK][BN + 4];
+  const int tid = threadIdx.x;
+  const int bz = blockIdx.z;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const bool akc = A.kcontig(), bkc = B.kcontig();
+  float ra[8], rb[8];
+  auto load_tiles = [&](int64_t k0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int e = tid + i * NT;
+      int mm, kk;
+      if (akc) { kk = e % BK; mm = e / BK; } else { mm = e % BM; kk = e / BM; }
+      ra[i] = A.get(bz, m0 + mm, k0 + kk);
+      int nn, kb;
+      if (bkc) { kb = e % BK; nn = e / BK; } else { nn = e % BN; kb = e / BN; }
+      rb[i] = B.get(bz, n0 + nn, k0 + kb);
+    }
+  };
+  auto store_tiles = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int e = tid + i * NT;
+      int mm, kk;
+      if (akc) { kk = e % BK; mm = e / BK; } else { mm = e % BM; kk = e / BM; }
+      As[buf][kk][mm] = ra[i];
+      int nn, kb;
+      if (bkc) { kb = e % BK; nn = e / BK; } else { nn = e % BN; kb = e / BN; }
+      Bs[buf][kb][nn] = rb[i];
+    }
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const int tx = tid % 16, ty = tid / 16;
+  load_tiles(0);
+  store_tiles(0);
+  __syncthreads();
+  int buf = 0;
+  for (int64_t k0 = 0; k0 < K; k0 += BK) {
+    const bool more = k0 + BK < K;
+    if (more) load_tiles(k0 + BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[8], b[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = As[buf][kk][ty * 4 + i];
+        a[i + 4] = As[buf][kk][64 + ty * 4 + i];
+        b[i] = Bs[buf][kk][tx * 4 + i];
+        b[i + 4] = Bs[buf][kk][64 + tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (more) {
+      store_tiles(buf ^ 1);
+      __syncthreads();
+      buf ^= 1;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int64_t n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+      E.put(bz, m, n, acc[i][j]);
+    }
+  }
+}
+
+int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_params& p,
+                     cudaStream_t s) {
+  const int need = 2 + (p.bias_mode != C3B_BIAS_NONE) + (p.has_residual ? 1 : 0);
+  C3B_REQUIRE(n_in == need, "gemm: input count does not match bias/residual flags");
+  C3B_REQUIRE(p.M >= 0 && p.N >= 0 && p.K >= 0 && p.batch >= 1, "gemm: extents");
+  C3B_REQUIRE(p.batch <= 65535, "gemm: batch too large");
+  const c3b_tensor& a = in[0];
+  const c3b_tensor& b = in[1];
+  C3B_REQUIRE(numel(a) >= p.M * p.K + (p.batch - 1) * p.stride_a, "gemm: A too small");
+  C3B_REQUIRE(numel(b) >= p.N * p.K + (p.batch - 1) * p.stride_b, "gemm: B too small");
+  C3B_REQUIRE(numel(out) >= p.M * p.N + (p.batch - 1) * p.stride_c, "gemm: C too small");
+  Epi e;
+  memset(&e, 0, sizeof(e));
+  e.out = out.ptr; e.dt_out = out.dtype;
+  int idx = 2;
+  if (p.bias_mode != C3B_BIAS_NONE) {
+    const c3b_tensor& bt = in[idx++];
+    C3B_REQUIRE(bt.dtype == C3B_F32, "gemm: bias must be f32");
+    int64_t want = p.bias_mode == C3B_BIAS_COL ? p.N : p.bias_mode == C3B_BIAS_ROW ? p.M
+                 : p.bias_mode == C3B_BIAS_FULL ? p.M * p.N : 1;
+    C3B_REQUIRE(numel(bt) == want, "gemm: bias size does not match bias_mode");
+    e.bias = (const float*)bt.ptr;
+  }
+  if (p.has_residual) {
+    const c3b_tensor& rt = in[idx++];
+    C3B_REQUIRE(numel(rt) >= p.M * p.N + (p.batch - 1) * p.stride_c, "gemm: residual too small");
+    e.res = rt.ptr; e.dt_res = rt.dtype;
+  }
+  e.bias_mode = p.bias_mode; e.alpha = p.alpha; e.beta = p.beta; e.act = p.act;
+  e.M = p.M; e.N = p.N; e.batch_stride = p.stride_c;
+  if (p.M == 0 || p.N == 0) return C3B_OK;
+  MatLoad al{a.ptr, a.dtype, p.M, p.K, p.stride_a, p.trans_a != 0};
+  MatLoad bl{b.ptr, b.dtype, p.N, p.K, p.stride_b, p.trans_b == 0};
+  dim3 grid((unsigned)((p.N + BN - 1) / BN), (unsigned)((p.M + BM - 1) / BM), (unsigned)p.batch);
+  C3B_REQUIRE(grid.y <= 65535, "gemm: M too large for the SIMT path");
+  simt_gemm_kernel<MatLoad, MatLoad><<<grid, NT, 0, s>>>(al, bl, e, p.M, p.N, p.K);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+int launch_conv_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_params& p,
+                     cudaStream_t s) {
+  const int need = 2 + (p.has_bias ? 1 : 0) + (p.has_residual ? 1 : 0);
+  C3B_REQUIRE(n_in == need, "conv: input count does not match bias/residual flags");
+  C3B_REQUIRE(in[0].dtype == C3B_F32, "conv: SIMT path takes f32 activations");
+  C3B_REQUIRE(p.layout == 0 || p.layout == 1, "conv: layout");
+  const int64_t M = (int64_t)p.n * p.ho * p.wo;
+  const int64_t K = (int64_t)p.c * p.g.kh * p.g.kw;
+  C3B_REQUIRE(numel(in[0]) == (int64_t)p.n * p.c * p.h * p.w, "conv: input extents");
+  C3B_REQUIRE(numel(in[1]) == (int64_t)p.cout * K, "conv: weight extents");
+  C3B_REQUIRE(numel(out) >= M * p.cout, "conv: output too small");
+  Epi e;
+  memset(&e, 0, sizeof(e));
+  e.out = out.ptr; e.dt_out = out.dtype;
+  int idx = 2;
+  if (p.has_bias) {
+    C3B_REQUIRE(in[idx].dtype == C3B_F32 && numel(in[idx]) == p.cout, "conv: bias must be f32 [Cout]");
+    e.bias = (const float*)in[idx++].ptr;
+    e.bias_mode = C3B_BIAS_COL;
+  }
+  if (p.has_residual) {
+    C3B_REQUIRE(numel(in[idx]) >= M * p.cout, "conv: residual too small");
+    e.res = in[idx].ptr; e.dt_res = in[idx].dtype; idx++;
+  }
+  e.alpha = 1.f; e.beta = 1.f; e.act = p.act; e.M = M; e.N = p.cout;
+  e.conv_nchw = p.layout == 0; e.hw = (int64_t)p.ho * p.wo;
+  if (M == 0) return C3B_OK;
+  ConvALoad al{(const float*)in[0].ptr, p.n, p.c, p.h, p.w, p.ho, p.wo, p.layout, p.g, M, K};
+  // weights: layout 0 [Cout, C, kh, kw], layout 1 [Cout, kh, kw, C]; both [Cout, K] k-contiguous
+  MatLoad bl{in[1].ptr, in[1].dtype, p.cout, K, 0, false};
+  dim3 grid((unsigned)((p.cout + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), 1);
+  C3B_REQUIRE(grid.y <= 65535, "conv: M too large for the SIMT path");
+  simt_gemm_kernel<ConvALoad, MatLoad><<<grid, NT, 0, s>>>(al, bl, e, M, p.cout, K);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+}  // namespace c3b

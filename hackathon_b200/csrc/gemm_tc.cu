@@ -1,0 +1,564 @@
+// tcgen05 / TMEM / TMA bf16 GEMM and NHWC implicit-GEMM convolution (sm_100a).
+//
+// Replaces, for the bf16 precision profile, the reference contractions
+// c3_gemm_epilogue (c35/engine.py:722-849; fused_gemm_epilogue_f32 and
+// fused_matmul_bias_f32) and the conv chain im2col_f32 -> matmul_f32 (cuBLAS) ->
+// conv_reshape_f32 -> add_bias_f32 -> relu_f32 / fused_residual_relu_f32
+// (c32/decompositions.py:301-378, 505-550; c32/kernel_registry.py:318-453, 654-662).
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: A tile 128x64 and B tile BNx64 (bf16, 128B swizzle)
+//               into a ring of shared-memory stages (mbarrier full/empty pairs).
+//               For convolution A is fetched straight from the NHWC activation
+//               with a 4-D tensor map per (kh,kw) tap — TMA's out-of-bounds zero
+//               fill supplies the padding, so no patch matrix ever exists.
+//               Stride-2 convs use four parity-split views of the input
+//               (dims C, W/2, H/2, N), one per (row parity, column parity).
+//   warp 1      allocates TMEM (2 accumulator buffers of BN fp32 columns) and
+//               issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16)
+//               from one thread; tcgen05.commit releases smem stages and
+//               publishes finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld 32x32b -> +bias (folded BN) [+residual]
+//               -> ReLU/GELU -> bf16/f32 stores.  Double-buffered accumulators
+//               let the epilogue of tile i overlap the MMAs of tile i+1.
+// Every mbarrier wait is bounded (globaltimer); on expiry the kernel records
+// an error in the device status word, stops issuing work, frees its TMEM and
+// returns, so the context stays usable.
+#include <cuda.h>
+#include "common.cuh"
+
+namespace c3b {
+
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int NUM_THREADS = 192;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
+
+struct __align__(64) TmaMaps {
+  CUtensorMap a[4];
+  CUtensorMap b;
+};
+
+struct TcArgs {
+  int64_t M, N, K;
+  int n_tiles_n, n_tiles, k_blocks;
+  int block_n, stages;
+  // epilogue
+  void* out;
+  int dt_out;
+  const float* bias;
+  const void* res;
+  int dt_res;
+  int act;
+  // conv geometry (conv == 0 -> plain GEMM with a 2-D A map)
+  int conv, cblocks, ksz, stride, pad;
+  int pix;         // Ho*Wo
+  int wo, bh;      // box geometry
+  int cin;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false (after flagging) when the limit expires or when
+// another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+  if (mbar_try(bar, parity)) return true;
+  uint64_t t0 = gtimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 255) == 0) {
+      if (*abort_flag) return false;
+      if (gtimer() - t0 > WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        atomicExch(&g_status, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major operand, 128-byte swizzle, 8-row
+// groups 1024 bytes apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;       // SBO
+  d |= (uint64_t)1 << 46;                 // version
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f16: D=f32, A=B=bf16, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accum) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled stages.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = a.stages;
+  const uint32_t a_bytes = BM * BK * 2;
+  const uint32_t b_bytes = (uint32_t)a.block_n * BK * 2;
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + (size_t)stages * a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + (size_t)stages * b_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + stages;
+  uint64_t* tfull = bars + 2 * stages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t tmem_cols = (uint32_t)a.block_n * 2;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < 4; ++i) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a[i])));
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)));
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+        const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
+        const int m0 = mb * BM, n0 = nb * a.block_n;
+        int img0 = 0, oh0 = 0;
+        if (a.conv) {
+          img0 = m0 / a.pix;
+          oh0 = (m0 % a.pix) / a.wo;
+        }
+        for (int kb = 0; kb < a.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 11)) goto producer_done;
+          mbar_arrive_tx(&full[stage], a_bytes + b_bytes);
+          uint8_t* dA = sa + (size_t)stage * a_bytes;
+          uint8_t* dB = sb + (size_t)stage * b_bytes;
+          if (!a.conv) {
+            tma_load_2d(dA, &maps.a[0], &full[stage], kb * BK, m0);
+            tma_load_2d(dB, &maps.b, &full[stage], kb * BK, n0);
+          } else {
+            const int tap = kb / a.cblocks, cb = kb % a.cblocks;
+            const int r = tap / a.ksz, s = tap % a.ksz;
+            int map = 0, ro, so;
+            if (a.stride == 1) {
+              ro = r - a.pad;
+              so = s - a.pad;
+            } else {
+              const int dr = r - a.pad, ds = s - a.pad;
+              const int pr = dr & 1, ps = ds & 1;
+              ro = (dr - pr) / 2;
+              so = (ds - ps) / 2;
+              map = pr * 2 + ps;
+            }
+            tma_load_4d(dA, &maps.a[map], &full[stage], cb * BK, so, oh0 + ro, img0);
+            tma_load_2d(dB, &maps.b, &full[stage], kb * BK, n0);
+          }
+          if (++stage == stages) { stage = 0; phase ^= 1; }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc(BM, a.block_n);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 12)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * a.block_n);
+        bool ok = true;
+        for (int kb = 0; kb < a.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, 13)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sa + (size_t)stage * a_bytes);
+          const uint32_t b_addr = smem_u32(sb + (size_t)stage * b_bytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            mma_bf16(d_tmem, smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32), idesc,
+                     (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == stages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+      const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 14);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)mb * BM + q * 32 + lane;
+      const bool row_ok = row < a.M;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.block_n);
+      for (int c0 = 0; c0 < a.block_n; c0 += 16) {
+        float v[16];
+        tmem_ld16(tbase + c0, v);
+        const int64_t col0 = (int64_t)nb * a.block_n + c0;
+        if (!row_ok || col0 >= a.N) continue;
+        if (a.bias) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] += a.bias[col0 + i];
+        }
+        const int64_t off = row * a.N + col0;
+        if (a.res) {
+          if (a.dt_res == C3B_BF16) {
+            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off);
+            uint4 r0 = rp[0], r1 = rp[1];
+            const __nv_bfloat16* rb0 = reinterpret_cast<const __nv_bfloat16*>(&r0);
+            const __nv_bfloat16* rb1 = reinterpret_cast<const __nv_bfloat16*>(&r1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              v[i] += __bfloat162float(rb0[i]);
+              v[i + 8] += __bfloat162float(rb1[i]);
+            }
+          } else {
+            const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + off);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float4 r = rp[i];
+              v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = apply_act(v[i], a.act);
+        if (a.dt_out == C3B_BF16) {
+          __align__(16) __nv_bfloat16 o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float2bfloat16_rn(v[i]);
+          uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
+          op[0] = reinterpret_cast<const uint4*>(o)[0];
+          op[1] = reinterpret_cast<const uint4*>(o)[1];
+        } else {
+          float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) op[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    // Give copies still in flight time to land before shared memory is released.
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+  }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+static int encode(CUtensorMap* m, void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                  const uint32_t* box) {
+  EncodeTiledFn fn = get_encode();
+  if (!fn) return fail(C3B_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, base, (const cuuint64_t*)dims,
+                  (const cuuint64_t*)strides_bytes, (const cuuint32_t*)box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(C3B_E_INVALID, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
+  return C3B_OK;
+}
+
+static int pick_block_n(int64_t N, int requested) {
+  if (requested == 64 || requested == 128 || requested == 256) return requested;
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  if (N % 256 == 0) return 256;
+  return 128;
+}
+
+static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s) {
+  const size_t stage_bytes = (size_t)tc::BM * tc::BK * 2 + (size_t)a.block_n * tc::BK * 2;
+  const size_t budget = 200 * 1024;
+  int stages = (int)(budget / stage_bytes);
+  if (stages > 8) stages = 8;
+  if (stages < 2) return fail(C3B_E_INVALID, "tc gemm: tile does not fit in shared memory");
+  a.stages = stages;
+  const size_t smem = 1024 + stages * stage_bytes + (2 * stages + 4) * 8 + 16;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_set = true;
+  }
+  int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
+  if (grid < 1) return C3B_OK;
+  tc::tc_gemm_kernel<<<grid, tc::NUM_THREADS, smem, s>>>(maps, a);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+static int fill_epilogue(tc::TcArgs& a, const c3b_tensor* in, int n_in, int first_extra, int bias_mode,
+                         int has_residual, int64_t M, int64_t N, const c3b_tensor& out) {
+  int idx = first_extra;
+  a.bias = nullptr;
+  a.res = nullptr;
+  if (bias_mode != C3B_BIAS_NONE) {
+    C3B_REQUIRE(bias_mode == C3B_BIAS_COL, "tc: only per-column bias");
+    C3B_REQUIRE(idx < n_in && in[idx].dtype == C3B_F32 && numel(in[idx]) == N, "tc: bias must be f32 [N]");
+    a.bias = (const float*)in[idx++].ptr;
+  }
+  if (has_residual) {
+    C3B_REQUIRE(idx < n_in, "tc: missing residual");
+    C3B_REQUIRE(in[idx].dtype == C3B_BF16 || in[idx].dtype == C3B_F32, "tc: residual bf16/f32");
+    C3B_REQUIRE(numel(in[idx]) >= M * N, "tc: residual too small");
+    C3B_REQUIRE(((uintptr_t)in[idx].ptr & 15) == 0, "tc: residual must be 16-byte aligned");
+    a.res = in[idx].ptr;
+    a.dt_res = in[idx].dtype;
+    idx++;
+  }
+  C3B_REQUIRE(idx == n_in, "tc: input count does not match bias/residual flags");
+  C3B_REQUIRE(out.dtype == C3B_BF16 || out.dtype == C3B_F32, "tc: output bf16/f32");
+  C3B_REQUIRE(numel(out) >= M * N, "tc: output too small");
+  C3B_REQUIRE(((uintptr_t)out.ptr & 15) == 0, "tc: output must be 16-byte aligned");
+  a.out = out.ptr;
+  a.dt_out = out.dtype;
+  return C3B_OK;
+}
+
+int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p,
+                   cudaStream_t s) {
+  C3B_REQUIRE(n_in >= 2, "tc gemm: needs A and B");
+  C3B_REQUIRE(in[0].dtype == C3B_BF16 && in[1].dtype == C3B_BF16, "tc gemm: A and B must be bf16");
+  C3B_REQUIRE(p.K > 0 && p.K % 8 == 0, "tc gemm: K must be a positive multiple of 8");
+  C3B_REQUIRE(p.N > 0 && p.N % 16 == 0, "tc gemm: N must be a positive multiple of 16");
+  C3B_REQUIRE(p.M >= 0 && p.M < (int64_t)1 << 31, "tc gemm: M range");
+  C3B_REQUIRE(numel(in[0]) >= p.M * p.K && numel(in[1]) >= p.N * p.K, "tc gemm: operand extents");
+  C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0, "tc gemm: 16-byte alignment");
+  tc::TcArgs a;
+  memset(&a, 0, sizeof(a));
+  int rc = fill_epilogue(a, in, n_in, 2, p.bias_mode, p.has_residual, p.M, p.N, out);
+  if (rc) return rc;
+  if (p.M == 0) return C3B_OK;
+  a.M = p.M; a.N = p.N; a.K = p.K; a.act = p.act;
+  a.block_n = pick_block_n(p.N, p.block_n);
+  a.n_tiles_n = (int)((p.N + a.block_n - 1) / a.block_n);
+  a.n_tiles = (int)((p.M + tc::BM - 1) / tc::BM) * a.n_tiles_n;
+  a.k_blocks = (int)((p.K + tc::BK - 1) / tc::BK);
+  tc::TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    uint64_t str[1] = {(uint64_t)p.K * 2};
+    uint32_t box[2] = {tc::BK, tc::BM};
+    if ((rc = encode(&maps.a[0], in[0].ptr, 2, dims, str, box))) return rc;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
+    uint64_t str[1] = {(uint64_t)p.K * 2};
+    uint32_t box[2] = {tc::BK, (uint32_t)a.block_n};
+    if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box))) return rc;
+  }
+  return launch_tc(maps, a, s);
+}
+
+int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_tc_params& p,
+                   cudaStream_t s) {
+  C3B_REQUIRE(n_in == 3 + (p.has_residual ? 1 : 0), "tc conv: inputs x, w, bias [, residual]");
+  C3B_REQUIRE(in[0].dtype == C3B_BF16 && in[1].dtype == C3B_BF16, "tc conv: bf16 activations and weights");
+  C3B_REQUIRE(p.cin % 64 == 0, "tc conv: Cin must be a multiple of 64");
+  C3B_REQUIRE(p.cout % 16 == 0, "tc conv: Cout must be a multiple of 16");
+  C3B_REQUIRE(p.stride == 1 || p.stride == 2, "tc conv: stride 1 or 2");
+  C3B_REQUIRE(p.ho == (p.h + 2 * p.pad - p.k) / p.stride + 1 && p.wo == (p.w + 2 * p.pad - p.k) / p.stride + 1,
+              "tc conv: output extents");
+  if (p.stride == 2) {
+    C3B_REQUIRE(p.h % 2 == 0 && p.w % 2 == 0, "tc conv: stride 2 needs even H, W");
+    C3B_REQUIRE(p.ho == p.h / 2 && p.wo == p.w / 2, "tc conv: stride-2 geometry must halve H and W");
+  }
+  const int pix = p.ho * p.wo;
+  C3B_REQUIRE(p.wo <= 128 && 128 % p.wo == 0, "tc conv: Wo must divide 128");
+  C3B_REQUIRE(pix >= 128 ? pix % 128 == 0 : 128 % pix == 0, "tc conv: Ho*Wo must divide or be a multiple of 128");
+  C3B_REQUIRE(numel(in[0]) == (int64_t)p.n * p.h * p.w * p.cin, "tc conv: input extents");
+  C3B_REQUIRE(numel(in[1]) == (int64_t)p.cout * p.k * p.k * p.cin, "tc conv: weight extents");
+  C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0, "tc conv: 16-byte alignment");
+  const int64_t M = (int64_t)p.n * pix;
+  tc::TcArgs a;
+  memset(&a, 0, sizeof(a));
+  int rc = fill_epilogue(a, in, n_in, 2, C3B_BIAS_COL, p.has_residual, M, p.cout, out);
+  if (rc) return rc;
+  if (M == 0) return C3B_OK;
+  const int64_t K = (int64_t)p.k * p.k * p.cin;
+  a.M = M; a.N = p.cout; a.K = K; a.act = p.act;
+  a.block_n = pick_block_n(p.cout, p.block_n);
+  a.n_tiles_n = (p.cout + a.block_n - 1) / a.block_n;
+  a.n_tiles = (int)((M + tc::BM - 1) / tc::BM) * a.n_tiles_n;
+  a.k_blocks = (int)(K / tc::BK);
+  a.conv = 1; a.cblocks = p.cin / 64; a.ksz = p.k; a.stride = p.stride; a.pad = p.pad;
+  a.pix = pix; a.wo = p.wo; a.cin = p.cin;
+  const uint32_t bw = (uint32_t)p.wo;
+  const uint32_t bh = pix >= 128 ? 128u / bw : (uint32_t)p.ho;
+  const uint32_t bn = pix >= 128 ? 1u : 128u / (uint32_t)pix;
+  a.bh = (int)bh;
+  tc::TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  uint8_t* x = static_cast<uint8_t*>(in[0].ptr);
+  const uint64_t C = p.cin;
+  if (p.stride == 1) {
+    uint64_t dims[4] = {C, (uint64_t)p.w, (uint64_t)p.h, (uint64_t)p.n};
+    uint64_t str[3] = {C * 2, (uint64_t)p.w * C * 2, (uint64_t)p.h * p.w * C * 2};
+    uint32_t box[4] = {64, bw, bh, bn};
+    if ((rc = encode(&maps.a[0], x, 4, dims, str, box))) return rc;
+  } else {
+    for (int pr = 0; pr < 2; ++pr)
+      for (int ps = 0; ps < 2; ++ps) {
+        uint64_t dims[4] = {C, (uint64_t)(p.w / 2), (uint64_t)(p.h / 2), (uint64_t)p.n};
+        uint64_t str[3] = {2 * C * 2, 2 * (uint64_t)p.w * C * 2, (uint64_t)p.h * p.w * C * 2};
+        uint32_t box[4] = {64, bw, bh, bn};
+        uint8_t* base = x + ((uint64_t)pr * p.w + ps) * C * 2;
+        if ((rc = encode(&maps.a[pr * 2 + ps], base, 4, dims, str, box))) return rc;
+      }
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)p.cout};
+    uint64_t str[1] = {(uint64_t)K * 2};
+    uint32_t box[2] = {tc::BK, (uint32_t)a.block_n};
+    if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box))) return rc;
+  }
+  return launch_tc(maps, a, s);
+}
+
+}  // namespace c3b

@@ -1,0 +1,709 @@
+// Bandwidth-bound kernels: elementwise programs, strided copies, reductions,
+// normalisation, softmax, gathers and layout conversions.
+//
+// Reference counterparts (c32/kernel_registry.py, c35/engine.py):
+//   EW        add/sub/mul/div/relu/erf/exp/sqrt/reciprocal (kernel_registry.py:200-265),
+//             add_bias (379-392), batchnorm (573-584), fused_residual_relu (654-662),
+//             fused_ew (engine.py:948-1013)
+//   COPY      transpose/reshape/flatten/split (kernel_registry.py:669-741),
+//             conv_reshape (365-372), fused_transpose_reshape (engine.py:1383-1445)
+//   IM2COL    im2col (kernel_registry.py:399-453)
+//   REDUCE    reduce_mean/sum/max (kernel_registry.py:290-311)
+//   LAYERNORM fused_layer_norm / fused_residual_norm (engine.py:1078-1247)
+//   SOFTMAX   fused_softmax (engine.py:1016-1075)
+//   ATTN      fused_attention_scores (engine.py:1250-1380)
+//   GATHER    gather (kernel_registry.py:744-752)
+#include "common.cuh"
+
+namespace c3b {
+
+static inline int grid_for(int64_t n, int block) {
+  int64_t g = (n + block - 1) / block;
+  int64_t cap = (int64_t)sm_count() * 32;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+// ------------------------------------------------------------------ EW
+
+struct EwArgs {
+  const void* in[C3B_EW_MAX_IN];
+  int dt_in[C3B_EW_MAX_IN];
+  int mode[C3B_EW_MAX_IN];  // 0 general, 1 same-as-out, 2 scalar
+  int64_t stride[C3B_EW_MAX_IN][C3B_MAX_RANK];
+  int64_t shape[C3B_MAX_RANK];
+  int rank, n_in, dt_out;
+  void* out;
+  int64_t total;
+  c3b_ew_params p;
+};
+
+__device__ __forceinline__ float erf_as(float x) {
+  // Abramowitz & Stegun 7.1.26, the reference's unfused Erf (engine.py:201-223).
+  float s = x < 0.f ? -1.f : (x > 0.f ? 1.f : 0.f);
+  float ax = fabsf(x);
+  float t = 1.0f / (1.0f + 0.3275911f * ax);
+  float poly = t * (0.254829592f + t * (-0.284496736f + t * (1.421413741f + t * (-1.453152027f + t * 1.061405429f))));
+  return s * (1.0f - poly * expf(-ax * ax));
+}
+
+__global__ void ew_kernel(const EwArgs a) {
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < a.total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    float x[C3B_EW_MAX_IN];
+    int64_t coord[C3B_MAX_RANK];
+    int64_t rem = idx;
+    for (int d = a.rank - 1; d >= 0; --d) {
+      coord[d] = rem % a.shape[d];
+      rem /= a.shape[d];
+    }
+#pragma unroll
+    for (int i = 0; i < C3B_EW_MAX_IN; ++i) {
+      if (i >= a.n_in) break;
+      int64_t off = 0;
+      if (a.mode[i] == 1) off = idx;
+      else if (a.mode[i] == 0)
+        for (int d = 0; d < a.rank; ++d) off += coord[d] * a.stride[i][d];
+      x[i] = load_as_f32(a.in[i], a.dt_in[i], off);
+    }
+    float r[C3B_EW_MAX_OPS];
+    float last = 0.f;
+    for (int k = 0; k < a.p.n_ops; ++k) {
+      int ia = a.p.a[k], ib = a.p.b[k];
+      float va = ia >= 0 ? x[ia] : r[-ia - 1];
+      float vb = 0.f;
+      int op = a.p.op[k];
+      if (op <= C3B_OP_DIV) vb = ib >= 0 ? x[ib] : r[-ib - 1];
+      float v;
+      switch (op) {
+        case C3B_OP_ADD: v = va + vb; break;
+        case C3B_OP_SUB: v = va - vb; break;
+        case C3B_OP_MUL: v = va * vb; break;
+        case C3B_OP_DIV: v = va / vb; break;
+        case C3B_OP_RELU: v = fmaxf(va, 0.0f); break;
+        case C3B_OP_ERF: v = erff(va); break;
+        case C3B_OP_ERF_AS: v = erf_as(va); break;
+        case C3B_OP_SQRT: v = sqrtf(va); break;
+        case C3B_OP_EXP: v = expf(va); break;
+        case C3B_OP_RECIP: v = 1.0f / va; break;
+        case C3B_OP_ADD_IMM: v = va + a.p.imm[ib]; break;
+        case C3B_OP_MUL_IMM: v = va * a.p.imm[ib]; break;
+        case C3B_OP_MAX_IMM: v = fmaxf(va, a.p.imm[ib]); break;
+        default: v = va; break;
+      }
+      r[k] = v;
+      last = v;
+    }
+    store_from_f32(a.out, a.dt_out, idx, last);
+  }
+}
+
+int launch_ew(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_ew_params& p, cudaStream_t s) {
+  C3B_REQUIRE(n_in >= 1 && n_in <= C3B_EW_MAX_IN, "ew: 1..6 inputs");
+  C3B_REQUIRE(p.n_ops >= 1 && p.n_ops <= C3B_EW_MAX_OPS, "ew: 1..12 ops");
+  EwArgs a;
+  memset(&a, 0, sizeof(a));
+  a.rank = out.ndim;
+  for (int d = 0; d < out.ndim; ++d) a.shape[d] = out.shape[d];
+  a.total = numel(out);
+  a.n_in = n_in;
+  a.out = out.ptr;
+  a.dt_out = out.dtype;
+  a.p = p;
+  for (int k = 0; k < p.n_ops; ++k) {
+    if (p.op[k] <= C3B_OP_DIV || p.op[k] == C3B_OP_RELU || p.op[k] == C3B_OP_ERF ||
+        p.op[k] == C3B_OP_ERF_AS || p.op[k] == C3B_OP_SQRT || p.op[k] == C3B_OP_EXP ||
+        p.op[k] == C3B_OP_RECIP || p.op[k] == C3B_OP_COPY) {
+      int refs[2] = {p.a[k], p.op[k] <= C3B_OP_DIV ? p.b[k] : 0};
+      for (int j = 0; j < (p.op[k] <= C3B_OP_DIV ? 2 : 1); ++j) {
+        int v = refs[j];
+        C3B_REQUIRE(v < n_in && (v >= 0 || -v - 1 < k), "ew: operand refers to a missing value");
+      }
+    } else {
+      C3B_REQUIRE(p.a[k] < n_in && (p.a[k] >= 0 || -p.a[k] - 1 < k), "ew: bad operand");
+      C3B_REQUIRE(p.b[k] >= 0 && p.b[k] < C3B_EW_MAX_OPS, "ew: bad immediate index");
+    }
+  }
+  for (int i = 0; i < n_in; ++i) {
+    const c3b_tensor& t = in[i];
+    C3B_REQUIRE(t.ndim <= out.ndim, "ew: input rank exceeds output rank");
+    a.in[i] = t.ptr;
+    a.dt_in[i] = t.dtype;
+    int64_t n = numel(t);
+    if (n == a.total && t.ndim == out.ndim) {
+      bool same = true;
+      for (int d = 0; d < t.ndim; ++d) same &= (t.shape[d] == out.shape[d]);
+      if (same) { a.mode[i] = 1; continue; }
+    }
+    if (n == 1) { a.mode[i] = 2; continue; }
+    a.mode[i] = 0;
+    int64_t st = 1;
+    int off = out.ndim - t.ndim;
+    for (int d = out.ndim - 1; d >= 0; --d) {
+      int td = d - off;
+      int64_t ext = td >= 0 ? t.shape[td] : 1;
+      C3B_REQUIRE(ext == 1 || ext == out.shape[d], "ew: shapes do not broadcast");
+      a.stride[i][d] = ext == 1 ? 0 : st;
+      st *= ext;
+    }
+  }
+  if (a.total == 0) return C3B_OK;
+  ew_kernel<<<grid_for(a.total, 256), 256, 0, s>>>(a);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ COPY
+
+struct CopyArgs {
+  const void* in;
+  void* out;
+  int dt_in, dt_out, rank, esize;
+  int64_t total, in_offset;
+  int64_t shape[C3B_MAX_RANK];
+  int64_t stride[C3B_MAX_RANK];
+};
+
+template <typename T>
+__global__ void copy_raw_kernel(const CopyArgs a) {
+  const T* in = static_cast<const T*>(a.in);
+  T* out = static_cast<T*>(a.out);
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < a.total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = idx, off = a.in_offset;
+    for (int d = a.rank - 1; d >= 0; --d) {
+      off += (rem % a.shape[d]) * a.stride[d];
+      rem /= a.shape[d];
+    }
+    out[idx] = in[off];
+  }
+}
+
+__global__ void copy_cast_kernel(const CopyArgs a) {
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < a.total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = idx, off = a.in_offset;
+    for (int d = a.rank - 1; d >= 0; --d) {
+      off += (rem % a.shape[d]) * a.stride[d];
+      rem /= a.shape[d];
+    }
+    store_from_f32(a.out, a.dt_out, idx, load_as_f32(a.in, a.dt_in, off));
+  }
+}
+
+int launch_copy(const c3b_tensor& in, const c3b_tensor& out, const c3b_copy_params& p, cudaStream_t s) {
+  CopyArgs a;
+  memset(&a, 0, sizeof(a));
+  a.in = in.ptr; a.out = out.ptr; a.dt_in = in.dtype; a.dt_out = out.dtype;
+  a.rank = out.ndim; a.total = numel(out); a.in_offset = p.in_offset;
+  int64_t maxoff = p.in_offset;
+  for (int d = 0; d < out.ndim; ++d) {
+    a.shape[d] = out.shape[d];
+    a.stride[d] = p.in_stride[d];
+    C3B_REQUIRE(p.in_stride[d] >= 0, "copy: negative stride");
+    if (out.shape[d] > 0) maxoff += (out.shape[d] - 1) * p.in_stride[d];
+  }
+  if (a.total == 0) return C3B_OK;
+  C3B_REQUIRE(maxoff < numel(in), "copy: source range exceeds the input tensor");
+  int g = grid_for(a.total, 256);
+  if (in.dtype == out.dtype) {
+    size_t es = dtype_size(in.dtype);
+    if (es == 4) copy_raw_kernel<uint32_t><<<g, 256, 0, s>>>(a);
+    else if (es == 2) copy_raw_kernel<uint16_t><<<g, 256, 0, s>>>(a);
+    else if (es == 8) copy_raw_kernel<uint64_t><<<g, 256, 0, s>>>(a);
+    else copy_raw_kernel<uint8_t><<<g, 256, 0, s>>>(a);
+  } else {
+    copy_cast_kernel<<<g, 256, 0, s>>>(a);
+  }
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ IM2COL
+
+__global__ void im2col_kernel(const float* __restrict__ x, float* __restrict__ out, int N, int C, int H,
+                              int W, int Ho, int Wo, c3b_conv_geom g, int64_t total) {
+  const int K = C * g.kh * g.kw;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t m = idx / K;
+    int k = (int)(idx - m * K);
+    int s = k % g.kw;
+    int r = (k / g.kw) % g.kh;
+    int c = k / (g.kw * g.kh);
+    int ow = (int)(m % Wo);
+    int oh = (int)((m / Wo) % Ho);
+    int n = (int)(m / ((int64_t)Wo * Ho));
+    int ih = oh * g.sh - g.ph0 + r * g.dh;
+    int iw = ow * g.sw - g.pw0 + s * g.dw;
+    float v = 0.f;
+    if (ih >= 0 && ih < H && iw >= 0 && iw < W) v = x[(((int64_t)n * C + c) * H + ih) * W + iw];
+    out[idx] = v;
+  }
+}
+
+int launch_im2col(const c3b_tensor& in, const c3b_tensor& out, const c3b_conv_geom& g, cudaStream_t s) {
+  C3B_REQUIRE(in.ndim == 4 && in.dtype == C3B_F32 && out.dtype == C3B_F32, "im2col: f32 NCHW input");
+  int N = (int)in.shape[0], C = (int)in.shape[1], H = (int)in.shape[2], W = (int)in.shape[3];
+  int Ho = (H + g.ph0 + g.ph1 - (g.dh * (g.kh - 1) + 1)) / g.sh + 1;
+  int Wo = (W + g.pw0 + g.pw1 - (g.dw * (g.kw - 1) + 1)) / g.sw + 1;
+  C3B_REQUIRE(Ho > 0 && Wo > 0, "im2col: empty output");
+  int64_t total = (int64_t)N * Ho * Wo * C * g.kh * g.kw;
+  C3B_REQUIRE(numel(out) >= total, "im2col: output too small");
+  if (total == 0) return C3B_OK;
+  im2col_kernel<<<grid_for(total, 256), 256, 0, s>>>((const float*)in.ptr, (float*)out.ptr, N, C, H, W, Ho,
+                                                     Wo, g, total);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ REDUCE
+
+__global__ void reduce_rows_kernel(const void* __restrict__ x, int dt, float* __restrict__ y, int64_t outer,
+                                   int64_t R, int op) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = warp; row < outer; row += nw) {
+    float acc = op == C3B_RED_MAX ? -INFINITY : 0.f;
+    for (int64_t j = lane; j < R; j += 32) {
+      float v = load_as_f32(x, dt, row * R + j);
+      acc = op == C3B_RED_MAX ? fmaxf(acc, v) : acc + v;
+    }
+    acc = op == C3B_RED_MAX ? warp_max(acc) : warp_sum(acc);
+    if (lane == 0) y[row] = op == C3B_RED_MEAN ? acc / (float)R : acc;
+  }
+}
+
+__global__ void reduce_cols_kernel(const void* __restrict__ x, int dt, float* __restrict__ y, int64_t outer,
+                                   int64_t R, int64_t inner, int op) {
+  int64_t total = outer * inner;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t o = idx / inner, i = idx - o * inner;
+    float acc = op == C3B_RED_MAX ? -INFINITY : 0.f;
+    for (int64_t j = 0; j < R; ++j) {
+      float v = load_as_f32(x, dt, (o * R + j) * inner + i);
+      acc = op == C3B_RED_MAX ? fmaxf(acc, v) : acc + v;
+    }
+    y[idx] = op == C3B_RED_MEAN ? acc / (float)R : acc;
+  }
+}
+
+int launch_reduce(const c3b_tensor& in, const c3b_tensor& out, const c3b_reduce_params& p, cudaStream_t s) {
+  C3B_REQUIRE(out.dtype == C3B_F32, "reduce: f32 output");
+  C3B_REQUIRE(p.outer * p.reduce * p.inner == numel(in), "reduce: extents do not match input");
+  C3B_REQUIRE(numel(out) >= p.outer * p.inner, "reduce: output too small");
+  if (p.outer * p.inner == 0) return C3B_OK;
+  if (p.inner == 1)
+    reduce_rows_kernel<<<grid_for(p.outer * 32, 256), 256, 0, s>>>(in.ptr, in.dtype, (float*)out.ptr, p.outer,
+                                                                   p.reduce, p.op);
+  else
+    reduce_cols_kernel<<<grid_for(p.outer * p.inner, 256), 256, 0, s>>>(in.ptr, in.dtype, (float*)out.ptr,
+                                                                        p.outer, p.reduce, p.inner, p.op);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ LAYERNORM
+// One warp per row; row held in registers when cols <= 32*LN_REG, else re-read.
+// Two-pass mean / centred variance like the reference kernels.
+
+template <int PER_LANE>
+__global__ void layernorm_kernel(const void* __restrict__ x, int dtx, const void* __restrict__ res, int dtr,
+                                 const float* __restrict__ scale, const float* __restrict__ bias,
+                                 void* __restrict__ y, int dty, void* __restrict__ sum_out, int dts,
+                                 int64_t rows, int cols, float eps) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = warp; row < rows; row += nw) {
+    const int64_t base = row * cols;
+    float v[PER_LANE];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+      int c = lane + 32 * i;
+      float t = 0.f;
+      if (c < cols) {
+        t = load_as_f32(x, dtx, base + c);
+        if (res) t += load_as_f32(res, dtr, base + c);
+        if (sum_out) store_from_f32(sum_out, dts, base + c, t);
+      }
+      v[i] = t;
+      s += t;
+    }
+    const float mean = warp_sum(s) / (float)cols;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+      int c = lane + 32 * i;
+      if (c < cols) { float d = v[i] - mean; q += d * d; }
+    }
+    const float inv = rsqrtf(warp_sum(q) / (float)cols + eps);
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+      int c = lane + 32 * i;
+      if (c < cols) {
+        float o = (v[i] - mean) * inv * scale[c];
+        if (bias) o += bias[c];
+        store_from_f32(y, dty, base + c, o);
+      }
+    }
+  }
+}
+
+__global__ void layernorm_wide_kernel(const void* __restrict__ x, int dtx, const void* __restrict__ res, int dtr,
+                                      const float* __restrict__ scale, const float* __restrict__ bias,
+                                      void* __restrict__ y, int dty, void* __restrict__ sum_out, int dts,
+                                      int64_t rows, int64_t cols, float eps) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = warp; row < rows; row += nw) {
+    const int64_t base = row * cols;
+    float s = 0.f;
+    for (int64_t c = lane; c < cols; c += 32) {
+      float t = load_as_f32(x, dtx, base + c) + (res ? load_as_f32(res, dtr, base + c) : 0.f);
+      s += t;
+    }
+    const float mean = warp_sum(s) / (float)cols;
+    float q = 0.f;
+    for (int64_t c = lane; c < cols; c += 32) {
+      float t = load_as_f32(x, dtx, base + c) + (res ? load_as_f32(res, dtr, base + c) : 0.f) - mean;
+      q += t * t;
+    }
+    const float inv = rsqrtf(warp_sum(q) / (float)cols + eps);
+    for (int64_t c = lane; c < cols; c += 32) {
+      float t = load_as_f32(x, dtx, base + c) + (res ? load_as_f32(res, dtr, base + c) : 0.f);
+      if (sum_out) store_from_f32(sum_out, dts, base + c, t);
+      float o = (t - mean) * inv * scale[c];
+      if (bias) o += bias[c];
+      store_from_f32(y, dty, base + c, o);
+    }
+  }
+}
+
+int launch_layernorm(const c3b_tensor* in, int n_in, const c3b_tensor* out, int n_out,
+                     const c3b_layernorm_params& p, cudaStream_t s) {
+  int need = 2 + p.has_residual + p.has_bias;
+  C3B_REQUIRE(n_in == need, "layernorm: input count does not match flags");
+  C3B_REQUIRE(n_out == 1 + (p.write_sum ? 1 : 0), "layernorm: output count does not match flags");
+  const c3b_tensor& x = in[0];
+  const c3b_tensor* res = p.has_residual ? &in[1] : nullptr;
+  const c3b_tensor& sc = in[1 + p.has_residual];
+  const c3b_tensor* bi = p.has_bias ? &in[2 + p.has_residual] : nullptr;
+  C3B_REQUIRE(numel(x) == p.rows * p.cols, "layernorm: rows*cols != numel(x)");
+  C3B_REQUIRE(numel(sc) == p.cols && sc.dtype == C3B_F32, "layernorm: scale must be f32 [cols]");
+  C3B_REQUIRE(!bi || (numel(*bi) == p.cols && bi->dtype == C3B_F32), "layernorm: bias must be f32 [cols]");
+  C3B_REQUIRE(!res || numel(*res) == numel(x), "layernorm: residual shape");
+  C3B_REQUIRE(numel(out[0]) >= numel(x), "layernorm: output too small");
+  if (p.rows == 0 || p.cols == 0) return C3B_OK;
+  const void* rp = res ? res->ptr : nullptr;
+  int rdt = res ? res->dtype : 0;
+  void* sp = p.write_sum ? out[1].ptr : nullptr;
+  int sdt = p.write_sum ? out[1].dtype : 0;
+  int g = grid_for(p.rows * 32, 256);
+  const float* bp = bi ? (const float*)bi->ptr : nullptr;
+#define C3B_LN(PL)                                                                                     \
+  layernorm_kernel<PL><<<g, 256, 0, s>>>(x.ptr, x.dtype, rp, rdt, (const float*)sc.ptr, bp, out[0].ptr, \
+                                         out[0].dtype, sp, sdt, p.rows, (int)p.cols, p.epsilon)
+  if (p.cols <= 32) C3B_LN(1);
+  else if (p.cols <= 128) C3B_LN(4);
+  else if (p.cols <= 256) C3B_LN(8);
+  else if (p.cols <= 512) C3B_LN(16);
+  else if (p.cols <= 1024) C3B_LN(32);
+  else
+    layernorm_wide_kernel<<<g, 256, 0, s>>>(x.ptr, x.dtype, rp, rdt, (const float*)sc.ptr, bp, out[0].ptr,
+                                            out[0].dtype, sp, sdt, p.rows, p.cols, p.epsilon);
+#undef C3B_LN
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ SOFTMAX
+
+__global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t L) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = warp; row < rows; row += nw) {
+    const float* xr = x + row * L;
+    float m = -INFINITY;
+    for (int64_t j = lane; j < L; j += 32) m = fmaxf(m, xr[j]);
+    m = warp_max(m);
+    float sum = 0.f;
+    for (int64_t j = lane; j < L; j += 32) sum += expf(xr[j] - m);
+    sum = warp_sum(sum);
+    for (int64_t j = lane; j < L; j += 32) y[row * L + j] = expf(xr[j] - m) / sum;
+  }
+}
+
+__global__ void softmax_cols_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t outer, int64_t L,
+                                    int64_t inner) {
+  int64_t total = outer * inner;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t o = idx / inner, i = idx - o * inner;
+    const int64_t base = o * L * inner + i;
+    float m = -INFINITY;
+    for (int64_t j = 0; j < L; ++j) m = fmaxf(m, x[base + j * inner]);
+    float sum = 0.f;
+    for (int64_t j = 0; j < L; ++j) sum += expf(x[base + j * inner] - m);
+    for (int64_t j = 0; j < L; ++j) y[base + j * inner] = expf(x[base + j * inner] - m) / sum;
+  }
+}
+
+int launch_softmax(const c3b_tensor& in, const c3b_tensor& out, const c3b_softmax_params& p, cudaStream_t s) {
+  C3B_REQUIRE(in.dtype == C3B_F32 && out.dtype == C3B_F32, "softmax: f32");
+  C3B_REQUIRE(p.outer * p.axis * p.inner == numel(in) && numel(out) >= numel(in), "softmax: extents");
+  if (numel(in) == 0) return C3B_OK;
+  if (p.inner == 1)
+    softmax_rows_kernel<<<grid_for(p.outer * 32, 256), 256, 0, s>>>((const float*)in.ptr, (float*)out.ptr,
+                                                                    p.outer, p.axis);
+  else
+    softmax_cols_kernel<<<grid_for(p.outer * p.inner, 256), 256, 0, s>>>((const float*)in.ptr, (float*)out.ptr,
+                                                                         p.outer, p.axis, p.inner);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ ATTENTION SCORES
+// softmax(Q K^T / div + mask) for one (batch, head, row) per block; the row of
+// scores lives in shared memory (one dot product per column, not three).
+
+__global__ void attn_scores_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                   const float* __restrict__ divisor, const float* __restrict__ mask,
+                                   float* __restrict__ out, c3b_attn_scores_params p) {
+  extern __shared__ float sm[];
+  float* qrow = sm;             // inner
+  float* sc = sm + p.inner;     // cols
+  __shared__ float red[32];
+  const int64_t seg = blockIdx.x;
+  const int row = (int)(seg % p.rows);
+  const int head = (int)((seg / p.rows) % p.out1);
+  const int b = (int)(seg / ((int64_t)p.rows * p.out1));
+  const int qb = p.q0 == 1 ? 0 : b, qh = p.q1 == 1 ? 0 : head;
+  const int kb = p.k0 == 1 ? 0 : b, kh = p.k1 == 1 ? 0 : head;
+  const float* qp = q + (((int64_t)qb * p.q1 + qh) * p.rows + row) * p.inner;
+  const float* kp = k + ((int64_t)kb * p.k1 + kh) * (int64_t)p.inner * p.cols;
+  for (int i = threadIdx.x; i < p.inner; i += blockDim.x) qrow[i] = qp[i];
+  __syncthreads();
+  const float dv = divisor[0];
+  const int mb = p.m[0] == 1 ? 0 : b, mh = p.m[1] == 1 ? 0 : head, mr = p.m[2] == 1 ? 0 : row;
+  float lmax = -INFINITY;
+  for (int c = threadIdx.x; c < p.cols; c += blockDim.x) {
+    float acc = 0.f;
+    for (int i = 0; i < p.inner; ++i) acc = fmaf(qrow[i], kp[(int64_t)i * p.cols + c], acc);
+    const int mc = p.m[3] == 1 ? 0 : c;
+    const int64_t mi = (((int64_t)mb * p.m[1] + mh) * p.m[2] + mr) * p.m[3] + mc;
+    float v = acc / dv + mask[mi];
+    sc[c] = v;
+    lmax = fmaxf(lmax, v);
+  }
+  lmax = warp_max(lmax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = lmax;
+  __syncthreads();
+  float m = -INFINITY;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+  __syncthreads();
+  float lsum = 0.f;
+  for (int c = threadIdx.x; c < p.cols; c += blockDim.x) lsum += expf(sc[c] - m);
+  lsum = warp_sum(lsum);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = lsum;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+  float* o = out + seg * p.cols;
+  for (int c = threadIdx.x; c < p.cols; c += blockDim.x) o[c] = expf(sc[c] - m) / tot;
+}
+
+int launch_attn_scores(const c3b_tensor* in, const c3b_tensor& out, const c3b_attn_scores_params& p,
+                       cudaStream_t s) {
+  for (int i = 0; i < 4; ++i) C3B_REQUIRE(in[i].dtype == C3B_F32, "attention scores: f32 inputs");
+  int64_t segs = (int64_t)p.out0 * p.out1 * p.rows;
+  C3B_REQUIRE(numel(out) >= segs * p.cols, "attention scores: output too small");
+  size_t smem = (size_t)(p.inner + p.cols) * sizeof(float);
+  C3B_REQUIRE(smem <= 200 * 1024, "attention scores: row too long for shared memory");
+  if (segs == 0) return C3B_OK;
+  if (smem > 48 * 1024)
+    C3B_CHECK_CUDA(cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  attn_scores_kernel<<<(unsigned)segs, 256, smem, s>>>((const float*)in[0].ptr, (const float*)in[1].ptr,
+                                                       (const float*)in[2].ptr, (const float*)in[3].ptr,
+                                                       (float*)out.ptr, p);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ GATHER
+
+template <typename T, typename I>
+__global__ void gather_kernel(const T* __restrict__ data, const I* __restrict__ idx, T* __restrict__ out,
+                              c3b_gather_params p) {
+  const int64_t total = p.outer * p.n_idx * p.inner;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t i = t % p.inner;
+    int64_t j = (t / p.inner) % p.n_idx;
+    int64_t o = t / (p.inner * p.n_idx);
+    int64_t k = (int64_t)idx[j];
+    if (k < 0) k += p.axis_len;
+    if (k < 0 || k >= p.axis_len) {
+      atomicExch(&g_status, 3);  // out-of-range index: report, write zero
+      out[t] = T(0);
+      continue;
+    }
+    out[t] = data[(o * p.axis_len + k) * p.inner + i];
+  }
+}
+
+int launch_gather(const c3b_tensor& data, const c3b_tensor& idx, const c3b_tensor& out, const c3b_gather_params& p,
+                  cudaStream_t s) {
+  C3B_REQUIRE(data.dtype == out.dtype, "gather: data and output dtypes differ");
+  C3B_REQUIRE(idx.dtype == C3B_I64 || idx.dtype == C3B_I32, "gather: int32/int64 indices");
+  C3B_REQUIRE(p.outer * p.axis_len * p.inner == numel(data), "gather: extents do not match data");
+  C3B_REQUIRE(numel(idx) == p.n_idx, "gather: index count");
+  int64_t total = p.outer * p.n_idx * p.inner;
+  C3B_REQUIRE(numel(out) >= total, "gather: output too small");
+  if (total == 0) return C3B_OK;
+  int g = grid_for(total, 256);
+  size_t es = dtype_size(data.dtype);
+#define C3B_G(T)                                                                                  \
+  if (idx.dtype == C3B_I64)                                                                       \
+    gather_kernel<T, long long><<<g, 256, 0, s>>>((const T*)data.ptr, (const long long*)idx.ptr, (T*)out.ptr, p); \
+  else                                                                                            \
+    gather_kernel<T, int><<<g, 256, 0, s>>>((const T*)data.ptr, (const int*)idx.ptr, (T*)out.ptr, p);
+  if (es == 4) { C3B_G(uint32_t) }
+  else if (es == 2) { C3B_G(uint16_t) }
+  else if (es == 8) { C3B_G(uint64_t) }
+  else { C3B_G(uint8_t) }
+#undef C3B_G
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ EMBED
+// out[b,s,:] = tok[ids[b,s],:] + pos[s,:]  (Gather + Add of the decoder input).
+// One warp per token, 4 floats per lane per step.
+
+__global__ void embed_kernel(const long long* __restrict__ ids, const float* __restrict__ tok,
+                             const float* __restrict__ pos, void* __restrict__ out, int dto, c3b_embed_params p) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  int nw = (gridDim.x * blockDim.x) >> 5;
+  const int64_t ntok = p.batch * p.seq;
+  for (int64_t t = warp; t < ntok; t += nw) {
+    long long id = ids[t];
+    if (id < 0) id += p.vocab;
+    const int64_t srow = t % p.seq;
+    if (id < 0 || id >= p.vocab) {
+      if (lane == 0) atomicExch(&g_status, 3);
+      id = 0;
+    }
+    const float* tr = tok + id * p.dim;
+    const float* pr = pos + srow * p.dim;
+    if ((p.dim & 3) == 0) {
+      for (int64_t c = lane * 4; c < p.dim; c += 128) {
+        float4 a = *reinterpret_cast<const float4*>(tr + c);
+        float4 b = *reinterpret_cast<const float4*>(pr + c);
+        float v[4] = {a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w};
+        if (dto == C3B_F32) {
+          *reinterpret_cast<float4*>((float*)out + t * p.dim + c) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+          __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]);
+          __nv_bfloat162 hi = __floats2bfloat162_rn(v[2], v[3]);
+          uint2 pk;
+          pk.x = *reinterpret_cast<uint32_t*>(&lo);
+          pk.y = *reinterpret_cast<uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>((__nv_bfloat16*)out + t * p.dim + c) = pk;
+        }
+      }
+    } else {
+      for (int64_t c = lane; c < p.dim; c += 32) store_from_f32(out, dto, t * p.dim + c, tr[c] + pr[c]);
+    }
+  }
+}
+
+int launch_embed(const c3b_tensor* in, const c3b_tensor& out, const c3b_embed_params& p, cudaStream_t s) {
+  // inputs: ids (i64 [B,S]), tok (f32 [V,D]), pos (f32 [S,D])
+  C3B_REQUIRE(in[0].dtype == C3B_I64 && in[1].dtype == C3B_F32 && in[2].dtype == C3B_F32, "embed: dtypes");
+  C3B_REQUIRE(numel(in[0]) == p.batch * p.seq && numel(in[1]) == p.vocab * p.dim &&
+                  numel(in[2]) >= p.seq * p.dim, "embed: extents");
+  C3B_REQUIRE(out.dtype == C3B_F32 || out.dtype == C3B_BF16, "embed: f32/bf16 output");
+  C3B_REQUIRE(numel(out) >= p.batch * p.seq * p.dim, "embed: output too small");
+  int64_t n = p.batch * p.seq;
+  if (n == 0) return C3B_OK;
+  embed_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>((const long long*)in[0].ptr, (const float*)in[1].ptr,
+                                                     (const float*)in[2].ptr, out.ptr, out.dtype, p);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ STEM IM2COL
+// NCHW f32 input -> bf16 patch matrix [N*Ho*Wo, kpad], K ordered (r, s, c), so
+// the 3-channel stem conv runs through the TMA/tcgen05 GEMM.  One thread per
+// output pixel writes its padded row as 16-byte vectors.
+
+__global__ void stem_im2col_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out, c3b_stem_params p) {
+  const int64_t M = (int64_t)p.n * p.ho * p.wo;
+  const int K = p.g.kh * p.g.kw * p.c;
+  for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < M; m += (int64_t)gridDim.x * blockDim.x) {
+    int ow = (int)(m % p.wo);
+    int oh = (int)((m / p.wo) % p.ho);
+    int n = (int)(m / ((int64_t)p.wo * p.ho));
+    __nv_bfloat16* orow = out + m * p.kpad;
+    for (int k0 = 0; k0 < p.kpad; k0 += 8) {
+      __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        int k = k0 + j;
+        float val = 0.f;
+        if (k < K) {
+          int c = k % p.c;
+          int s = (k / p.c) % p.g.kw;
+          int r = k / (p.c * p.g.kw);
+          int ih = oh * p.g.sh - p.g.ph0 + r * p.g.dh;
+          int iw = ow * p.g.sw - p.g.pw0 + s * p.g.dw;
+          if (ih >= 0 && ih < p.h && iw >= 0 && iw < p.w) val = x[(((int64_t)n * p.c + c) * p.h + ih) * p.w + iw];
+        }
+        v[j] = __float2bfloat16_rn(val);
+      }
+      *reinterpret_cast<uint4*>(orow + k0) = *reinterpret_cast<const uint4*>(v);
+    }
+  }
+}
+
+int launch_stem_im2col(const c3b_tensor& in, const c3b_tensor& out, const c3b_stem_params& p, cudaStream_t s) {
+  C3B_REQUIRE(in.dtype == C3B_F32 && out.dtype == C3B_BF16, "stem im2col: f32 in, bf16 out");
+  C3B_REQUIRE(p.kpad % 8 == 0 && p.kpad >= p.g.kh * p.g.kw * p.c, "stem im2col: kpad");
+  C3B_REQUIRE(numel(in) == (int64_t)p.n * p.c * p.h * p.w, "stem im2col: input extents");
+  int64_t M = (int64_t)p.n * p.ho * p.wo;
+  C3B_REQUIRE(numel(out) >= M * p.kpad, "stem im2col: output too small");
+  if (M == 0) return C3B_OK;
+  stem_im2col_kernel<<<grid_for(M, 128), 128, 0, s>>>((const float*)in.ptr, (__nv_bfloat16*)out.ptr, p);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ GAP (NHWC)
+
+__global__ void gap_nhwc_kernel(const void* __restrict__ x, int dt, float* __restrict__ y, c3b_gap_params p) {
+  const int64_t total = p.n * p.c;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t n = t / p.c, c = t - n * p.c;
+    float acc = 0.f;
+    for (int64_t i = 0; i < p.hw; ++i) acc += load_as_f32(x, dt, (n * p.hw + i) * p.c + c);
+    y[t] = acc / (float)p.hw;
+  }
+}
+
+int launch_gap_nhwc(const c3b_tensor& in, const c3b_tensor& out, const c3b_gap_params& p, cudaStream_t s) {
+  C3B_REQUIRE(out.dtype == C3B_F32, "gap: f32 output");
+  C3B_REQUIRE(numel(in) == p.n * p.hw * p.c && numel(out) >= p.n * p.c, "gap: extents");
+  if (p.n * p.c == 0) return C3B_OK;
+  gap_nhwc_kernel<<<grid_for(p.n * p.c, 256), 256, 0, s>>>(in.ptr, in.dtype, (float*)out.ptr, p);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+}  // namespace c3b

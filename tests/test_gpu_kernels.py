@@ -1,0 +1,354 @@
+"""Per-kernel parity on the GPU, through the reference kernel ABI.
+
+Each test calls a registry kernel exactly as the reference executor would
+(``lookup(name)(inputs, outputs, params, tuning)``, c35/executor.py:576-581),
+with pre-allocated float32 arena views as outputs, and compares with the
+oracle restatement of the same reference kernel.  FP32 tolerance: 1e-4 relative
+(max|a-b| / max|b|).  bf16 tensor-core kernels are checked against the oracle
+evaluated on the same bf16-rounded operands with fp32 accumulation.
+"""
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import ops as O
+from oracle.bf16 import round_bf16
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-4
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    assert torch.cuda.is_available()
+    from hackathon_b200 import _lib
+    _lib.lib()
+    return torch
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def arena(torch, n):
+    return torch.full((int(n),), float("nan"), dtype=torch.float32, device="cuda")
+
+
+def call(name, ins, outs, params):
+    from hackathon_b200.kernel_registry import lookup
+    lookup(name)(ins, outs, params, {"block_x": 256, "grid_x": 1, "smem_bytes": 0})
+    import torch
+    torch.cuda.synchronize()
+    return outs
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+RNG = np.random.default_rng(1234)
+
+
+def randn(*s):
+    return RNG.standard_normal(s, dtype=np.float32)
+
+
+def test_elementwise_family(torch_cuda):
+    t = torch_cuda
+    a, b = randn(2, 3, 4), randn(3, 1)
+    for name, ref in [("add_f32", a + b), ("sub", a - b), ("mul_f32", a * b), ("div", a / (np.abs(b) + 0.5))]:
+        bb = b if name != "div" else np.abs(b) + 0.5
+        outs = call(name, [dev(t, a), dev(t, bb)], [arena(t, 64)], {})
+        assert tuple(outs[0].shape) == ref.shape
+        assert rel(host(outs[0]), ref) < RTOL
+    x = randn(5, 7)
+    for name, ref in [("relu_f32", np.maximum(x, 0)), ("erf_f32", O.erf_as(x)), ("exp", np.exp(x)),
+                      ("sqrt", np.sqrt(np.abs(x))), ("reciprocal", 1.0 / (np.abs(x) + 1))]:
+        xin = np.abs(x) if name == "sqrt" else (np.abs(x) + 1 if name == "reciprocal" else x)
+        outs = call(name, [dev(t, xin)], [arena(t, 64)], {})
+        assert rel(host(outs[0]), ref) < RTOL, name
+    outs = call("add", [dev(t, x)], [arena(t, 64)], {"epsilon": 1e-3})
+    assert rel(host(outs[0]), x + np.float32(1e-3)) < RTOL
+
+
+def test_bias_bn_residual(torch_cuda):
+    t = torch_cuda
+    x, bias = randn(2, 4, 3, 3), randn(4)
+    outs = call("add_bias_f32", [dev(t, x), dev(t, bias)], [arena(t, 100)], {"bias_axis": 1, "beta": 0.5})
+    assert rel(host(outs[0]), x + 0.5 * bias.reshape(1, 4, 1, 1)) < RTOL
+    sc, be, mu = randn(4), randn(4), randn(4)
+    var = np.abs(randn(4)) + 0.5
+    outs = call("batchnorm_f32", [dev(t, v) for v in (x, sc, be, mu, var)], [arena(t, 100)], {"epsilon": 1e-5})
+    assert rel(host(outs[0]), O.batchnorm(x, sc, be, mu, var, 1e-5)) < RTOL
+    r = randn(2, 4, 3, 3)
+    outs = call("fused_residual_relu_f32", [dev(t, x), dev(t, r)], [arena(t, 100)], {})
+    assert rel(host(outs[0]), np.maximum(x + r, 0)) < RTOL
+
+
+def test_fused_ew_gelu_chain(torch_cuda):
+    t = torch_cuda
+    f = randn(8, 16)
+    ops = [{"op": "Div", "inputs": [0, 1], "output": "d"}, {"op": "Erf", "inputs": ["d"], "output": "e"},
+           {"op": "Add", "inputs": ["e", 2], "output": "a"}, {"op": "Mul", "inputs": [0, "a"], "output": "m"},
+           {"op": "Mul", "inputs": ["m", 3], "output": "o"}]
+    consts = [np.array([math.sqrt(2)], np.float32), np.array([1.0], np.float32), np.array([0.5], np.float32)]
+    outs = call("fused_ew_f32", [dev(t, f)] + [dev(t, c) for c in consts], [arena(t, 200)], {"_ops": ops})
+    assert rel(host(outs[0]), O.ew_chain(ops, [f] + consts)) < RTOL
+    assert rel(host(outs[0]), O.gelu_erf(f)) < RTOL
+
+
+def test_reductions_softmax(torch_cuda):
+    t = torch_cuda
+    x = randn(3, 5, 4, 6)
+    outs = call("reduce_mean_f32", [dev(t, x)], [arena(t, 100)], {"axes": [-2, -1], "keepdims": True})
+    assert tuple(outs[0].shape) == (3, 5, 1, 1)
+    assert rel(host(outs[0]), O.global_average_pool(x)) < RTOL
+    outs = call("reduce_max", [dev(t, x)], [arena(t, 100)], {"axis": 1})
+    assert rel(host(outs[0]), x.max(axis=1)) < RTOL
+    outs = call("reduce_sum", [dev(t, x)], [arena(t, 400)], {"axis": -1, "keepdims": True})
+    assert rel(host(outs[0]), x.sum(axis=-1, keepdims=True)) < RTOL
+    for axis in (-1, 1):
+        outs = call("fused_softmax_f32", [dev(t, x)], [arena(t, x.size)], {"axis": axis})
+        assert rel(host(outs[0]), O.softmax(x, axis)) < RTOL
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_gemm_epilogue(torch_cuda, ta, tb):
+    t = torch_cuda
+    M, N, K = 67, 45, 131
+    a = randn(K, M) if ta else randn(M, K)
+    b = randn(N, K) if tb else randn(K, N)
+    for bias in (randn(N), randn(1, N), randn(M, 1), randn(M, N)):
+        p = {"transA": ta, "transB": tb, "alpha": 0.7, "beta": 1.3, "_activation": "Relu"}
+        outs = call("fused_gemm_epilogue_f32", [dev(t, a), dev(t, b), dev(t, bias)], [arena(t, M * N)], p)
+        ref = O.gemm_epilogue(a, b, bias, alpha=0.7, beta=1.3, transA=ta, transB=tb, relu=True)
+        assert rel(host(outs[0]), ref) < RTOL
+
+
+def test_gemm_flatten_and_matmul_bias(torch_cuda):
+    t = torch_cuda
+    x, w, b = randn(6, 8, 2, 2), randn(10, 32), randn(10)
+    outs = call("fused_gemm_epilogue_f32", [dev(t, x), dev(t, w), dev(t, b)], [arena(t, 60)],
+                {"transB": 1, "_flatten_axis": 1})
+    assert rel(host(outs[0]), O.gemm_epilogue(x, w, b, transB=1, flatten_axis=1)) < RTOL
+    x3, w2, b2 = randn(3, 17, 40), randn(40, 24), randn(24)
+    outs = call("fused_matmul_bias_f32", [dev(t, x3), dev(t, w2), dev(t, b2)], [arena(t, 3 * 17 * 24)], {})
+    assert tuple(outs[0].shape) == (3, 17, 24)
+    assert rel(host(outs[0]), O.gemm_epilogue(x3, w2, b2, matmul=True)) < RTOL
+
+
+def test_matmul_batched_and_conv_contract(torch_cuda):
+    t = torch_cuda
+    a, b = randn(2, 3, 9, 16), randn(2, 3, 16, 5)
+    outs = call("matmul_f32", [dev(t, a), dev(t, b)], [arena(t, 2 * 3 * 45)], {"lowering_kind": "matmul"})
+    assert rel(host(outs[0]), np.matmul(a, b)) < RTOL
+    z = np.load(_golden("registry_kat.npz"))
+    outs = call("matmul_f32", [dev(t, z["im2col"]), dev(t, z["w"])], [arena(t, z["contract"].size)],
+                {"lowering_kind": "conv_contract"})
+    assert rel(host(outs[0]), z["contract"]) < RTOL
+
+
+def _golden(name):
+    import os
+    return os.path.join(os.path.dirname(__file__), "golden", name)
+
+
+def test_registry_conv_chain_matches_reference_kat(torch_cuda):
+    """im2col -> conv_contract -> conv_reshape -> add_bias, against the outputs
+    the reference registry produced on the same inputs (registry_kat.npz)."""
+    t = torch_cuda
+    import json
+    z = np.load(_golden("registry_kat.npz"))
+    p = json.loads(str(z["params"]))
+    col = call("im2col_f32", [dev(t, z["x"])], [arena(t, z["im2col"].size)], p)[0]
+    assert np.array_equal(host(col), z["im2col"])
+    mm = call("matmul_f32", [col, dev(t, z["w"])], [arena(t, z["contract"].size)],
+              {**p, "lowering_kind": "conv_contract"})[0]
+    n, o, ho, wo = z["nchw"].shape
+    rs = call("conv_reshape_f32", [mm], [arena(t, z["nchw"].size)], {**p, "_output_spatial": [ho, wo]})[0]
+    assert rel(host(rs), z["nchw"]) < RTOL
+    ob = call("add_bias_f32", [rs, dev(t, z["b"])], [arena(t, z["nchw"].size)], {"bias_axis": 1})[0]
+    assert rel(host(ob), z["biased"]) < RTOL
+    er = call("erf_f32", [dev(t, z["x"])], [arena(t, z["x"].size)], {})[0]
+    assert np.abs(host(er) - z["erf_as"]).max() < 1e-6
+
+
+@pytest.mark.parametrize("stride,k,pads", [(1, 3, [1, 1, 1, 1]), (2, 3, [1, 1, 1, 1]), (2, 1, [0, 0, 0, 0]),
+                                           (1, 3, [0, 1, 2, 0])])
+def test_winograd_stands_for_conv(torch_cuda, stride, k, pads):
+    t = torch_cuda
+    x, w = randn(2, 5, 9, 8), randn(7, 5, k, k)
+    p = {"kernel_shape": [k, k], "strides": [stride, stride], "pads": pads, "dilations": [1, 1], "group": 1}
+    ref = O.conv2d(x, w, None, **p)
+    outs = call("winograd_forward_f32", [dev(t, x), dev(t, w)], [arena(t, ref.size)], p)
+    assert tuple(outs[0].shape) == ref.shape
+    assert rel(host(outs[0]), ref) < RTOL
+
+
+def test_layernorm_and_residual_norm(torch_cuda):
+    t = torch_cuda
+    for cols in (7, 64, 256, 1024, 2000):
+        x, r, g, b = randn(5, cols), randn(5, cols), randn(cols), randn(cols)
+        outs = call("fused_layer_norm_f32", [dev(t, x), dev(t, g), dev(t, b)], [arena(t, x.size)],
+                    {"axis": -1, "epsilon": 1e-5})
+        assert rel(host(outs[0]), O.layer_norm(x, g, b)) < RTOL
+        outs = call("fused_residual_norm_f32", [dev(t, x), dev(t, r), dev(t, g), dev(t, b)], [arena(t, x.size)],
+                    {"axis": -1, "epsilon": 1e-5})
+        assert rel(host(outs[0]), O.residual_layer_norm(x, r, g, b)) < RTOL
+
+
+def test_attention_scores(torch_cuda):
+    t = torch_cuda
+    B, H, S, D = 2, 3, 37, 16
+    q, kT = randn(B, H, S, D), randn(B, H, D, S)
+    div = np.array([4.0], np.float32)
+    mask = np.triu(np.full((S, S), -1e9, np.float32), 1).reshape(1, 1, S, S)
+    outs = call("fused_attention_scores_f32", [dev(t, q), dev(t, kT), dev(t, div), dev(t, mask)],
+                [arena(t, B * H * S * S)], {"axis": -1})
+    assert rel(host(outs[0]), O.attention_scores(q, kT, div, mask)) < RTOL
+
+
+def test_layout_kernels(torch_cuda):
+    t = torch_cuda
+    x = randn(2, 6, 4, 8)
+    outs = call("transpose", [dev(t, x)], [arena(t, x.size)], {"perm": [0, 2, 1, 3]})
+    assert np.array_equal(host(outs[0]), x.transpose(0, 2, 1, 3))
+    outs = call("fused_transpose_reshape_f32", [dev(t, x), dev(t, np.array([0, 0, 48], np.int64))],
+                [arena(t, x.size)], {"perm": [0, 2, 1, 3]})
+    assert np.array_equal(host(outs[0]), x.transpose(0, 2, 1, 3).reshape(2, 4, 48))
+    outs = call("reshape", [dev(t, x), dev(t, np.array([0, -1], np.int64))], [arena(t, x.size)], {})
+    assert np.array_equal(host(outs[0]), x.reshape(2, -1))
+    outs = call("flatten", [dev(t, x)], [arena(t, x.size)], {"axis": 2})
+    assert np.array_equal(host(outs[0]), x.reshape(12, 32))
+    y = randn(2, 5, 12)
+    outs = call("split", [dev(t, y), dev(t, np.array([3, 4, 5], np.int64))],
+                [arena(t, 100), arena(t, 100), arena(t, 100)], {"axis": -1})
+    for o, r in zip(outs, O.split(y, [3, 4, 5], -1)):
+        assert np.array_equal(host(o), r)
+    outs = call("split", [dev(t, y)], [arena(t, 100), arena(t, 100)], {"axis": -1, "_num_outputs": 2})
+    for o, r in zip(outs, O.split(y, [6, 6], -1)):
+        assert np.array_equal(host(o), r)
+    mm = randn(2 * 3 * 4, 5)
+    outs = call("conv_reshape_f32", [dev(t, mm)], [arena(t, mm.size)], {"_batch_size": 2, "_output_spatial": [3, 4]})
+    assert np.array_equal(host(outs[0]), mm.reshape(2, 3, 4, 5).transpose(0, 3, 1, 2))
+
+
+def test_gather(torch_cuda):
+    t = torch_cuda
+    table = randn(50, 12)
+    ids = RNG.integers(-50, 50, size=(3, 7)).astype(np.int64)
+    outs = call("gather", [dev(t, table), dev(t, ids)], [arena(t, 3 * 7 * 12)], {"axis": 0})
+    assert np.array_equal(host(outs[0]), O.gather(table, ids, 0))
+    x = randn(4, 9, 6)
+    outs = call("gather", [dev(t, x), dev(t, np.array([8], np.int64))], [arena(t, 24)], {"axis": 1})
+    assert np.array_equal(host(outs[0]), O.gather(x, [8], 1))
+
+
+def test_unknown_kernel_fails_closed(torch_cuda):
+    from hackathon_b200.kernel_registry import lookup
+    with pytest.raises(RuntimeError, match="Unknown kernel"):
+        lookup("sigmoid_f32")
+
+
+# ---------------------------------------------------------------- tensor cores
+
+def _bf16(t, a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda().to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K,act,res", [(128, 64, 64, 0, 0), (300, 128, 192, 1, 0), (1000, 256, 512, 2, 1),
+                                           (257, 96, 72, 0, 1), (4096, 512, 1024, 1, 1)])
+def test_gemm_tc(torch_cuda, M, N, K, act, res):
+    import torch
+    from hackathon_b200 import _lib as L
+    a, w, b = round_bf16(randn(M, K)), round_bf16(randn(N, K) * 0.1), randn(N)
+    r = randn(M, N)
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    g = L.GemmTcParams()
+    g.M, g.N, g.K, g.bias_mode, g.act, g.has_residual, g.block_n = M, N, K, L.BIAS_COL, act, res, 0
+    ta, tw, tb, tr = _bf16(torch, a), _bf16(torch, w), dev(torch, b), dev(torch, r)
+    ins = [L.make_tensor(ta.data_ptr(), L.BF16, (M, K)), L.make_tensor(tw.data_ptr(), L.BF16, (N, K)),
+           L.make_tensor(tb.data_ptr(), L.F32, (N,))]
+    if res:
+        ins.append(L.make_tensor(tr.data_ptr(), L.F32, (M, N)))
+    L.launch(L.K_GEMM_TC, ins, [L.make_tensor(out.data_ptr(), L.F32, (M, N))], g,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + b
+    if res:
+        ref = ref + r
+    if act == 1:
+        ref = np.maximum(ref, 0)
+    elif act == 2:
+        ref = O.gelu_erf(ref.astype(np.float32))
+    assert rel(host(out), ref) < 2e-5
+
+
+@pytest.mark.parametrize("n,h,cin,cout,k,stride,res", [(2, 32, 64, 64, 3, 1, 0), (3, 16, 64, 128, 3, 2, 0),
+                                                       (4, 16, 128, 128, 3, 1, 1), (8, 8, 128, 256, 1, 2, 0),
+                                                       (10, 4, 256, 512, 3, 1, 1), (16, 8, 256, 512, 3, 2, 0)])
+def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res):
+    import torch
+    from hackathon_b200 import _lib as L
+    pad = k // 2
+    x = round_bf16(randn(n, cin, h, h))
+    w = round_bf16(randn(cout, cin, k, k) * 0.05)
+    b = randn(cout)
+    ref = O.conv2d(x, w, b, strides=[stride, stride], pads=[pad] * 4)
+    ho = ref.shape[2]
+    r = round_bf16(randn(n, cout, ho, ho)) if res else None
+    if res:
+        ref = np.maximum(ref + r, 0)
+    xn = _bf16(torch, x.transpose(0, 2, 3, 1))
+    wn = _bf16(torch, w.transpose(0, 2, 3, 1))
+    tb = dev(torch, b)
+    out = torch.empty((n, ho, ho, cout), dtype=torch.bfloat16, device="cuda")
+    cp = L.ConvTcParams()
+    cp.n, cp.h, cp.w, cp.cin, cp.cout, cp.ho, cp.wo, cp.k, cp.stride, cp.pad = n, h, h, cin, cout, ho, ho, k, stride, pad
+    cp.has_residual, cp.act, cp.block_n = res, 1 if res else 0, 0
+    ins = [L.make_tensor(xn.data_ptr(), L.BF16, (n, h, h, cin)), L.make_tensor(wn.data_ptr(), L.BF16, (cout, k, k, cin)),
+           L.make_tensor(tb.data_ptr(), L.F32, (cout,))]
+    if res:
+        rn = _bf16(torch, r.transpose(0, 2, 3, 1))
+        ins.append(L.make_tensor(rn.data_ptr(), L.BF16, (n, ho, ho, cout)))
+    L.launch(L.K_CONV_TC, ins, [L.make_tensor(out.data_ptr(), L.BF16, (n, ho, ho, cout))], cp,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    got = out.float().cpu().numpy().transpose(0, 3, 1, 2)
+    # bf16 output rounding: half an ulp of bf16 relative to the largest value
+    assert rel(got, ref) < 8e-3
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("B,S,H", [(2, 128, 4), (1, 200, 2), (3, 64, 1)])
+def test_flash_attention(torch_cuda, dt, B, S, H):
+    import torch
+    from hackathon_b200 import _lib as L
+    D = 64
+    qkv = randn(B, S, 3, H, D)
+    if dt == "bf16":
+        qkv = round_bf16(qkv)
+    q, k, v = (qkv[:, :, i].transpose(0, 2, 1, 3) for i in range(3))
+    ref = O.causal_attention(q, k, v, 1.0 / 8.0).transpose(0, 2, 1, 3).reshape(B, S, H * D)
+    tq = dev(torch, qkv) if dt == "f32" else _bf16(torch, qkv)
+    out = torch.empty((B, S, H * D), dtype=tq.dtype, device="cuda")
+    code = L.F32 if dt == "f32" else L.BF16
+    fp = L.FlashParams(B, S, H, D, 1.0 / 8.0, 1)
+    L.launch(L.K_FLASH_ATTN, [L.make_tensor(tq.data_ptr(), code, (B, S, 3, H, D))],
+             [L.make_tensor(out.data_ptr(), code, (B, S, H * D))], fp, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    assert rel(got, ref) < (RTOL if dt == "f32" else 2e-2)
