@@ -198,6 +198,10 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--per-gpu-batch", type=int, default=0,
+                    help="override the per-GPU batch (profiling small cases)")
+    ap.add_argument("--kernel-report", action="store_true",
+                    help="print per-launch device times to stderr")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
@@ -222,6 +226,8 @@ def main():
         base, extra = divmod(total, ws)
         per = base + (1 if rank < extra else 0)
         start = rank * base + min(rank, extra)
+    if args.per_gpu_batch:
+        per, total, start = args.per_gpu_batch, args.per_gpu_batch * ws, rank * args.per_gpu_batch
     feeds_all = make_inputs(g, total) if (scaling == "strong" or ws == 1) else None
     if feeds_all is not None:
         feeds = {k: v[start:start + per] for k, v in feeds_all.items()}
@@ -285,6 +291,12 @@ def main():
     for (label, ms), si in zip(kt, ex_dev.step_of_kernel):
         fam_ms[label] = fam_ms.get(label, 0.0) + ms
         fam_flops[label] = fam_flops.get(label, 0.0) + prog.steps[si].flops
+    if args.kernel_report and rank == 0:
+        for (label, ms), si in zip(kt, ex_dev.step_of_kernel):
+            st = prog.steps[si]
+            shp = prog.tensors[st.outputs[0]].shape
+            tf = st.flops / (ms / 1e3) / 1e12 if ms > 0 and st.flops else 0.0
+            print(f"[kernel] {si:3d} {label:16s} out={shp} {ms:8.4f} ms {tf:7.1f} TFLOP/s", file=sys.stderr)
     top = max(fam_ms, key=fam_ms.get)
     peaks, src = load_peaks()
     launches_top = sum(1 for (label, _) in kt if label == top)

@@ -96,7 +96,9 @@ class Program:
             for t in s.inputs:
                 last[t] = max(last.get(t, i), i)
                 first.setdefault(t, i)
-        for name in self.outputs:
+        # Outputs and inputs live for the whole pass: inputs may be uploaded once
+        # and replayed (kernels-only executor), so their bytes are never reused.
+        for name in list(self.outputs) + list(self.inputs):
             last[name] = len(self.steps)
         acts = [t for t in self.tensors.values() if t.kind in ("act", "input") and t.name in first]
         # best-fit free list over [base, ...)
