@@ -246,6 +246,21 @@ int c3b_device_status(int* status);
 /* Number of streaming multiprocessors of the current device. */
 int c3b_sm_count(void);
 
+/* Stem convolution that allocates nothing: the same computation as
+ * C3B_K_STEM_IM2COL followed by C3B_K_GEMM_TC (out = act(patches(x) * w^T + bias),
+ * x NCHW f32, w [Cout, kpad] bf16, bias f32 [Cout], out [N*Ho*Wo, Cout] bf16),
+ * but the bf16 patch matrix lives in a fixed 16 MiB device array inside this
+ * library instead of caller-allocated memory.  No counterpart in the reference:
+ * it exists for callers that cannot call cudaMalloc (they run inside a memory
+ * budget owned by someone else, or on a hot path where allocation would
+ * synchronise the device).  Limit: N*Ho*Wo*kpad*2 <= 16 MiB, otherwise
+ * C3B_E_INVALID with a message.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  All calls share the one array: calls that
+ * overlap on the GPU (different streams, or different host threads) race. */
+int c3b_stem_conv_noalloc(const c3b_tensor* x, const c3b_tensor* w, const c3b_tensor* bias,
+                          const c3b_tensor* out, const c3b_stem_params* p, int act, void* stream);
+
 /* ------------------------------------------------------------------ plans
  * Native replacement for PlannedGraphExecutor.run_planned
  * (c35/executor.py:723-903).  Arena = plan.pool_stats.peak_reserved_bytes
