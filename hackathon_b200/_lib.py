@@ -26,12 +26,12 @@ TENSOR_ARENA = 1
 
 # kernel ids
 K_EW, K_COPY, K_IM2COL, K_REDUCE, K_GEMM, K_LAYERNORM, K_SOFTMAX, K_ATTN_SCORES, K_GATHER, K_CONV, \
-    K_GEMM_TC, K_CONV_TC, K_FLASH_ATTN, K_EMBED, K_STEM_IM2COL, K_GAP_NHWC = range(1, 17)
+    K_GEMM_TC, K_CONV_TC, K_FLASH_ATTN, K_EMBED, K_STEM_IM2COL, K_GAP_NHWC, K_STEM_CONV = range(1, 18)
 KERNEL_NAMES = {
     0: "noop", K_EW: "ew", K_COPY: "copy", K_IM2COL: "im2col", K_REDUCE: "reduce", K_GEMM: "gemm_simt",
     K_LAYERNORM: "layernorm", K_SOFTMAX: "softmax", K_ATTN_SCORES: "attn_scores", K_GATHER: "gather",
     K_CONV: "conv_simt", K_GEMM_TC: "gemm_tc", K_CONV_TC: "conv_tc", K_FLASH_ATTN: "flash_attn",
-    K_EMBED: "embed", K_STEM_IM2COL: "stem_im2col", K_GAP_NHWC: "gap_nhwc",
+    K_EMBED: "embed", K_STEM_IM2COL: "stem_im2col", K_GAP_NHWC: "gap_nhwc", K_STEM_CONV: "stem_conv",
 }
 
 # ew ops
@@ -103,7 +103,7 @@ class GemmTcParams(C.Structure):
 
 class ConvTcParams(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("n", "h", "w", "cin", "cout", "ho", "wo", "k", "stride", "pad",
-                                         "has_residual", "act", "block_n", "_pad")]
+                                         "has_residual", "act", "block_n", "mode")]
 
 
 class FlashParams(C.Structure):
@@ -118,6 +118,10 @@ class EmbedParams(C.Structure):
 class StemParams(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("n", "c", "h", "w", "ho", "wo", "kpad", "_pad")] + \
                [("g", ConvGeom), ("_pad2", C.c_int32 * 2)]
+
+
+class StemConvParams(C.Structure):
+    _fields_ = [("geom", StemParams), ("cout", C.c_int32), ("act", C.c_int32)]
 
 
 class GapParams(C.Structure):

@@ -70,6 +70,7 @@ static const NameEntry kNames[] = {
     {"gemm_bias_act_bf16", C3B_K_GEMM_TC}, {"flash_attention_f32", C3B_K_FLASH_ATTN},
     {"flash_attention_bf16", C3B_K_FLASH_ATTN}, {"embed_positions", C3B_K_EMBED},
     {"stem_im2col_bf16", C3B_K_STEM_IM2COL}, {"global_avgpool_nhwc", C3B_K_GAP_NHWC},
+    {"stem_conv_bias_act_bf16", C3B_K_STEM_CONV},
     {"layout_copy", C3B_K_COPY},
 };
 
@@ -213,6 +214,12 @@ int dispatch(int kid, const c3b_tensor* in, int n_in, const c3b_tensor* out, int
       if ((rc = get_params(params, len, p))) return rc;
       C3B_REQUIRE(n_in == 1 && n_out == 1, "stem im2col: one input, one output");
       return launch_stem_im2col(in[0], out[0], p, s);
+    }
+    case C3B_K_STEM_CONV: {
+      c3b_stem_conv_params p;
+      if ((rc = get_params(params, len, p))) return rc;
+      C3B_REQUIRE(n_out == 1, "stem conv: one output");
+      return launch_stem_conv(in, n_in, out[0], p, s);
     }
     case C3B_K_GAP_NHWC: {
       c3b_gap_params p;

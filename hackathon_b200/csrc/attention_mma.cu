@@ -143,6 +143,8 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
     }
     // scale, mask, running max
     const int k0 = kt * KB;
+    // Only the diagonal tile (causal) and the sequence tail need masking.
+    const bool need_mask = (p.causal && k0 + KB > qb * QB) || (k0 + KB > p.seq);
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int nb = 0; nb < 8; ++nb) {
@@ -150,8 +152,10 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
       for (int j = 0; j < 2; ++j) {
         const int key = k0 + nb * 8 + 2 * t + j;
         float v0 = s[nb][j] * sl2, v1 = s[nb][2 + j] * sl2;
-        if (key >= p.seq || (p.causal && key > row0)) v0 = -INFINITY;
-        if (key >= p.seq || (p.causal && key > row1)) v1 = -INFINITY;
+        if (need_mask) {
+          if (key >= p.seq || (p.causal && key > row0)) v0 = -INFINITY;
+          if (key >= p.seq || (p.causal && key > row1)) v1 = -INFINITY;
+        }
         s[nb][j] = v0;
         s[nb][2 + j] = v1;
         mx0 = fmaxf(mx0, v0);

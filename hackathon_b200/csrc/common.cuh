@@ -103,6 +103,8 @@ int launch_gather(const c3b_tensor& data, const c3b_tensor& idx, const c3b_tenso
                   const c3b_gather_params& p, cudaStream_t s);
 int launch_embed(const c3b_tensor* in, const c3b_tensor& out, const c3b_embed_params& p, cudaStream_t s);
 int launch_stem_im2col(const c3b_tensor& in, const c3b_tensor& out, const c3b_stem_params& p, cudaStream_t s);
+int launch_stem_conv(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_stem_conv_params& p,
+                     cudaStream_t s);
 int launch_gap_nhwc(const c3b_tensor& in, const c3b_tensor& out, const c3b_gap_params& p, cudaStream_t s);
 int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_params& p, cudaStream_t s);
 int launch_conv_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_params& p, cudaStream_t s);

@@ -13,6 +13,7 @@
 // (transA/transB/broadcast batch) and NCHW / NHWC implicit-GEMM convolution (the
 // im2col_f32 -> matmul_f32 -> conv_reshape_f32 -> add_bias_f32 -> relu chain of
 // c32/decompositions.py:301-378 in one launch, with no patch matrix in memory).
+#include <algorithm>
 #include "common.cuh"
 
 namespace c3b {
@@ -172,6 +173,33 @@ __global__ void __launch_bounds__(NT) simt_gemm_kernel(AL A, BL B, Epi E, int64_
   }
 }
 
+// Skinny GEMM (N <= 32): one warp per output row, lanes split K, the N partial
+// sums are reduced with warp shuffles.  A 128x128 tile grid would leave most
+// of the GPU idle for shapes like the classifier heads ([B,512] x [512,10]).
+template <class AL, class BL>
+__global__ void __launch_bounds__(256) skinny_gemm_kernel(AL A, BL B, Epi E, int64_t M, int N, int64_t K) {
+  const int lane = threadIdx.x & 31;
+  const int bz = blockIdx.z;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < M; m += nw) {
+    float acc[32];
+#pragma unroll
+    for (int n = 0; n < 32; ++n) acc[n] = 0.f;
+    for (int64_t k = lane; k < K; k += 32) {
+      const float av = A.get(bz, m, k);
+#pragma unroll
+      for (int n = 0; n < 32; ++n)
+        if (n < N) acc[n] = fmaf(av, B.get(bz, n, k), acc[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < 32; ++n) {
+      if (n >= N) break;
+      const float v = warp_sum(acc[n]);
+      if (lane == 0) E.put(bz, m, n, v);
+    }
+  }
+}
+
 int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_params& p,
                      cudaStream_t s) {
   const int need = 2 + (p.bias_mode != C3B_BIAS_NONE) + (p.has_residual ? 1 : 0);
@@ -205,6 +233,13 @@ int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, cons
   if (p.M == 0 || p.N == 0) return C3B_OK;
   MatLoad al{a.ptr, a.dtype, p.M, p.K, p.stride_a, p.trans_a != 0};
   MatLoad bl{b.ptr, b.dtype, p.N, p.K, p.stride_b, p.trans_b == 0};
+  if (p.N <= 32 && p.K >= 64) {
+    const int blocks = (int)std::min<int64_t>((p.M * 32 + 255) / 256, (int64_t)sm_count() * 8);
+    dim3 g2((unsigned)blocks, 1, (unsigned)p.batch);
+    skinny_gemm_kernel<MatLoad, MatLoad><<<g2, 256, 0, s>>>(al, bl, e, p.M, (int)p.N, p.K);
+    C3B_CHECK_CUDA(cudaGetLastError());
+    return C3B_OK;
+  }
   dim3 grid((unsigned)((p.N + BN - 1) / BN), (unsigned)((p.M + BM - 1) / BM), (unsigned)p.batch);
   C3B_REQUIRE(grid.y <= 65535, "gemm: M too large for the SIMT path");
   simt_gemm_kernel<MatLoad, MatLoad><<<grid, NT, 0, s>>>(al, bl, e, p.M, p.N, p.K);

@@ -34,6 +34,7 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int NUM_THREADS = 192;
+constexpr int HALO_THREADS = 320;  // producer, MMA, 8 epilogue warps
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 
 struct __align__(64) TmaMaps {
@@ -57,6 +58,8 @@ struct TcArgs {
   int pix;         // Ho*Wo
   int wo, bh;      // box geometry
   int cin;
+  // halo mode (3x3 stride-1 convolution, tc_conv_halo_kernel)
+  int img, wt, wblocks, ho, n_img, rows, halo_bytes, hstages;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -173,7 +176,110 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
+// 32 consecutive fp32 accumulator columns of this thread's TMEM lane, one wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Epilogue for 32 columns of one bf16 output row whose residual (bf16) was
+// prefetched into `rv` (4 x 16 bytes): +bias -> +residual -> act -> 64-byte store.
+__device__ __forceinline__ void store32_bf16(const TcArgs& a, int64_t off, int64_t col0, float* v, const uint4* rv) {
+  if (a.bias) {
+    const float4* bp = reinterpret_cast<const float4*>(a.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = __ldg(bp + i);
+      v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+    }
+  }
+  if (rv) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[8 * i + j] += __bfloat162float(rb[j]);
+    }
+  }
+  uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(apply_act(v[8 * i + j], a.act));
+    op[i] = *reinterpret_cast<const uint4*>(o);
+  }
+}
+
+// Residual of 32 consecutive columns (bf16: 64 bytes, f32: 128 bytes) as raw words.
+__device__ __forceinline__ void load_res32(const TcArgs& a, int64_t off, uint4* r) {
+  if (a.dt_res == C3B_BF16) {
+    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = rp[i];
+  } else {
+    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const float*>(a.res) + off);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = rp[i];
+  }
+}
+
+// +bias -> +residual -> act -> store 32 columns of one output row (bf16 or f32).
+__device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t col0, float* v, const uint4* r) {
+  if (a.bias) {
+    const float4* bp = reinterpret_cast<const float4*>(a.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = __ldg(bp + i);
+      v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+    }
+  }
+  if (r) {
+    if (a.dt_res == C3B_BF16) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&r[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[8 * i + j] += __bfloat162float(rb[j]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float* rf = reinterpret_cast<const float*>(&r[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[4 * i + j] += rf[j];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i], a.act);
+  if (a.dt_out == C3B_BF16) {
+    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(v[8 * i + j]);
+      op[i] = *reinterpret_cast<const uint4*>(o);
+    }
+  } else {
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) op[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+}
+
+__global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled stages.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -201,7 +307,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], 8);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -296,61 +402,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // ---------------- epilogue warps 2..9: warp w reads TMEM lane quarter
+    // (w % 4) and one half of the tile's columns; the residual of the first
+    // 32-column chunk is prefetched before waiting for the accumulator.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int cols = a.block_n >> 1;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
       const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
+      const int64_t row = (int64_t)mb * BM + q * 32 + lane;
+      const int64_t col_base = (int64_t)nb * a.block_n + half * cols;
+      const bool row_ok = row < a.M && col_base < a.N;
+      uint4 r0[8];
+      if (a.res && row_ok) load_res32(a, row * a.N + col_base, r0);
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 14);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int64_t row = (int64_t)mb * BM + q * 32 + lane;
-      const bool row_ok = row < a.M;
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.block_n);
-      for (int c0 = 0; c0 < a.block_n; c0 += 16) {
-        float v[16];
-        tmem_ld16(tbase + c0, v);
-        const int64_t col0 = (int64_t)nb * a.block_n + c0;
-        if (!row_ok || col0 >= a.N) continue;
-        if (a.bias) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] += a.bias[col0 + i];
-        }
-        const int64_t off = row * a.N + col0;
-        if (a.res) {
-          if (a.dt_res == C3B_BF16) {
-            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off);
-            uint4 r0 = rp[0], r1 = rp[1];
-            const __nv_bfloat16* rb0 = reinterpret_cast<const __nv_bfloat16*>(&r0);
-            const __nv_bfloat16* rb1 = reinterpret_cast<const __nv_bfloat16*>(&r1);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              v[i] += __bfloat162float(rb0[i]);
-              v[i + 8] += __bfloat162float(rb1[i]);
-            }
-          } else {
-            const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + off);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              float4 r = rp[i];
-              v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
-            }
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = apply_act(v[i], a.act);
-        if (a.dt_out == C3B_BF16) {
-          __align__(16) __nv_bfloat16 o[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float2bfloat16_rn(v[i]);
-          uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
-          op[0] = reinterpret_cast<const uint4*>(o)[0];
-          op[1] = reinterpret_cast<const uint4*>(o)[1];
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.block_n + half * cols);
+      for (int c0 = 0; c0 < cols; c0 += 32) {
+        float v[32];
+        tmem_ld32(tbase + c0, v);
+        if (!row_ok || col_base + c0 >= a.N) continue;
+        const int64_t off = row * a.N + col_base + c0;
+        if (a.res && c0 > 0) {
+          uint4 r1[8];
+          load_res32(a, off, r1);
+          finish32(a, off, col_base + c0, v, r1);
         } else {
-          float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) op[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          finish32(a, off, col_base + c0, v, a.res ? r0 : nullptr);
         }
       }
       tc_fence_before();
@@ -364,6 +445,259 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   __syncthreads();
   if (*abort_flag) {
     // Give copies still in flight time to land before shared memory is released.
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+  }
+}
+
+// Epilogue for one 16-column chunk of one output row: +bias [+residual] -> act -> store.
+__device__ __forceinline__ void store_chunk(const TcArgs& a, int64_t off, int64_t col0, float* v) {
+  if (a.bias) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] += a.bias[col0 + i];
+  }
+  if (a.res) {
+    if (a.dt_res == C3B_BF16) {
+      const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off);
+      uint4 r0 = rp[0], r1 = rp[1];
+      const __nv_bfloat16* rb0 = reinterpret_cast<const __nv_bfloat16*>(&r0);
+      const __nv_bfloat16* rb1 = reinterpret_cast<const __nv_bfloat16*>(&r1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[i] += __bfloat162float(rb0[i]);
+        v[i + 8] += __bfloat162float(rb1[i]);
+      }
+    } else {
+      const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + off);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float4 r = rp[i];
+        v[4 * i] += r.x; v[4 * i + 1] += r.y; v[4 * i + 2] += r.z; v[4 * i + 3] += r.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = apply_act(v[i], a.act);
+  if (a.dt_out == C3B_BF16) {
+    __align__(16) __nv_bfloat16 o[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = __float2bfloat16_rn(v[i]);
+    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
+    op[0] = reinterpret_cast<const uint4*>(o)[0];
+    op[1] = reinterpret_cast<const uint4*>(o)[1];
+  } else {
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) op[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+}
+
+// 3x3 stride-1 pad-1 convolution with halo tiles.
+//
+// A super-tile is `rows` output rows x `wt` output columns x `img` images
+// (each row block = 128 pixels = one M=128 MMA).  The producer loads the input
+// halo for a 64-channel block ONCE — (rows+2) input rows x (wt+2) columns x
+// img images, 4-D box over dims (C, N, W, H) so that shared-memory row index
+// = img + IMG*(w + (wt+2)*h) — and every one of the 9 taps is then a shifted
+// window of that halo: tap (r,s) for output row j starts at shared row
+// ((j+r)*(wt+2) + s)*IMG, always a multiple of 8 rows (IMG >= 8), so each
+// window is a standard 1024-byte-aligned SW128 K-major operand.  Each weight
+// tap (BN x 64) is loaded once and used by all `rows` MMAs.  Versus one TMA
+// window per tap, this cuts L2->SM traffic about 3x for Cout <= 128.
+__global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __grid_constant__ TmaMaps maps,
+                                                                      const TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int bst = a.stages;       // weight-tap ring depth
+  const int hst = a.hstages;      // halo ring depth
+  const uint32_t hbytes_al = (uint32_t)((a.halo_bytes + 1023) & ~1023);
+  const uint32_t b_bytes = (uint32_t)a.block_n * BK * 2;
+  uint8_t* sh = smem;
+  uint8_t* sb = smem + (size_t)hst * hbytes_al;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + (size_t)bst * b_bytes);
+  uint64_t* hfull = bars;
+  uint64_t* hempty = hfull + hst;
+  uint64_t* bfull = hempty + hst;
+  uint64_t* bempty = bfull + bst;
+  uint64_t* tfull = bempty + bst;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int R = a.rows;
+  const uint32_t tmem_cols = (uint32_t)(a.block_n * R * 2);
+  const int WT2 = a.wt + 2;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < hst; ++i) {
+      mbar_init(&hfull[i], 1);
+      mbar_init(&hempty[i], 1);
+    }
+    for (int i = 0; i < bst; ++i) {
+      mbar_init(&bfull[i], 1);
+      mbar_init(&bempty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a[0])));
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)));
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int hs = 0, bs = 0;
+      uint32_t hph = 0, bph = 0;
+      for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+        const int nb = t % a.n_tiles_n;
+        int pt = t / a.n_tiles_n;
+        const int wb = pt % a.wblocks;
+        pt /= a.wblocks;
+        const int hb = pt % (a.ho / R);
+        const int ib = pt / (a.ho / R);
+        const int n0 = ib * a.img, w0 = wb * a.wt, h0 = hb * R;
+        for (int cb = 0; cb < a.cblocks; ++cb) {
+          if (!mbar_wait(&hempty[hs], hph ^ 1, abort_flag, 21)) goto producer_done;
+          mbar_arrive_tx(&hfull[hs], (uint32_t)a.halo_bytes);
+          tma_load_4d(sh + (size_t)hs * hbytes_al, &maps.a[0], &hfull[hs], cb * BK, n0, w0 - 1, h0 - 1);
+          if (++hs == hst) { hs = 0; hph ^= 1; }
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!mbar_wait(&bempty[bs], bph ^ 1, abort_flag, 22)) goto producer_done;
+            mbar_arrive_tx(&bfull[bs], b_bytes);
+            tma_load_2d(sb + (size_t)bs * b_bytes, &maps.b, &bfull[bs], tap * a.cin + cb * BK, nb * a.block_n);
+            if (++bs == bst) { bs = 0; bph ^= 1; }
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc(BM, a.block_n);
+      int hs = 0, bs = 0, acc = 0;
+      uint32_t hph = 0, bph = 0, acc_phase = 0;
+      for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 23)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem_base + (uint32_t)(acc * R * a.block_n);
+        bool ok = true;
+        for (int cb = 0; cb < a.cblocks && ok; ++cb) {
+          if (!mbar_wait(&hfull[hs], hph, abort_flag, 24)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t hbase = smem_u32(sh + (size_t)hs * hbytes_al);
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!mbar_wait(&bfull[bs], bph, abort_flag, 25)) { ok = false; break; }
+            tc_fence_after();
+            const int r = tap / 3, s = tap % 3;
+            const uint32_t b_addr = smem_u32(sb + (size_t)bs * b_bytes);
+            for (int j = 0; j < R; ++j) {
+              const uint32_t a_addr = hbase + (uint32_t)(((j + r) * WT2 + s) * a.img) * 128u;
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                mma_bf16(d0 + (uint32_t)(j * a.block_n), smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32),
+                         idesc, (cb > 0 || tap > 0 || k > 0) ? 1u : 0u);
+            }
+            mma_commit(&bempty[bs]);
+            if (++bs == bst) { bs = 0; bph ^= 1; }
+          }
+          if (!ok) break;
+          mma_commit(&hempty[hs]);
+          if (++hs == hst) { hs = 0; hph ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // 8 epilogue warps: warp w reads TMEM lane quarter (w % 4) and one half of
+    // the tile's columns.  Residual rows are prefetched into registers before
+    // waiting for the accumulator, so their latency overlaps the MMAs.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int cols = a.block_n >> 1;  // 32 or 64 columns per warp
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+      const int nb = t % a.n_tiles_n;
+      int pt = t / a.n_tiles_n;
+      const int wb = pt % a.wblocks;
+      pt /= a.wblocks;
+      const int hb = pt % (a.ho / R);
+      const int ib = pt / (a.ho / R);
+      const int m = q * 32 + lane;
+      const int img = ib * a.img + (m % a.img);
+      const int w = wb * a.wt + m / a.img;
+      const bool img_ok = img < a.n_img;
+      const int64_t col_base = (int64_t)nb * a.block_n + half * cols;
+      // residual of the first 32 columns of both rows, prefetched
+      uint4 rv[2][4];
+      if (a.res && img_ok) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int64_t pix = ((int64_t)img * a.ho + hb * R + j) * a.wo + w;
+          const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) +
+                                                           pix * a.N + col_base);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) rv[j][i] = rp[i];
+        }
+      }
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 26);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int64_t pix = ((int64_t)img * a.ho + hb * R + j) * a.wo + w;
+        const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) +
+                            (uint32_t)((acc * R + j) * a.block_n + half * cols);
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 32) {
+          if (c0 >= cols) break;
+          float v[32];
+          tmem_ld32(tb + c0, v);
+          if (!img_ok) continue;
+          if (a.res && c0 > 0) {
+            uint4 r2[4];
+            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) +
+                                                             pix * a.N + col_base + c0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) r2[i] = rp[i];
+            store32_bf16(a, pix * a.N + col_base + c0, col_base + c0, v, r2);
+          } else {
+            store32_bf16(a, pix * a.N + col_base + c0, col_base + c0, v, a.res ? rv[j] : nullptr);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
     for (int i = 0; i < 1000; ++i) __nanosleep(1000);
   }
   if (warp == 1) {
@@ -427,7 +761,7 @@ static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s) {
   }
   int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
   if (grid < 1) return C3B_OK;
-  tc::tc_gemm_kernel<<<grid, tc::NUM_THREADS, smem, s>>>(maps, a);
+  tc::tc_gemm_kernel<<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
@@ -465,7 +799,7 @@ int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   C3B_REQUIRE(n_in >= 2, "tc gemm: needs A and B");
   C3B_REQUIRE(in[0].dtype == C3B_BF16 && in[1].dtype == C3B_BF16, "tc gemm: A and B must be bf16");
   C3B_REQUIRE(p.K > 0 && p.K % 8 == 0, "tc gemm: K must be a positive multiple of 8");
-  C3B_REQUIRE(p.N > 0 && p.N % 16 == 0, "tc gemm: N must be a positive multiple of 16");
+  C3B_REQUIRE(p.N > 0 && p.N % 32 == 0, "tc gemm: N must be a positive multiple of 32");
   C3B_REQUIRE(p.M >= 0 && p.M < (int64_t)1 << 31, "tc gemm: M range");
   C3B_REQUIRE(numel(in[0]) >= p.M * p.K && numel(in[1]) >= p.N * p.K, "tc gemm: operand extents");
   C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0, "tc gemm: 16-byte alignment");
@@ -501,7 +835,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   C3B_REQUIRE(n_in == 3 + (p.has_residual ? 1 : 0), "tc conv: inputs x, w, bias [, residual]");
   C3B_REQUIRE(in[0].dtype == C3B_BF16 && in[1].dtype == C3B_BF16, "tc conv: bf16 activations and weights");
   C3B_REQUIRE(p.cin % 64 == 0, "tc conv: Cin must be a multiple of 64");
-  C3B_REQUIRE(p.cout % 16 == 0, "tc conv: Cout must be a multiple of 16");
+  C3B_REQUIRE(p.cout % 32 == 0, "tc conv: Cout must be a multiple of 32");
   C3B_REQUIRE(p.stride == 1 || p.stride == 2, "tc conv: stride 1 or 2");
   C3B_REQUIRE(p.ho == (p.h + 2 * p.pad - p.k) / p.stride + 1 && p.wo == (p.w + 2 * p.pad - p.k) / p.stride + 1,
               "tc conv: output extents");
@@ -537,6 +871,48 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   memset(&maps, 0, sizeof(maps));
   uint8_t* x = static_cast<uint8_t*>(in[0].ptr);
   const uint64_t C = p.cin;
+  {
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)p.cout};
+    uint64_t str[1] = {(uint64_t)K * 2};
+    uint32_t box[2] = {tc::BK, (uint32_t)a.block_n};
+    if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box))) return rc;
+  }
+  // Halo mode: 3x3, stride 1, pad 1, Cout <= 128 (one weight tile), two output
+  // rows per super-tile.
+  const int wt = p.wo < 16 ? p.wo : 16;
+  if (p.mode == 0 && p.k == 3 && p.stride == 1 && p.pad == 1 && p.cout <= 128 && a.n_tiles_n == 1 &&
+      p.wo % wt == 0 && 128 % wt == 0 && (128 / wt) >= 8 && p.ho % 2 == 0) {
+    a.img = 128 / wt;
+    a.wt = wt;
+    a.wblocks = p.wo / wt;
+    a.ho = p.ho;
+    a.n_img = p.n;
+    a.rows = 2;
+    a.halo_bytes = 64 * a.img * (wt + 2) * (a.rows + 2) * 2;
+    a.n_tiles = ((p.n + a.img - 1) / a.img) * (p.ho / a.rows) * a.wblocks;
+    uint64_t dims[4] = {C, (uint64_t)p.n, (uint64_t)p.w, (uint64_t)p.h};
+    uint64_t str[3] = {(uint64_t)p.h * p.w * C * 2, C * 2, (uint64_t)p.w * C * 2};
+    uint32_t box[4] = {64, (uint32_t)a.img, (uint32_t)(wt + 2), (uint32_t)(a.rows + 2)};
+    if ((rc = encode(&maps.a[0], x, 4, dims, str, box))) return rc;
+    const size_t hb = ((size_t)a.halo_bytes + 1023) & ~(size_t)1023;
+    const size_t bb = (size_t)a.block_n * tc::BK * 2;
+    a.hstages = 2;
+    const size_t budget = 212 * 1024;
+    if (2 * hb + 2 * bb > budget) return fail(C3B_E_INVALID, "tc conv: halo tiles do not fit in shared memory");
+    int bst = (int)((budget - 2 * hb) / bb);
+    a.stages = bst > 8 ? 8 : bst;
+    const size_t smem = 1024 + 2 * hb + a.stages * bb + (2 * 2 + 2 * a.stages + 4) * 8 + 16;
+    static bool attr_halo = false;
+    if (!attr_halo) {
+      C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_conv_halo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          227 * 1024));
+      attr_halo = true;
+    }
+    int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
+    tc::tc_conv_halo_kernel<<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
+    C3B_CHECK_CUDA(cudaGetLastError());
+    return C3B_OK;
+  }
   if (p.stride == 1) {
     uint64_t dims[4] = {C, (uint64_t)p.w, (uint64_t)p.h, (uint64_t)p.n};
     uint64_t str[3] = {C * 2, (uint64_t)p.w * C * 2, (uint64_t)p.h * p.w * C * 2};
@@ -551,12 +927,6 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
         uint8_t* base = x + ((uint64_t)pr * p.w + ps) * C * 2;
         if ((rc = encode(&maps.a[pr * 2 + ps], base, 4, dims, str, box))) return rc;
       }
-  }
-  {
-    uint64_t dims[2] = {(uint64_t)K, (uint64_t)p.cout};
-    uint64_t str[1] = {(uint64_t)K * 2};
-    uint32_t box[2] = {tc::BK, (uint32_t)a.block_n};
-    if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box))) return rc;
   }
   return launch_tc(maps, a, s);
 }

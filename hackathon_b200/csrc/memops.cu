@@ -13,6 +13,7 @@
 //   SOFTMAX   fused_softmax (engine.py:1016-1075)
 //   ATTN      fused_attention_scores (engine.py:1250-1380)
 //   GATHER    gather (kernel_registry.py:744-752)
+#include <algorithm>
 #include "common.cuh"
 
 namespace c3b {
@@ -385,6 +386,94 @@ __global__ void layernorm_wide_kernel(const void* __restrict__ x, int dtx, const
   }
 }
 
+// Vectorised fast path: cols = 128*V, one warp per row, each lane owns V
+// groups of 4 consecutive columns (16-byte f32 / 8-byte bf16 accesses), the
+// row stays in registers between the two statistics passes.
+__device__ __forceinline__ void ld4(const float* p, float* v) {
+  float4 t = *reinterpret_cast<const float4*>(p);
+  v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+__device__ __forceinline__ void ld4(const __nv_bfloat16* p, float* v) {
+  uint2 t = *reinterpret_cast<const uint2*>(p);
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&t.x), b = *reinterpret_cast<__nv_bfloat162*>(&t.y);
+  float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+  v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
+}
+__device__ __forceinline__ void st4(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void st4(__nv_bfloat16* p, const float* v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 t;
+  t.x = *reinterpret_cast<uint32_t*>(&a);
+  t.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = t;
+}
+
+template <typename TI, typename TO, int V>
+__global__ void __launch_bounds__(256) layernorm_vec_kernel(const TI* __restrict__ x, const TI* __restrict__ res,
+                                                            const float* __restrict__ scale,
+                                                            const float* __restrict__ bias, TO* __restrict__ y,
+                                                            int64_t rows, float eps) {
+  constexpr int COLS = 128 * V;
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {
+    const int64_t base = row * COLS;
+    float v[V][4];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = i * 128 + lane * 4;
+      ld4(x + base + c, v[i]);
+      if (res) {
+        float r[4];
+        ld4(res + base + c, r);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] += r[j];
+      }
+      s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+    }
+    const float mean = warp_sum(s) * (1.0f / COLS);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float d = v[i][j] - mean;
+        q += d * d;
+      }
+    const float inv = rsqrtf(warp_sum(q) * (1.0f / COLS) + eps);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = i * 128 + lane * 4;
+      const float4 g = *reinterpret_cast<const float4*>(scale + c);
+      float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (bias) b = *reinterpret_cast<const float4*>(bias + c);
+      float o[4] = {(v[i][0] - mean) * inv * g.x + b.x, (v[i][1] - mean) * inv * g.y + b.y,
+                    (v[i][2] - mean) * inv * g.z + b.z, (v[i][3] - mean) * inv * g.w + b.w};
+      st4(y + base + c, o);
+    }
+  }
+}
+
+template <typename TI, typename TO>
+static bool launch_ln_vec(const void* x, const void* r, const float* sc, const float* b, void* y, int64_t rows,
+                          int64_t cols, float eps, cudaStream_t s, int grid) {
+#define C3B_LNV(V)                                                                                           \
+  layernorm_vec_kernel<TI, TO, V><<<grid, 256, 0, s>>>((const TI*)x, (const TI*)r, sc, b, (TO*)y, rows, eps); \
+  return true;
+  switch (cols) {
+    case 128: C3B_LNV(1)
+    case 256: C3B_LNV(2)
+    case 512: C3B_LNV(4)
+    case 1024: C3B_LNV(8)
+    case 2048: C3B_LNV(16)
+  }
+#undef C3B_LNV
+  return false;
+}
+
 int launch_layernorm(const c3b_tensor* in, int n_in, const c3b_tensor* out, int n_out,
                      const c3b_layernorm_params& p, cudaStream_t s) {
   int need = 2 + p.has_residual + p.has_bias;
@@ -406,7 +495,33 @@ int launch_layernorm(const c3b_tensor* in, int n_in, const c3b_tensor* out, int 
   int sdt = p.write_sum ? out[1].dtype : 0;
   int g = grid_for(p.rows * 32, 256);
   const float* bp = bi ? (const float*)bi->ptr : nullptr;
-#define C3B_LN(PL)                                                                                     \
+  const bool vec_ok = !p.write_sum && (x.dtype == C3B_F32 || x.dtype == C3B_BF16) &&
+                      (!res || res->dtype == x.dtype) && (out[0].dtype == C3B_F32 || out[0].dtype == C3B_BF16) &&
+                      ((uintptr_t)x.ptr % 16 == 0) && (!res || (uintptr_t)res->ptr % 16 == 0) &&
+                      ((uintptr_t)out[0].ptr % 16 == 0) && ((uintptr_t)sc.ptr % 16 == 0) &&
+                      (!bp || (uintptr_t)bp % 16 == 0);
+  if (vec_ok) {
+    // One warp per row, enough resident warps to cover HBM latency.
+    const int gv = (int)std::min<int64_t>((p.rows * 32 + 255) / 256, (int64_t)sm_count() * 16);
+    bool done;
+    if (x.dtype == C3B_F32)
+      done = out[0].dtype == C3B_F32
+                 ? launch_ln_vec<float, float>(x.ptr, rp, (const float*)sc.ptr, bp, out[0].ptr, p.rows, p.cols,
+                                               p.epsilon, s, gv)
+                 : launch_ln_vec<float, __nv_bfloat16>(x.ptr, rp, (const float*)sc.ptr, bp, out[0].ptr, p.rows,
+                                                       p.cols, p.epsilon, s, gv);
+    else
+      done = out[0].dtype == C3B_F32
+                 ? launch_ln_vec<__nv_bfloat16, float>(x.ptr, rp, (const float*)sc.ptr, bp, out[0].ptr, p.rows,
+                                                       p.cols, p.epsilon, s, gv)
+                 : launch_ln_vec<__nv_bfloat16, __nv_bfloat16>(x.ptr, rp, (const float*)sc.ptr, bp, out[0].ptr,
+                                                               p.rows, p.cols, p.epsilon, s, gv);
+    if (done) {
+      C3B_CHECK_CUDA(cudaGetLastError());
+      return C3B_OK;
+    }
+  }
+#define C3B_LN(PL)                                                                                   \
   layernorm_kernel<PL><<<g, 256, 0, s>>>(x.ptr, x.dtype, rp, rdt, (const float*)sc.ptr, bp, out[0].ptr, \
                                          out[0].dtype, sp, sdt, p.rows, (int)p.cols, p.epsilon)
   if (p.cols <= 32) C3B_LN(1);
@@ -681,6 +796,102 @@ int launch_stem_im2col(const c3b_tensor& in, const c3b_tensor& out, const c3b_st
   C3B_REQUIRE(numel(out) >= M * p.kpad, "stem im2col: output too small");
   if (M == 0) return C3B_OK;
   stem_im2col_kernel<<<grid_for(M, 128), 128, 0, s>>>((const float*)in.ptr, (__nv_bfloat16*)out.ptr, p);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+// ------------------------------------------------------------------ STEM CONV (direct)
+// Small-Cin convolution straight from the NCHW fp32 input to NHWC bf16 with
+// bias + activation: one thread per output pixel, all Cout (<= 64) channels in
+// registers, weights [K][Cout] fp32 in shared memory read as float4
+// broadcasts.  Replaces the patch matrix + GEMM pair for the ResNet stem
+// (K = 27 is too small for the tensor cores to pay for the 128-byte-per-pixel
+// patch matrix round trip through HBM).
+
+template <int COUT>
+__global__ void __launch_bounds__(256) stem_conv_kernel(const float* __restrict__ x, const float* __restrict__ wt,
+                                                        const float* __restrict__ bias,
+                                                        __nv_bfloat16* __restrict__ out, c3b_stem_params p, int act) {
+  // Two threads per output pixel, each owning half of the output channels
+  // (keeps the accumulators in registers at high occupancy).
+  constexpr int CH = COUT / 2;
+  extern __shared__ float sw[];  // [K][COUT] then bias[COUT]
+  const int K = p.g.kh * p.g.kw * p.c;
+  for (int i = threadIdx.x; i < K * COUT; i += blockDim.x) sw[i] = wt[i];
+  for (int i = threadIdx.x; i < COUT; i += blockDim.x) sw[K * COUT + i] = bias[i];
+  __syncthreads();
+  const int64_t M = (int64_t)p.n * p.ho * p.wo;
+  const int half = threadIdx.x & 1;
+  for (int64_t m = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 1; m < M;
+       m += ((int64_t)gridDim.x * blockDim.x) >> 1) {
+    const int ow = (int)(m % p.wo);
+    const int oh = (int)((m / p.wo) % p.ho);
+    const int n = (int)(m / ((int64_t)p.wo * p.ho));
+    float acc[CH];
+#pragma unroll
+    for (int o = 0; o < CH; ++o) acc[o] = sw[K * COUT + half * CH + o];
+    int k = 0;
+    for (int c = 0; c < p.c; ++c)
+      for (int r = 0; r < p.g.kh; ++r) {
+        const int ih = oh * p.g.sh - p.g.ph0 + r * p.g.dh;
+        for (int s = 0; s < p.g.kw; ++s, ++k) {
+          const int iw = ow * p.g.sw - p.g.pw0 + s * p.g.dw;
+          float v = 0.f;
+          if (ih >= 0 && ih < p.h && iw >= 0 && iw < p.w) v = __ldg(x + (((int64_t)n * p.c + c) * p.h + ih) * p.w + iw);
+          const float4* wr = reinterpret_cast<const float4*>(sw + k * COUT + half * CH);
+#pragma unroll
+          for (int o = 0; o < CH / 4; ++o) {
+            const float4 w4 = wr[o];
+            acc[4 * o] = fmaf(v, w4.x, acc[4 * o]);
+            acc[4 * o + 1] = fmaf(v, w4.y, acc[4 * o + 1]);
+            acc[4 * o + 2] = fmaf(v, w4.z, acc[4 * o + 2]);
+            acc[4 * o + 3] = fmaf(v, w4.w, acc[4 * o + 3]);
+          }
+        }
+      }
+    uint4* orow = reinterpret_cast<uint4*>(out + m * COUT + half * CH);
+#pragma unroll
+    for (int o = 0; o < CH / 8; ++o) {
+      __align__(16) __nv_bfloat16 b8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b8[j] = __float2bfloat16_rn(apply_act(acc[8 * o + j], act));
+      orow[o] = *reinterpret_cast<const uint4*>(b8);
+    }
+  }
+}
+
+bool launch_stem_mma(const c3b_tensor* in, const c3b_tensor& out, const c3b_stem_conv_params& p, cudaStream_t s);
+
+int launch_stem_conv(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_stem_conv_params& p,
+                     cudaStream_t s) {
+  // inputs: x NCHW f32, w [K][Cout] f32 with K ordered (c, r, s), bias f32 [Cout]
+  C3B_REQUIRE(n_in == 3, "stem conv: inputs x, w, bias");
+  const c3b_stem_params& g = p.geom;
+  const int K = g.g.kh * g.g.kw * g.c;
+  C3B_REQUIRE(in[0].dtype == C3B_F32 && in[1].dtype == C3B_F32 && in[2].dtype == C3B_F32, "stem conv: f32 inputs");
+  C3B_REQUIRE(out.dtype == C3B_BF16, "stem conv: bf16 NHWC output");
+  C3B_REQUIRE(p.cout == 64 || p.cout == 32 || p.cout == 16, "stem conv: Cout 16, 32 or 64");
+  C3B_REQUIRE(K <= 64, "stem conv: at most 64 taps x channels");
+  C3B_REQUIRE(numel(in[0]) == (int64_t)g.n * g.c * g.h * g.w, "stem conv: input extents");
+  C3B_REQUIRE(numel(in[1]) == (int64_t)K * p.cout && numel(in[2]) == p.cout, "stem conv: weight / bias extents");
+  const int64_t M = (int64_t)g.n * g.ho * g.wo;
+  C3B_REQUIRE(numel(out) >= M * p.cout, "stem conv: output too small");
+  C3B_REQUIRE((uintptr_t)out.ptr % 16 == 0, "stem conv: output alignment");
+  if (M == 0) return C3B_OK;
+  C3B_REQUIRE((uintptr_t)in[1].ptr % 16 == 0, "stem conv: weight alignment");
+  if (launch_stem_mma(in, out, p, s)) {  // tensor-core path (Cout 64, K <= 32)
+    C3B_CHECK_CUDA(cudaGetLastError());
+    return C3B_OK;
+  }
+  const size_t smem = (size_t)(K * p.cout + p.cout) * sizeof(float);
+  const int grid = (int)std::min<int64_t>((2 * M + 255) / 256, (int64_t)sm_count() * 8);
+#define C3B_STEM(CO) \
+  stem_conv_kernel<CO><<<grid, 256, smem, s>>>((const float*)in[0].ptr, (const float*)in[1].ptr, \
+                                               (const float*)in[2].ptr, (__nv_bfloat16*)out.ptr, g, p.act)
+  if (p.cout == 64) C3B_STEM(64);
+  else if (p.cout == 32) C3B_STEM(32);
+  else C3B_STEM(16);
+#undef C3B_STEM
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }

@@ -29,6 +29,7 @@ stream and fp32 LayerNorm statistics for transformers, fp32 logits.
 from __future__ import annotations
 
 import math
+import os
 from typing import Dict, List, Optional, Tuple
 
 import numpy as np
@@ -422,8 +423,22 @@ def _emit(st: _State, op: dict) -> None:
                 return [Launch(L.K_CONV, ins, [d[out].t()], cp)]
             P.add_step("conv_f32", [x, wname, bname] + ([res] if res else []), [out], build, flops)
             st.layout[out] = "nchw"
+        elif C % 64 != 0 and C * kh * kw <= 64 and O in (16, 32, 64) and not res and lay == "nchw":
+            # stem: direct conv from the NCHW f32 input to NHWC bf16 (K = C*kh*kw is tiny)
+            wk = np.ascontiguousarray(w.reshape(O, -1).T, np.float32)  # [K (c,r,s)][Cout]
+            wname = st.weight("stem", wk, L.F32)
+            P.add_tensor(out, (N * Ho * Wo, O), L.BF16)
+            sp = L.StemParams()
+            sp.n, sp.c, sp.h, sp.w, sp.ho, sp.wo, sp.kpad = N, C, H, W, Ho, Wo, 0
+            sp.g = geo
+            scp = L.StemConvParams(sp, O, op["act"])
+
+            def bst(d, x=x, wname=wname, bname=bname, out=out, scp=scp):
+                return [Launch(L.K_STEM_CONV, [d[x].t(), d[wname].t(), d[bname].t()], [d[out].t()], scp)]
+            P.add_step("stem_conv", [x, wname, bname], [out], bst, flops)
+            st.layout[out] = "nhwc"
         elif C % 64 != 0:
-            # stem: patch matrix (K ordered r,s,c; padded to 64) + tcgen05 GEMM
+            # small-Cin conv: patch matrix (K ordered r,s,c; padded to 64) + tcgen05 GEMM
             if lay != "nchw" or res:
                 raise RuntimeError("bf16 stem conv expects the NCHW f32 graph input and no residual")
             kpad = (C * kh * kw + 63) // 64 * 64
@@ -456,6 +471,8 @@ def _emit(st: _State, op: dict) -> None:
             cp.n, cp.h, cp.w, cp.cin, cp.cout, cp.ho, cp.wo = N, H, W, C, O, Ho, Wo
             cp.k, cp.stride, cp.pad = kh, geo.sh, geo.ph0
             cp.has_residual, cp.act, cp.block_n = int(res is not None), op["act"], 0
+            # C3B200_CONV_MODE=1 forces one TMA window per tap (A/B comparisons)
+            cp.mode = int(os.environ.get("C3B200_CONV_MODE", "0"))
 
             def build(d, x=x, wname=wname, bname=bname, res=res, out=out, cp=cp):
                 ins = [d[x].t(), d[wname].t(), d[bname].t()] + ([d[res].t()] if res else [])
@@ -538,7 +555,7 @@ def _emit(st: _State, op: dict) -> None:
         res = st.t(op["res"]) if op["res"] else None
         out = op["out"]
         flops = 2.0 * M * N * K
-        use_tc = bf and N % 16 == 0 and K % 64 == 0 and P.tensors[x].dtype == L.BF16
+        use_tc = bf and N % 32 == 0 and K % 64 == 0 and P.tensors[x].dtype == L.BF16
         bname = st.weight("bias", (op["b"] * op.get("beta", 1.0)).astype(np.float32), L.F32) \
             if op["b"] is not None else None
         if use_tc:

@@ -84,7 +84,8 @@ enum {
   C3B_K_EMBED = 14,      /* token-row gather + position add               */
   C3B_K_STEM_IM2COL = 15,/* NCHW f32 -> bf16 [N*Ho*Wo, Kpad] patch matrix */
   C3B_K_GAP_NHWC = 16,   /* NHWC mean over H,W -> [N, C]                  */
-  C3B_K_COUNT = 17
+  C3B_K_STEM_CONV = 17,  /* direct small-Cin conv NCHW f32 -> NHWC bf16    */
+  C3B_K_COUNT = 18
 };
 
 /* --- C3B_K_EW: out = program(in0..in5) with NumPy broadcasting.
@@ -186,7 +187,7 @@ typedef struct {
 /* --- C3B_K_GEMM_TC: bf16 x bf16 -> fp32 accumulate in TMEM.
  * A [M,K] bf16 row-major, B [N,K] bf16 row-major (i.e. both K-major).
  * inputs: A, B, [bias f32 [N]], [residual [M,N] f32|bf16] ; output C [M,N] f32|bf16.
- * K % 64 == 0, N % 16 == 0; M arbitrary. */
+ * K % 8 == 0, N % 32 == 0; M arbitrary. */
 typedef struct {
   int64_t M, N, K;
   int32_t bias_mode, act, has_residual, block_n;
@@ -195,11 +196,12 @@ typedef struct {
 /* --- C3B_K_CONV_TC: NHWC bf16 implicit GEMM, K ordered (kh, kw, Cin).
  * inputs: x [N,H,W,Cin] bf16, w [Cout, kh, kw, Cin] bf16, bias f32 [Cout],
  * [residual [N,Ho,Wo,Cout] bf16] ; output y [N,Ho,Wo,Cout] bf16.
- * Cin % 64 == 0, Cout % 16 == 0, stride 1 or 2 (H, W even for stride 2),
+ * Cin % 64 == 0, Cout % 32 == 0, stride 1 or 2 (H, W even for stride 2),
  * square kernel, symmetric padding. */
 typedef struct {
   int32_t n, h, w, cin, cout, ho, wo, k, stride, pad;
-  int32_t has_residual, act, block_n, _pad;
+  int32_t has_residual, act, block_n;
+  int32_t mode; /* 0: halo tiles where eligible (3x3 s1 p1, Cout <= 128), 1: one TMA window per tap */
 } c3b_conv_tc_params;
 
 /* --- C3B_K_FLASH_ATTN: qkv [B, S, 3, H, D] (f32 or bf16) -> out [B, S, H*D].
@@ -222,6 +224,14 @@ typedef struct {
   c3b_conv_geom g;
   int32_t _pad2[2];
 } c3b_stem_params;
+
+/* --- C3B_K_STEM_CONV: inputs x NCHW f32, w [K][Cout] f32 (K ordered c, kh, kw;
+ * K <= 64), bias f32 [Cout]; output [N*Ho*Wo, Cout] bf16 = act(conv + bias).
+ * Cout in {16, 32, 64}. */
+typedef struct {
+  c3b_stem_params geom;
+  int32_t cout, act;
+} c3b_stem_conv_params;
 
 /* --- C3B_K_GAP_NHWC: x [N, HW, C] -> y [N, C] f32 */
 typedef struct {

@@ -296,10 +296,14 @@ def test_gemm_tc(torch_cuda, M, N, K, act, res):
     assert rel(host(out), ref) < 2e-5
 
 
+@pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("n,h,cin,cout,k,stride,res", [(2, 32, 64, 64, 3, 1, 0), (3, 16, 64, 128, 3, 2, 0),
                                                        (4, 16, 128, 128, 3, 1, 1), (8, 8, 128, 256, 1, 2, 0),
-                                                       (10, 4, 256, 512, 3, 1, 1), (16, 8, 256, 512, 3, 2, 0)])
-def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res):
+                                                       (10, 4, 256, 512, 3, 1, 1), (16, 8, 256, 512, 3, 2, 0),
+                                                       (9, 32, 64, 64, 3, 1, 1), (3, 8, 64, 128, 3, 1, 1),
+                                                       (5, 4, 128, 64, 3, 1, 0), (33, 16, 128, 128, 3, 1, 0)])
+def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res, mode):
+    """mode 0 uses halo tiles where eligible (3x3 s1, Cout <= 128), mode 1 one TMA window per tap."""
     import torch
     from hackathon_b200 import _lib as L
     pad = k // 2
@@ -317,7 +321,7 @@ def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res):
     out = torch.empty((n, ho, ho, cout), dtype=torch.bfloat16, device="cuda")
     cp = L.ConvTcParams()
     cp.n, cp.h, cp.w, cp.cin, cp.cout, cp.ho, cp.wo, cp.k, cp.stride, cp.pad = n, h, h, cin, cout, ho, ho, k, stride, pad
-    cp.has_residual, cp.act, cp.block_n = res, 1 if res else 0, 0
+    cp.has_residual, cp.act, cp.block_n, cp.mode = res, 1 if res else 0, 0, mode
     ins = [L.make_tensor(xn.data_ptr(), L.BF16, (n, h, h, cin)), L.make_tensor(wn.data_ptr(), L.BF16, (cout, k, k, cin)),
            L.make_tensor(tb.data_ptr(), L.F32, (cout,))]
     if res:
@@ -352,3 +356,39 @@ def test_flash_attention(torch_cuda, dt, B, S, H):
     torch.cuda.synchronize()
     got = out.float().cpu().numpy()
     assert rel(got, ref) < (RTOL if dt == "f32" else 2e-2)
+
+
+@pytest.mark.parametrize("n,cout,act", [(3, 64, 1), (2, 32, 0), (1, 16, 1)])
+def test_stem_conv_direct(torch_cuda, n, cout, act):
+    """Direct small-Cin conv (NCHW f32 -> NHWC bf16) against the oracle conv."""
+    import torch
+    from hackathon_b200 import _lib as L
+    x, w, b = randn(n, 3, 32, 32), randn(cout, 3, 3, 3) * 0.3, randn(cout)
+    ref = O.conv2d(x, w, b, strides=[1, 1], pads=[1, 1, 1, 1])
+    if act:
+        ref = np.maximum(ref, 0)
+    wk = np.ascontiguousarray(w.reshape(cout, -1).T)
+    tx, tw, tb = dev(torch, x), dev(torch, wk), dev(torch, b)
+    out = torch.empty((n * 1024, cout), dtype=torch.bfloat16, device="cuda")
+    sp = L.StemParams()
+    sp.n, sp.c, sp.h, sp.w, sp.ho, sp.wo, sp.kpad = n, 3, 32, 32, 32, 32, 0
+    sp.g = L.ConvGeom(3, 3, 1, 1, 1, 1, 1, 1, 1, 1)
+    L.launch(L.K_STEM_CONV, [L.make_tensor(tx.data_ptr(), L.F32, x.shape), L.make_tensor(tw.data_ptr(), L.F32, wk.shape),
+                             L.make_tensor(tb.data_ptr(), L.F32, b.shape)],
+             [L.make_tensor(out.data_ptr(), L.BF16, (n * 1024, cout))], L.StemConvParams(sp, cout, act),
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy().reshape(n, 32, 32, cout).transpose(0, 3, 1, 2)
+    assert rel(got, ref) < 8e-3
+
+
+def test_skinny_gemm(torch_cuda):
+    """N <= 32 GEMMs take the warp-per-row path."""
+    t = torch_cuda
+    a, w, b = randn(300, 512), randn(10, 512), randn(10)
+    outs = call("fused_gemm_epilogue_f32", [dev(t, a), dev(t, w), dev(t, b)], [arena(t, 3000)],
+                {"transB": 1, "_activation": "Relu"})
+    assert rel(host(outs[0]), O.gemm_epilogue(a, w, b, transB=1, relu=True)) < RTOL
+    w2 = randn(512, 7)
+    outs = call("fused_gemm_epilogue_f32", [dev(t, a), dev(t, w2)], [arena(t, 2100)], {"alpha": 0.5})
+    assert rel(host(outs[0]), O.gemm_epilogue(a, w2, None, alpha=0.5)) < RTOL
