@@ -15,9 +15,9 @@ namespace c3b {
 
 namespace fam {
 constexpr int D = 64;
-constexpr int QB = 64;
+constexpr int QB = 128;
 constexpr int KB = 64;
-constexpr int NT = 128;
+constexpr int NT = 256;
 }  // namespace fam
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -93,9 +93,9 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
   }
 
   auto load_kv = [&](int buf, int k0) {
-    // 64 rows x 8 chunks for K and for V: 1024 chunks, 8 per thread.
+    // 64 rows x 8 chunks for K and for V: 1024 chunks over the block.
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 1024 / NT; ++i) {
       const int e = tid + i * NT;
       const int which = e >> 9;  // 0: K, 1: V
       const int r = (e >> 3) & 63, c = e & 7;
@@ -114,7 +114,9 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const int row0 = qb * QB + warp * 16 + g, row1 = row0 + 8;
 
-  const int ntiles = p.causal ? qb + 1 : (p.seq + KB - 1) / KB;
+  const int kv_tiles = (p.seq + KB - 1) / KB;
+  const int ntiles = p.causal ? min(kv_tiles, ((qb + 1) * QB + KB - 1) / KB) : kv_tiles;
+  const int warp_last_row = qb * QB + warp * 16 + 15;
   load_kv(0, 0);
   for (int kt = 0; kt < ntiles; ++kt) {
     const int buf = kt & 1;
@@ -125,6 +127,7 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
       cp_wait<0>();
     }
     __syncthreads();
+    if (!(p.causal && warp_last_row < kt * KB)) {
     const uint32_t kbase = su32(Ks[buf]), vbase = su32(Vs[buf]);
     // S = Q K^T : 16 x 64 per warp, 8 n-blocks of 8 keys.
     float s[8][4];
@@ -206,6 +209,7 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
         mma16816(o[nb + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], b2, b3);
       }
     }
+    }  // rows of this warp see at least one key of the tile
     __syncthreads();
   }
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
