@@ -217,15 +217,8 @@ def main():
 
     key, gbatch, profile, unit, scaling, ups, note = WORKLOADS[args.workload]
     g = BUILDERS[key]()
-    if scaling == "weak":
-        per = gbatch
-        total = gbatch * ws
-        start = rank * per
-    else:
-        total = gbatch
-        base, extra = divmod(total, ws)
-        per = base + (1 if rank < extra else 0)
-        start = rank * base + min(rank, extra)
+    from hackathon_b200.dist import rows_for
+    total, start, per = rows_for(scaling, gbatch, ws, rank)
     if args.per_gpu_batch:
         per, total, start = args.per_gpu_batch, args.per_gpu_batch * ws, rank * args.per_gpu_batch
     feeds_all = make_inputs(g, total) if (scaling == "strong" or ws == 1) else None

@@ -15,9 +15,9 @@ namespace c3b {
 
 namespace fam {
 constexpr int D = 64;
-constexpr int QB = 128;
+constexpr int QB = 64;
 constexpr int KB = 64;
-constexpr int NT = 256;
+constexpr int NT = 128;
 }  // namespace fam
 
 __device__ __forceinline__ uint32_t su32(const void* p) {

@@ -60,6 +60,7 @@ struct TcArgs {
   int cin;
   // halo mode (3x3 stride-1 convolution, tc_conv_halo_kernel)
   int img, wt, wblocks, ho, n_img, rows, halo_bytes, hstages;
+  int bres;  // 1: all weight taps resident in shared memory for the whole kernel
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -568,6 +569,13 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
     if (lane == 0) {
       int hs = 0, bs = 0;
       uint32_t hph = 0, bph = 0;
+      if (a.bres) {
+        // every (cin block, tap) weight tile once, into its own slot
+        const int nk = 9 * a.cblocks;
+        mbar_arrive_tx(&bfull[0], (uint32_t)nk * b_bytes);
+        for (int kb = 0; kb < nk; ++kb)
+          tma_load_2d(sb + (size_t)kb * b_bytes, &maps.b, &bfull[0], (kb % 9) * a.cin + (kb / 9) * BK, 0);
+      }
       for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
         const int nb = t % a.n_tiles_n;
         int pt = t / a.n_tiles_n;
@@ -581,7 +589,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
           mbar_arrive_tx(&hfull[hs], (uint32_t)a.halo_bytes);
           tma_load_4d(sh + (size_t)hs * hbytes_al, &maps.a[0], &hfull[hs], cb * BK, n0, w0 - 1, h0 - 1);
           if (++hs == hst) { hs = 0; hph ^= 1; }
-          for (int tap = 0; tap < 9; ++tap) {
+          for (int tap = 0; tap < 9 && !a.bres; ++tap) {
             if (!mbar_wait(&bempty[bs], bph ^ 1, abort_flag, 22)) goto producer_done;
             mbar_arrive_tx(&bfull[bs], b_bytes);
             tma_load_2d(sb + (size_t)bs * b_bytes, &maps.b, &bfull[bs], tap * a.cin + cb * BK, nb * a.block_n);
@@ -596,7 +604,12 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
       const uint32_t idesc = instr_desc(BM, a.block_n);
       int hs = 0, bs = 0, acc = 0;
       uint32_t hph = 0, bph = 0, acc_phase = 0;
-      for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+      bool bres_ok = true;
+      if (a.bres) {
+        bres_ok = mbar_wait(&bfull[0], 0, abort_flag, 27);
+        tc_fence_after();
+      }
+      for (int t = blockIdx.x; t < a.n_tiles && bres_ok; t += gridDim.x) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 23)) break;
         tc_fence_after();
         const uint32_t d0 = tmem_base + (uint32_t)(acc * R * a.block_n);
@@ -606,10 +619,12 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
           tc_fence_after();
           const uint32_t hbase = smem_u32(sh + (size_t)hs * hbytes_al);
           for (int tap = 0; tap < 9; ++tap) {
-            if (!mbar_wait(&bfull[bs], bph, abort_flag, 25)) { ok = false; break; }
-            tc_fence_after();
+            if (!a.bres) {
+              if (!mbar_wait(&bfull[bs], bph, abort_flag, 25)) { ok = false; break; }
+              tc_fence_after();
+            }
             const int r = tap / 3, s = tap % 3;
-            const uint32_t b_addr = smem_u32(sb + (size_t)bs * b_bytes);
+            const uint32_t b_addr = smem_u32(sb + (size_t)(a.bres ? cb * 9 + tap : bs) * b_bytes);
             for (int j = 0; j < R; ++j) {
               const uint32_t a_addr = hbase + (uint32_t)(((j + r) * WT2 + s) * a.img) * 128u;
 #pragma unroll
@@ -617,8 +632,10 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
                 mma_bf16(d0 + (uint32_t)(j * a.block_n), smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32),
                          idesc, (cb > 0 || tap > 0 || k > 0) ? 1u : 0u);
             }
-            mma_commit(&bempty[bs]);
-            if (++bs == bst) { bs = 0; bph ^= 1; }
+            if (!a.bres) {
+              mma_commit(&bempty[bs]);
+              if (++bs == bst) { bs = 0; bph ^= 1; }
+            }
           }
           if (!ok) break;
           mma_commit(&hempty[hs]);
@@ -899,8 +916,14 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
     a.hstages = 2;
     const size_t budget = 212 * 1024;
     if (2 * hb + 2 * bb > budget) return fail(C3B_E_INVALID, "tc conv: halo tiles do not fit in shared memory");
-    int bst = (int)((budget - 2 * hb) / bb);
-    a.stages = bst > 8 ? 8 : bst;
+    const size_t all_b = (size_t)9 * a.cblocks * bb;
+    if (2 * hb + all_b <= budget && p.mode != 2) {
+      a.bres = 1;  // weights stay resident: one load per CTA
+      a.stages = 9 * a.cblocks;
+    } else {
+      int bst = (int)((budget - 2 * hb) / bb);
+      a.stages = bst > 8 ? 8 : bst;
+    }
     const size_t smem = 1024 + 2 * hb + a.stages * bb + (2 * 2 + 2 * a.stages + 4) * 8 + 16;
     static bool attr_halo = false;
     if (!attr_halo) {

@@ -296,7 +296,7 @@ def test_gemm_tc(torch_cuda, M, N, K, act, res):
     assert rel(host(out), ref) < 2e-5
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("n,h,cin,cout,k,stride,res", [(2, 32, 64, 64, 3, 1, 0), (3, 16, 64, 128, 3, 2, 0),
                                                        (4, 16, 128, 128, 3, 1, 1), (8, 8, 128, 256, 1, 2, 0),
                                                        (10, 4, 256, 512, 3, 1, 1), (16, 8, 256, 512, 3, 2, 0),
