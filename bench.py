@@ -97,9 +97,21 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def all_host_threads() -> int:
+    """Let NumPy's BLAS use every host core (torchrun defaults OMP_NUM_THREADS to 1)."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(n)
+    except Exception:
+        pass
+    return n
+
+
 def cpu_baseline(model_key, g, feeds_global, unit, units_per_sample, steps=1):
     """The oracle (NumPy restatement of the reference's own engine ops) on a
     bounded sample, on all host cores."""
+    all_host_threads()
     from oracle.evaluate import run_graph
     n = CPU_SAMPLE[model_key]
     sample = {k: v[:n] for k, v in feeds_global.items()}
@@ -161,6 +173,7 @@ def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    all_host_threads()
     from hackathon_b200.workloads import BUILDERS, make_inputs
     key, gbatch, profile, unit, scaling, ups, note = WORKLOADS[args.workload]
     g = BUILDERS[key]()

@@ -61,6 +61,8 @@ struct TcArgs {
   // halo mode (3x3 stride-1 convolution, tc_conv_halo_kernel)
   int img, wt, wblocks, ho, n_img, rows, halo_bytes, hstages;
   int bres;  // 1: all weight taps resident in shared memory for the whole kernel
+  // row-ring mode (tc_conv_rowring_kernel)
+  int segs, seg_rows, ring, row_bytes, n_items;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -723,6 +725,190 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
   }
 }
 
+// 3x3 stride-1 convolution, Cin = 64 (one channel block), weights resident:
+// row-ring variant of the halo kernel.  Work items are column strips of one
+// image group (IMG images x WT output columns) split into segments of
+// `seg_rows` output rows; a CTA walks a segment top to bottom two output rows
+// at a time.  Input rows (IMG x (WT+2) pixels x 64 channels = one 128-byte
+// swizzled row per pixel) live in a ring of `ring` shared-memory slots, so each
+// input row is loaded once per segment instead of once per output row pair;
+// every tap window of an MMA lies inside one slot (start (s*IMG) rows, a
+// multiple of 8).
+__global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const __grid_constant__ TmaMaps maps,
+                                                                         const TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int NS = a.ring;
+  const uint32_t rb_al = (uint32_t)((a.row_bytes + 1023) & ~1023);
+  const uint32_t b_bytes = (uint32_t)a.block_n * BK * 2;
+  uint8_t* sr = smem;
+  uint8_t* sb = smem + (size_t)NS * rb_al;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + (size_t)9 * b_bytes);
+  uint64_t* rfull = bars;
+  uint64_t* rempty = rfull + NS;
+  uint64_t* wfull = rempty + NS;
+  uint64_t* tfull = wfull + 1;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t tmem_cols = (uint32_t)(a.block_n * 4);  // 2 rows x 2 buffers
+  const int SR = a.seg_rows;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&rfull[i], 1);
+      mbar_init(&rempty[i], 1);
+    }
+    mbar_init(&wfull[0], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a[0])));
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)));
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_tx(&wfull[0], 9u * b_bytes);
+      for (int tap = 0; tap < 9; ++tap)
+        tma_load_2d(sb + (size_t)tap * b_bytes, &maps.b, &wfull[0], tap * a.cin, 0);
+      uint32_t c = 0;  // rows loaded so far
+      for (int u = blockIdx.x; u < a.n_items; u += gridDim.x) {
+        const int seg = u % a.segs;
+        const int strip = u / a.segs;
+        const int wb = strip % a.wblocks, ib = strip / a.wblocks;
+        const int h0 = seg * SR;
+        for (int ir = 0; ir < SR + 2; ++ir, ++c) {
+          const int slot = (int)(c % NS);
+          if (!mbar_wait(&rempty[slot], ((c / NS) & 1) ^ 1, abort_flag, 31)) goto producer_done;
+          mbar_arrive_tx(&rfull[slot], (uint32_t)a.row_bytes);
+          tma_load_4d(sr + (size_t)slot * rb_al, &maps.a[0], &rfull[slot], 0, ib * a.img, wb * a.wt - 1,
+                      h0 - 1 + ir);
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc(BM, a.block_n);
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      uint32_t cbase = 0;
+      bool ok = mbar_wait(&wfull[0], 0, abort_flag, 32);
+      tc_fence_after();
+      for (int u = blockIdx.x; u < a.n_items && ok; u += gridDim.x) {
+        for (int pr = 0; pr < SR / 2 && ok; ++pr) {
+          // input rows 2pr .. 2pr+3 of this segment; the first pair waits for
+          // all four, later pairs for the two new ones
+          for (int ir = (pr == 0 ? 0 : 2 * pr + 2); ir <= 2 * pr + 3; ++ir) {
+            const uint32_t c = cbase + ir;
+            if (!mbar_wait(&rfull[c % NS], (c / NS) & 1, abort_flag, 33)) { ok = false; break; }
+          }
+          if (!ok) break;
+          tc_fence_after();
+          if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 34)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d0 = tmem_base + (uint32_t)(acc * 2 * a.block_n);
+          for (int tap = 0; tap < 9; ++tap) {
+            const int r = tap / 3, s = tap % 3;
+            const uint32_t b_addr = smem_u32(sb + (size_t)tap * b_bytes);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint32_t c = cbase + 2 * pr + j + r;
+              const uint32_t a_addr = smem_u32(sr + (size_t)(c % NS) * rb_al) + (uint32_t)(s * a.img) * 128u;
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                mma_bf16(d0 + (uint32_t)(j * a.block_n), smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32),
+                         idesc, (tap > 0 || k > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(&tfull[acc]);
+          if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+          // rows 2pr and 2pr+1 are no longer needed (all rows at segment end)
+          const int rel_end = (pr == SR / 2 - 1) ? SR + 2 : 2 * pr + 2;
+          for (int ir = 2 * pr; ir < rel_end; ++ir) mma_commit(&rempty[(cbase + ir) % NS]);
+        }
+        cbase += SR + 2;
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int cols = a.block_n >> 1;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool run = true;
+    for (int u = blockIdx.x; u < a.n_items && run; u += gridDim.x) {
+      const int seg = u % a.segs;
+      const int strip = u / a.segs;
+      const int wb = strip % a.wblocks, ib = strip / a.wblocks;
+      const int m = q * 32 + lane;
+      const int img = ib * a.img + (m % a.img);
+      const int w = wb * a.wt + m / a.img;
+      const bool img_ok = img < a.n_img;
+      const int64_t col_base = half * cols;
+      for (int pr = 0; pr < SR / 2; ++pr) {
+        const int hrow = seg * SR + 2 * pr;
+        uint4 rv[2][4];
+        if (a.res && img_ok) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int64_t pix = ((int64_t)img * a.ho + hrow + j) * a.wo + w;
+            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) +
+                                                             pix * a.N + col_base);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) rv[j][i] = rp[i];
+          }
+        }
+        const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 35);
+        if (!__all_sync(0xffffffffu, ok)) { run = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int64_t pix = ((int64_t)img * a.ho + hrow + j) * a.wo + w;
+          const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) +
+                              (uint32_t)((acc * 2 + j) * a.block_n + half * cols);
+          float v[32];
+          tmem_ld32(tb, v);
+          if (img_ok) store32_bf16(a, pix * a.N + col_base, col_base, v, a.res ? rv[j] : nullptr);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+  }
+}
+
 }  // namespace tc
 
 // ------------------------------------------------------------------ host side
@@ -897,13 +1083,48 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   // Halo mode: 3x3, stride 1, pad 1, Cout <= 128 (one weight tile), two output
   // rows per super-tile.
   const int wt = p.wo < 16 ? p.wo : 16;
-  if (p.mode == 0 && p.k == 3 && p.stride == 1 && p.pad == 1 && p.cout <= 128 && a.n_tiles_n == 1 &&
+  if (p.mode != 1 && p.k == 3 && p.stride == 1 && p.pad == 1 && p.cout <= 128 && a.n_tiles_n == 1 &&
       p.wo % wt == 0 && 128 % wt == 0 && (128 / wt) >= 8 && p.ho % 2 == 0) {
     a.img = 128 / wt;
     a.wt = wt;
     a.wblocks = p.wo / wt;
     a.ho = p.ho;
     a.n_img = p.n;
+    if ((p.mode == 0) && p.cin == 64 && p.cout == 64 && a.block_n == 64) {
+      // row ring: strips of IMG images x WT columns, segments of seg_rows rows
+      const int strips = ((p.n + a.img - 1) / a.img) * a.wblocks;
+      int segs = 1;
+      while (strips * segs < 8 * sm_count() && segs * 2 <= p.ho / 2) segs *= 2;
+      if (p.ho % (2 * segs) == 0) {
+        a.segs = segs;
+        a.seg_rows = p.ho / segs;
+        a.n_items = strips * segs;
+        a.row_bytes = 64 * a.img * (wt + 2) * 2;
+        const size_t rb = ((size_t)a.row_bytes + 1023) & ~(size_t)1023;
+        const size_t wbytes = (size_t)9 * 64 * tc::BK * 2;
+        const size_t budget = 212 * 1024;
+        int ring = (int)((budget - wbytes) / rb);
+        if (ring > 8) ring = 8;
+        if (ring >= 5) {
+          a.ring = ring;
+          uint64_t dims[4] = {C, (uint64_t)p.n, (uint64_t)p.w, (uint64_t)p.h};
+          uint64_t str[3] = {(uint64_t)p.h * p.w * C * 2, C * 2, (uint64_t)p.w * C * 2};
+          uint32_t box[4] = {64, (uint32_t)a.img, (uint32_t)(wt + 2), 1};
+          if ((rc = encode(&maps.a[0], x, 4, dims, str, box))) return rc;
+          const size_t smem = 1024 + ring * rb + wbytes + (2 * ring + 5) * 8 + 16;
+          static bool attr_ring = false;
+          if (!attr_ring) {
+            C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_conv_rowring_kernel,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+            attr_ring = true;
+          }
+          int grid = a.n_items < sm_count() ? a.n_items : sm_count();
+          tc::tc_conv_rowring_kernel<<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
+          C3B_CHECK_CUDA(cudaGetLastError());
+          return C3B_OK;
+        }
+      }
+    }
     a.rows = 2;
     a.halo_bytes = 64 * a.img * (wt + 2) * (a.rows + 2) * 2;
     a.n_tiles = ((p.n + a.img - 1) / a.img) * (p.ho / a.rows) * a.wblocks;

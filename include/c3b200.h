@@ -201,9 +201,10 @@ typedef struct {
 typedef struct {
   int32_t n, h, w, cin, cout, ho, wo, k, stride, pad;
   int32_t has_residual, act, block_n;
-  int32_t mode; /* 0: halo tiles where eligible (3x3 s1 p1, Cout <= 128), weights resident in
-                   shared memory when they fit; 1: one TMA window per tap; 2: halo tiles with
-                   streamed weights */
+  int32_t mode; /* 0: fastest eligible path: row-ring halo (3x3 s1 p1, Cin = Cout = 64), halo
+                   tiles (3x3 s1 p1, Cout <= 128, weights resident when they fit), else one TMA
+                   window per tap; 1: one TMA window per tap; 2: halo tiles, streamed weights;
+                   3: halo tiles, resident weights, no row ring */
 } c3b_conv_tc_params;
 
 /* --- C3B_K_FLASH_ATTN: qkv [B, S, 3, H, D] (f32 or bf16) -> out [B, S, H*D].

@@ -296,12 +296,13 @@ def test_gemm_tc(torch_cuda, M, N, K, act, res):
     assert rel(host(out), ref) < 2e-5
 
 
-@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
 @pytest.mark.parametrize("n,h,cin,cout,k,stride,res", [(2, 32, 64, 64, 3, 1, 0), (3, 16, 64, 128, 3, 2, 0),
                                                        (4, 16, 128, 128, 3, 1, 1), (8, 8, 128, 256, 1, 2, 0),
                                                        (10, 4, 256, 512, 3, 1, 1), (16, 8, 256, 512, 3, 2, 0),
                                                        (9, 32, 64, 64, 3, 1, 1), (3, 8, 64, 128, 3, 1, 1),
-                                                       (5, 4, 128, 64, 3, 1, 0), (33, 16, 128, 128, 3, 1, 0)])
+                                                       (5, 4, 128, 64, 3, 1, 0), (33, 16, 128, 128, 3, 1, 0),
+                                                       (17, 32, 64, 64, 3, 1, 1), (40, 16, 64, 64, 3, 1, 0)])
 def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res, mode):
     """mode 0 uses halo tiles where eligible (3x3 s1, Cout <= 128), mode 1 one TMA window per tap."""
     import torch
