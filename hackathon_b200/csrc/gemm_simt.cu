@@ -200,6 +200,36 @@ __global__ void __launch_bounds__(256) skinny_gemm_kernel(AL A, BL B, Epi E, int
   }
 }
 
+// fp32 A [M,K] x B [N,K]^T for N <= 16 (classifier heads): one warp per row,
+// 16-byte loads along K, all N dot products accumulated per lane.
+__global__ void __launch_bounds__(256) skinny_f32_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                         Epi E, int64_t M, int N, int64_t K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < M; m += nw) {
+    float acc[16];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) acc[n] = 0.f;
+    const float4* ar = reinterpret_cast<const float4*>(A + m * K);
+    for (int64_t k4 = lane; k4 < K / 4; k4 += 32) {
+      const float4 av = __ldg(ar + k4);
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        if (n < N) {
+          const float4 bv = __ldg(reinterpret_cast<const float4*>(B + (int64_t)n * K) + k4);
+          acc[n] = fmaf(av.x, bv.x, fmaf(av.y, bv.y, fmaf(av.z, bv.z, fmaf(av.w, bv.w, acc[n]))));
+        }
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      if (n >= N) break;
+      const float v = warp_sum(acc[n]);
+      if (lane == 0) E.put(0, m, n, v);
+    }
+  }
+}
+
 int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_params& p,
                      cudaStream_t s) {
   const int need = 2 + (p.bias_mode != C3B_BIAS_NONE) + (p.has_residual ? 1 : 0);
@@ -233,6 +263,13 @@ int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, cons
   if (p.M == 0 || p.N == 0) return C3B_OK;
   MatLoad al{a.ptr, a.dtype, p.M, p.K, p.stride_a, p.trans_a != 0};
   MatLoad bl{b.ptr, b.dtype, p.N, p.K, p.stride_b, p.trans_b == 0};
+  if (p.N <= 16 && p.K % 4 == 0 && p.batch == 1 && !p.trans_a && p.trans_b && a.dtype == C3B_F32 &&
+      b.dtype == C3B_F32 && ((uintptr_t)a.ptr % 16 == 0) && ((uintptr_t)b.ptr % 16 == 0)) {
+    const int blocks = (int)std::min<int64_t>((p.M * 32 + 255) / 256, (int64_t)sm_count() * 16);
+    skinny_f32_kernel<<<blocks, 256, 0, s>>>((const float*)a.ptr, (const float*)b.ptr, e, p.M, (int)p.N, p.K);
+    C3B_CHECK_CUDA(cudaGetLastError());
+    return C3B_OK;
+  }
   if (p.N <= 32 && p.K >= 64) {
     const int blocks = (int)std::min<int64_t>((p.M * 32 + 255) / 256, (int64_t)sm_count() * 8);
     dim3 g2((unsigned)blocks, 1, (unsigned)p.batch);
