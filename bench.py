@@ -311,7 +311,11 @@ def main():
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
-        traffic = json.load(open(tpath)).get(f"{args.workload}:{top}")
+        rec = json.load(open(tpath)).get(f"{args.workload}:{top}")
+        if rec and per == 4096:
+            # DRAM bytes of the kernel family over one pass (all its launches),
+            # the same unit as `achieved` (family FLOPs / family time)
+            traffic = rec["bytes_per_step"]
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if peak else None, "traffic": traffic,
                 "kernel": top, "launches_per_step": launches_top,

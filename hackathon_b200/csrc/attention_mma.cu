@@ -50,6 +50,28 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// 2^x for x <= 0 on the FMA/ALU pipes: Cody-Waite split x = n + f with
+// f in [-0.5, 0.5] (round-to-nearest through the 1.5*2^23 shifter), Taylor
+// polynomial of 2^f = e^(f ln 2) to degree 5 (relative error < 4e-6 in fp32
+// arithmetic, far below the bf16 rounding the result goes through), and 2^n applied
+// by adding n to the exponent field.  Inputs below -126 flush to 0.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.0f);
+  const float shifter = 12582912.0f;  // 1.5 * 2^23
+  const float t = x + shifter;
+  const float n = t - shifter;
+  const float f = x - n;
+  float p = 1.3333558146428443e-3f;        // ln2^5 / 5!
+  p = fmaf(p, f, 9.6181291076284772e-3f);  // ln2^4 / 4!
+  p = fmaf(p, f, 5.5504108664821580e-2f);  // ln2^3 / 3!
+  p = fmaf(p, f, 2.4022650695910071e-1f);  // ln2^2 / 2!
+  p = fmaf(p, f, 6.9314718055994531e-1f);  // ln2
+  p = fmaf(p, f, 1.0f);
+  const int ni = __float_as_int(t) - 0x4B400000;
+  const float r = __int_as_float(__float_as_int(p) + (ni << 23));
+  return x > -126.0f ? r : 0.0f;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -178,10 +200,22 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
     uint32_t pa[4][4];
 #pragma unroll
     for (int nb = 0; nb < 8; ++nb) {
-      const float p00 = mn0 == -INFINITY ? 0.f : exp2f(s[nb][0] - mn0);
-      const float p01 = mn0 == -INFINITY ? 0.f : exp2f(s[nb][1] - mn0);
-      const float p10 = mn1 == -INFINITY ? 0.f : exp2f(s[nb][2] - mn1);
-      const float p11 = mn1 == -INFINITY ? 0.f : exp2f(s[nb][3] - mn1);
+      // Half of the exponentials on the SFU, half as a polynomial on the FMA
+      // pipe: the SFU is the bottleneck of this loop on sm_100.
+      float p00, p01, p10, p11;
+      if (nb & 1) {
+        p00 = exp2_fma(s[nb][0] - mn0);
+        p01 = exp2_fma(s[nb][1] - mn0);
+        p10 = exp2_fma(s[nb][2] - mn1);
+        p11 = exp2_fma(s[nb][3] - mn1);
+      } else {
+        p00 = exp2f(s[nb][0] - mn0);
+        p01 = exp2f(s[nb][1] - mn0);
+        p10 = exp2f(s[nb][2] - mn1);
+        p11 = exp2f(s[nb][3] - mn1);
+      }
+      if (mn0 == -INFINITY) p00 = p01 = 0.f;
+      if (mn1 == -INFINITY) p10 = p11 = 0.f;
       ls0 += p00 + p01;
       ls1 += p10 + p11;
       const int kk = nb >> 1, hi = nb & 1;
