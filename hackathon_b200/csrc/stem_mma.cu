@@ -127,124 +127,12 @@ __global__ void __launch_bounds__(WARPS * 32) stem_mma_kernel(const float* __res
   }
 }
 
-// Row-tiled variant: a CTA of 8 warps owns 128 consecutive output pixels that
-// form whole output rows of one image (128 % Wo == 0).  The input rows they
-// read (all channels, padded with zeros) are staged once in shared memory with
-// coalesced loads; fragments are then gathered from shared memory instead of
-// scattered global loads.
-constexpr int RW = 8;             // warps per CTA
-constexpr int SMEM_IN = 4096;     // floats of staged input (C * rows * cols)
-
-__global__ void __launch_bounds__(RW * 32) stem_mma_rows_kernel(const float* __restrict__ x,
-                                                                const float* __restrict__ w,
-                                                                const float* __restrict__ bias,
-                                                                __nv_bfloat16* __restrict__ out, c3b_stem_params p,
-                                                                int act, int IR, int IC) {
-  __shared__ float sin_[SMEM_IN];
-  __shared__ __align__(16) __nv_bfloat16 stage[RW][16][COUT + 8];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int K = p.c * p.g.kh * p.g.kw;
-  uint32_t bf[8][2][2];
-#pragma unroll
-  for (int nb = 0; nb < 8; ++nb)
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      const int n = nb * 8 + g;
-      const int k0 = ks * 16 + 2 * t;
-      auto wv = [&](int k) { return k < K ? w[k * COUT + n] : 0.f; };
-      bf[nb][ks][0] = pk_bf16(wv(k0), wv(k0 + 1));
-      bf[nb][ks][1] = pk_bf16(wv(k0 + 8), wv(k0 + 9));
-    }
-  // shared-memory offsets of this thread's 8 k values (relative to the pixel's origin)
-  int koff[8];
-  bool kv[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int k = (i >> 2) * 16 + 2 * t + (i & 1) + ((i >> 1) & 1) * 8;
-    kv[i] = k < K;
-    const int kk = kv[i] ? k : 0;
-    const int c = kk / (p.g.kh * p.g.kw), r = (kk / p.g.kw) % p.g.kh, s = kk % p.g.kw;
-    koff[i] = (c * IR + r * p.g.dh) * IC + s * p.g.dw;
-  }
-  const int rows = 128 / p.wo;
-  const int64_t M = (int64_t)p.n * p.ho * p.wo;
-  const int64_t nblk = M / 128;
-  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
-    const int64_t m0 = blk * 128;
-    const int n = (int)(m0 / ((int64_t)p.ho * p.wo));
-    const int oh0 = (int)((m0 / p.wo) % p.ho);
-    const int ih0 = oh0 * p.g.sh - p.g.ph0, iw0 = -p.g.pw0;
-    __syncthreads();  // previous block's fragments are gathered
-    for (int e = threadIdx.x; e < p.c * IR * IC; e += blockDim.x) {
-      const int col = e % IC, rr = (e / IC) % IR, c = e / (IC * IR);
-      const int ih = ih0 + rr, iw = iw0 + col;
-      float v = 0.f;
-      if (ih >= 0 && ih < p.h && iw >= 0 && iw < p.w) v = __ldg(x + (((int64_t)n * p.c + c) * p.h + ih) * p.w + iw);
-      sin_[e] = v;
-    }
-    __syncthreads();
-    float v[2][8];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int pix = warp * 16 + g + 8 * h;  // 0..127 within the block
-      const int orow = pix / p.wo, ocol = pix % p.wo;
-      const int base = (orow * p.g.sh) * IC + ocol * p.g.sw;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[h][i] = kv[i] ? sin_[base + koff[i]] : 0.f;
-    }
-    uint32_t af[2][4];
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      af[ks][0] = pk_bf16(v[0][ks * 4 + 0], v[0][ks * 4 + 1]);
-      af[ks][1] = pk_bf16(v[1][ks * 4 + 0], v[1][ks * 4 + 1]);
-      af[ks][2] = pk_bf16(v[0][ks * 4 + 2], v[0][ks * 4 + 3]);
-      af[ks][3] = pk_bf16(v[1][ks * 4 + 2], v[1][ks * 4 + 3]);
-    }
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      const float b0 = __ldg(bias + nb * 8 + 2 * t), b1 = __ldg(bias + nb * 8 + 2 * t + 1);
-      float acc[4] = {b0, b1, b0, b1};
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) mma_16816(acc, af[ks], bf[nb][ks][0], bf[nb][ks][1]);
-      const int col = nb * 8 + 2 * t;
-      *reinterpret_cast<uint32_t*>(&stage[warp][g][col]) = pk_bf16(apply_act(acc[0], act), apply_act(acc[1], act));
-      *reinterpret_cast<uint32_t*>(&stage[warp][g + 8][col]) =
-          pk_bf16(apply_act(acc[2], act), apply_act(acc[3], act));
-    }
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int chunk = lane + 32 * i;
-      const int row = chunk >> 3, c8 = (chunk & 7) * 8;
-      const int64_t m = m0 + warp * 16 + row;
-      *reinterpret_cast<uint4*>(out + m * COUT + c8) = *reinterpret_cast<const uint4*>(&stage[warp][row][c8]);
-    }
-    (void)rows;
-  }
-}
-
 }  // namespace
 
 bool launch_stem_mma(const c3b_tensor* in, const c3b_tensor& out, const c3b_stem_conv_params& p, cudaStream_t s) {
   const c3b_stem_params& g = p.geom;
   if (p.cout != COUT || g.c * g.g.kh * g.g.kw > 32) return false;
   const int64_t M = (int64_t)g.n * g.ho * g.wo;
-  const int pix = g.ho * g.wo;
-  if (pix % 128 == 0 && 128 % g.wo == 0) {
-    const int rows = 128 / g.wo;
-    const int IR = (rows - 1) * g.g.sh + (g.g.kh - 1) * g.g.dh + 1;
-    const int IC = (g.wo - 1) * g.g.sw + (g.g.kw - 1) * g.g.dw + 1;
-    if (g.c * IR * IC <= SMEM_IN) {
-      int64_t blocks = M / 128;
-      const int64_t cap2 = (int64_t)sm_count() * 4;
-      if (blocks > cap2) blocks = cap2;
-      stem_mma_rows_kernel<<<(unsigned)blocks, RW * 32, 0, s>>>((const float*)in[0].ptr, (const float*)in[1].ptr,
-                                                                (const float*)in[2].ptr, (__nv_bfloat16*)out.ptr, g,
-                                                                p.act, IR, IC);
-      return true;
-    }
-  }
   const int64_t tiles = (M + 15) / 16;
   int64_t blocks = (tiles + WARPS - 1) / WARPS;
   const int64_t cap = (int64_t)sm_count() * 16;
