@@ -90,6 +90,41 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   return v;
 }
 
+// GELU for bf16 outputs: erf from the Abramowitz & Stegun 7.1.26 rational
+// approximation (|error| < 1.5e-7, the same formula the reference's unfused Erf
+// uses) with the fast reciprocal and exponential — two SFU operations and a
+// handful of FMAs per element instead of the full-precision erff, whose cost
+// made the FFN1 epilogue slower than its MMAs.  The result is rounded to bf16.
+__device__ __forceinline__ float gelu_as_fast(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f),
+                                      -0.284496736f), 0.254829592f);
+  const float e = 1.0f - poly * __expf(-z * z);  // erf(|x| / sqrt 2)
+  const float erf_v = x < 0.f ? -e : e;
+  return 0.5f * x * (1.0f + erf_v);
+}
+
+// Activation over a register array, chosen once per call (a warp-uniform
+// branch): a per-element select lets the compiler evaluate every variant,
+// erff included, for every element — which cost the tcgen05 GEMM epilogues a
+// third of their throughput.  bf16 outputs take the fast GELU.
+template <int N>
+__device__ __forceinline__ void act_inplace(float* v, int act, bool bf16_out) {
+  if (act == C3B_ACT_RELU) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = fmaxf(v[i], 0.0f);
+  } else if (act == C3B_ACT_GELU) {
+    if (bf16_out) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = gelu_as_fast(v[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = gelu_erf(v[i]);
+    }
+  }
+}
+
 // ---- kernel entry points implemented in the .cu files (host launchers)
 int launch_ew(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_ew_params& p, cudaStream_t s);
 int launch_copy(const c3b_tensor& in, const c3b_tensor& out, const c3b_copy_params& p, cudaStream_t s);

@@ -214,12 +214,13 @@ __device__ __forceinline__ void store32_bf16(const TcArgs& a, int64_t off, int64
       for (int j = 0; j < 8; ++j) v[8 * i + j] += __bfloat162float(rb[j]);
     }
   }
+  act_inplace<32>(v, a.act, true);
   uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     __align__(16) __nv_bfloat16 o[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(apply_act(v[8 * i + j], a.act));
+    for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(v[8 * i + j]);
     op[i] = *reinterpret_cast<const uint4*>(o);
   }
 }
@@ -264,8 +265,7 @@ __device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t c
       }
     }
   }
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i], a.act);
+  act_inplace<32>(v, a.act, a.dt_out == C3B_BF16);
   if (a.dt_out == C3B_BF16) {
     uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
 #pragma unroll
@@ -418,23 +418,28 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
       const int64_t row = (int64_t)mb * BM + q * 32 + lane;
       const int64_t col_base = (int64_t)nb * a.block_n + half * cols;
       const bool row_ok = row < a.M && col_base < a.N;
-      uint4 r0[8];
-      if (a.res && row_ok) load_res32(a, row * a.N + col_base, r0);
+      // Residual chunks are software-pipelined one chunk ahead (chunk 0 before
+      // the accumulator wait), so their load latency hides behind the
+      // previous chunk's TMEM load, math and stores.
+      uint4 rcur[8], rnext[8];
+      if (a.res && row_ok) load_res32(a, row * a.N + col_base, rcur);
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 14);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.block_n + half * cols);
+#pragma unroll 1
       for (int c0 = 0; c0 < cols; c0 += 32) {
+        const bool more = a.res && row_ok && c0 + 32 < cols && col_base + c0 + 32 < a.N;
+        if (more) load_res32(a, row * a.N + col_base + c0 + 32, rnext);
         float v[32];
         tmem_ld32(tbase + c0, v);
-        if (!row_ok || col_base + c0 >= a.N) continue;
-        const int64_t off = row * a.N + col_base + c0;
-        if (a.res && c0 > 0) {
-          uint4 r1[8];
-          load_res32(a, off, r1);
-          finish32(a, off, col_base + c0, v, r1);
-        } else {
-          finish32(a, off, col_base + c0, v, a.res ? r0 : nullptr);
+        if (row_ok && col_base + c0 < a.N) {
+          const int64_t off = row * a.N + col_base + c0;
+          finish32(a, off, col_base + c0, v, a.res ? rcur : nullptr);
+        }
+        if (more) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rcur[i] = rnext[i];
         }
       }
       tc_fence_before();
@@ -482,8 +487,7 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, int64_t off, int64_
       }
     }
   }
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = apply_act(v[i], a.act);
+  act_inplace<16>(v, a.act, a.dt_out == C3B_BF16);
   if (a.dt_out == C3B_BF16) {
     __align__(16) __nv_bfloat16 o[16];
 #pragma unroll

@@ -849,12 +849,13 @@ __global__ void __launch_bounds__(256) stem_conv_kernel(const float* __restrict_
           }
         }
       }
+    act_inplace<CH>(acc, act, true);
     uint4* orow = reinterpret_cast<uint4*>(out + m * COUT + half * CH);
 #pragma unroll
     for (int o = 0; o < CH / 8; ++o) {
       __align__(16) __nv_bfloat16 b8[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) b8[j] = __float2bfloat16_rn(apply_act(acc[8 * o + j], act));
+      for (int j = 0; j < 8; ++j) b8[j] = __float2bfloat16_rn(acc[8 * o + j]);
       orow[o] = *reinterpret_cast<const uint4*>(b8);
     }
   }

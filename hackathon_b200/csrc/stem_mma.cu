@@ -105,13 +105,12 @@ __global__ void __launch_bounds__(WARPS * 32) stem_mma_kernel(const float* __res
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks) mma_16816(acc[nb], af[ks], bf[nb][ks][0], bf[nb][ks][1]);
     }
+    act_inplace<32>(&acc[0][0], act, true);
 #pragma unroll
     for (int nb = 0; nb < 8; ++nb) {
       const int col = nb * 8 + 2 * t;
-      *reinterpret_cast<uint32_t*>(&stage[warp][g][col]) =
-          pk_bf16(apply_act(acc[nb][0], act), apply_act(acc[nb][1], act));
-      *reinterpret_cast<uint32_t*>(&stage[warp][g + 8][col]) =
-          pk_bf16(apply_act(acc[nb][2], act), apply_act(acc[nb][3], act));
+      *reinterpret_cast<uint32_t*>(&stage[warp][g][col]) = pk_bf16(acc[nb][0], acc[nb][1]);
+      *reinterpret_cast<uint32_t*>(&stage[warp][g + 8][col]) = pk_bf16(acc[nb][2], acc[nb][3]);
     }
     __syncwarp();
     // 16 rows x 128 bytes: 128 chunks of 16 bytes, 4 per lane, consecutive in memory.
