@@ -40,6 +40,9 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 struct __align__(64) TmaMaps {
   CUtensorMap a[4];
   CUtensorMap b;
+  // epilogue tiles (row-ring conv): residual load and output store, 64-byte
+  // swizzled boxes of 32 channels x one warp's 32 pixels
+  CUtensorMap res, out;
 };
 
 struct TcArgs {
@@ -132,6 +135,26 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "[%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The shared-memory source of every committed bulk store has been read.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk `ch` (0..3) of row `row` in a 64-byte-row tile
+// stored with the TMA 64-byte swizzle (chunk bits 4-5 XOR address bits 7-8;
+// the tile base is 1024-byte aligned).
+__device__ __forceinline__ uint32_t swz64(int row, int ch) {
+  return (uint32_t)(row * 64) + (uint32_t)((ch ^ ((row >> 1) & 3)) << 4);
 }
 
 // UMMA shared-memory descriptor: K-major operand, 128-byte swizzle, 8-row
@@ -747,13 +770,15 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
   const uint32_t b_bytes = (uint32_t)a.block_n * BK * 2;
   uint8_t* sr = smem;
   uint8_t* sb = smem + (size_t)NS * rb_al;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + (size_t)9 * b_bytes);
+  uint8_t* stg = sb + (size_t)9 * b_bytes;  // 8 epilogue warps x 2 rows x 2 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stg + 8 * 4096);
   uint64_t* rfull = bars;
   uint64_t* rempty = rfull + NS;
   uint64_t* wfull = rempty + NS;
   uint64_t* tfull = wfull + 1;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* resbar = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(resbar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -771,6 +796,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 8);
     }
+    for (int i = 0; i < 8; ++i) mbar_init(&resbar[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -831,17 +857,26 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
           if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 34)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d0 = tmem_base + (uint32_t)(acc * 2 * a.block_n);
+          // One thread issues all 72 MMAs of the pair, so their operands are
+          // precomputed descriptors plus compile-time offsets (the descriptor
+          // address field is in 16-byte units): no per-MMA division or
+          // descriptor rebuild on the issue path.
+          uint64_t arow[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) arow[i] = smem_desc(smem_u32(sr + (size_t)((cbase + 2 * pr + i) % NS) * rb_al));
+          const uint64_t bd0 = smem_desc(smem_u32(sb));
+          const uint64_t sstep = (uint64_t)(a.img * 128) >> 4;
+#pragma unroll
           for (int tap = 0; tap < 9; ++tap) {
             const int r = tap / 3, s = tap % 3;
-            const uint32_t b_addr = smem_u32(sb + (size_t)tap * b_bytes);
+            const uint64_t bd = bd0 + (uint64_t)((tap * 64 * BK * 2) >> 4);
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-              const uint32_t c = cbase + 2 * pr + j + r;
-              const uint32_t a_addr = smem_u32(sr + (size_t)(c % NS) * rb_al) + (uint32_t)(s * a.img) * 128u;
+              const uint64_t ad = arow[j + r] + (uint64_t)s * sstep;
 #pragma unroll
               for (int k = 0; k < BK / 16; ++k)
-                mma_bf16(d0 + (uint32_t)(j * a.block_n), smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32),
-                         idesc, (tap > 0 || k > 0) ? 1u : 0u);
+                mma_bf16(d0 + (uint32_t)(j * 64), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                         (tap > 0 || k > 0) ? 1u : 0u);
             }
           }
           mma_commit(&tfull[acc]);
@@ -854,52 +889,88 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
       }
     }
   } else {
+    // Epilogue: warp (q, half) owns TMEM lanes 32q..32q+31 (pixels) and
+    // channels 32*half..+31 of both output rows.  Its residual rows arrive by
+    // TMA into a private 2 x 2 KB tile; results overwrite the tile in place and
+    // leave by TMA store, so global traffic is whole 64-byte rows instead of
+    // one 16-byte piece per lane per instruction.
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int cols = a.block_n >> 1;
+    const int ew = warp - 2;
+    uint8_t* tile = stg + (size_t)ew * 4096;
+    uint64_t* rbar = &resbar[ew];
+    uint32_t rphase = 0;
+    const int pw = 32 / a.img;  // output columns per warp
     int acc = 0;
     uint32_t acc_phase = 0;
     bool run = true;
+    float bias[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) bias[i] = a.bias ? __ldg(a.bias + half * 32 + i) : 0.f;
     for (int u = blockIdx.x; u < a.n_items && run; u += gridDim.x) {
       const int seg = u % a.segs;
       const int strip = u / a.segs;
       const int wb = strip % a.wblocks, ib = strip / a.wblocks;
-      const int m = q * 32 + lane;
-      const int img = ib * a.img + (m % a.img);
-      const int w = wb * a.wt + m / a.img;
-      const bool img_ok = img < a.n_img;
-      const int64_t col_base = half * cols;
+      const int img0 = ib * a.img;
+      const int w0 = wb * a.wt + q * pw;
       for (int pr = 0; pr < SR / 2; ++pr) {
         const int hrow = seg * SR + 2 * pr;
-        uint4 rv[2][4];
-        if (a.res && img_ok) {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int64_t pix = ((int64_t)img * a.ho + hrow + j) * a.wo + w;
-            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) +
-                                                             pix * a.N + col_base);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) rv[j][i] = rp[i];
+        if (lane == 0) {
+          bulk_wait_read0();  // the previous stores have left the tile
+          if (a.res) {
+            mbar_arrive_tx(rbar, 4096);
+            tma_load_4d(tile, &maps.res, rbar, half * 32, img0, w0, hrow);
+            tma_load_4d(tile + 2048, &maps.res, rbar, half * 32, img0, w0, hrow + 1);
           }
         }
         const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 35);
         if (!__all_sync(0xffffffffu, ok)) { run = false; break; }
         tc_fence_after();
+        float v[2][32];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int64_t pix = ((int64_t)img * a.ho + hrow + j) * a.wo + w;
-          const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) +
-                              (uint32_t)((acc * 2 + j) * a.block_n + half * cols);
-          float v[32];
-          tmem_ld32(tb, v);
-          if (img_ok) store32_bf16(a, pix * a.N + col_base, col_base, v, a.res ? rv[j] : nullptr);
-        }
+        for (int j = 0; j < 2; ++j)
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((acc * 2 + j) * a.block_n + half * 32), v[j]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        if (a.res) {
+          const bool rok = mbar_wait(rbar, rphase, abort_flag, 36);
+          rphase ^= 1;
+          if (!__all_sync(0xffffffffu, rok)) { run = false; break; }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint8_t* trow = tile + j * 2048;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4* cp = reinterpret_cast<uint4*>(trow + swz64(lane, c));
+            float x[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = v[j][c * 8 + e] + bias[c * 8 + e];
+            if (a.res) {
+              const uint4 rw = *cp;
+              const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rw);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) x[e] += __bfloat162float(rb[e]);
+            }
+            act_inplace<8>(x, a.act, true);
+            __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = __float2bfloat16_rn(x[e]);
+            *cp = *reinterpret_cast<const uint4*>(o);
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_4d(&maps.out, tile, half * 32, img0, w0, hrow);
+          tma_store_4d(&maps.out, tile + 2048, half * 32, img0, w0, hrow + 1);
+          bulk_commit();
+        }
       }
     }
+    if (lane == 0) bulk_wait0();
   }
 
   tc_fence_before();
@@ -934,13 +1005,12 @@ static EncodeTiledFn get_encode() {
 }
 
 static int encode(CUtensorMap* m, void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                  const uint32_t* box) {
+                  const uint32_t* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = get_encode();
   if (!fn) return fail(C3B_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, base, (const cuuint64_t*)dims,
-                  (const cuuint64_t*)strides_bytes, (const cuuint32_t*)box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  (const cuuint64_t*)strides_bytes, (const cuuint32_t*)box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(C3B_E_INVALID, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
   return C3B_OK;
 }
@@ -1087,7 +1157,9 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   // Halo mode: 3x3, stride 1, pad 1, Cout <= 128 (one weight tile), two output
   // rows per super-tile.
   const int wt = p.wo < 16 ? p.wo : 16;
-  if (p.mode != 1 && p.k == 3 && p.stride == 1 && p.pad == 1 && p.cout <= 128 && a.n_tiles_n == 1 &&
+  // (bf16 output and residual only: their epilogues store bf16 rows)
+  const bool bf16_epi = a.dt_out == C3B_BF16 && (!a.res || a.dt_res == C3B_BF16);
+  if (p.mode != 1 && bf16_epi && p.k == 3 && p.stride == 1 && p.pad == 1 && p.cout <= 128 && a.n_tiles_n == 1 &&
       p.wo % wt == 0 && 128 % wt == 0 && (128 / wt) >= 8 && p.ho % 2 == 0) {
     a.img = 128 / wt;
     a.wt = wt;
@@ -1106,16 +1178,25 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
         a.row_bytes = 64 * a.img * (wt + 2) * 2;
         const size_t rb = ((size_t)a.row_bytes + 1023) & ~(size_t)1023;
         const size_t wbytes = (size_t)9 * 64 * tc::BK * 2;
+        const size_t epi = 8 * 4096;  // per-warp epilogue tiles
         const size_t budget = 212 * 1024;
-        int ring = (int)((budget - wbytes) / rb);
+        int ring = (int)((budget - wbytes - epi) / rb);
         if (ring > 8) ring = 8;
-        if (ring >= 5) {
+        if (ring >= 5 && 32 % a.img == 0) {
           a.ring = ring;
           uint64_t dims[4] = {C, (uint64_t)p.n, (uint64_t)p.w, (uint64_t)p.h};
           uint64_t str[3] = {(uint64_t)p.h * p.w * C * 2, C * 2, (uint64_t)p.w * C * 2};
           uint32_t box[4] = {64, (uint32_t)a.img, (uint32_t)(wt + 2), 1};
           if ((rc = encode(&maps.a[0], x, 4, dims, str, box))) return rc;
-          const size_t smem = 1024 + ring * rb + wbytes + (2 * ring + 5) * 8 + 16;
+          // residual and output: NHWC [n, ho, wo, 64], one warp's 32 pixels x 32 channels per box
+          uint64_t odims[4] = {64, (uint64_t)p.n, (uint64_t)p.wo, (uint64_t)p.ho};
+          uint64_t ostr[3] = {(uint64_t)p.ho * p.wo * 64 * 2, 64 * 2, (uint64_t)p.wo * 64 * 2};
+          uint32_t obox[4] = {32, (uint32_t)a.img, (uint32_t)(32 / a.img), 1};
+          if ((rc = encode(&maps.out, out.ptr, 4, odims, ostr, obox, CU_TENSOR_MAP_SWIZZLE_64B))) return rc;
+          if (p.has_residual &&
+              (rc = encode(&maps.res, const_cast<void*>(a.res), 4, odims, ostr, obox, CU_TENSOR_MAP_SWIZZLE_64B)))
+            return rc;
+          const size_t smem = 1024 + ring * rb + wbytes + epi + (2 * ring + 13) * 8 + 16;
           static bool attr_ring = false;
           if (!attr_ring) {
             C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_conv_rowring_kernel,

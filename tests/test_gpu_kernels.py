@@ -302,9 +302,10 @@ def test_gemm_tc(torch_cuda, M, N, K, act, res):
                                                        (10, 4, 256, 512, 3, 1, 1), (16, 8, 256, 512, 3, 2, 0),
                                                        (9, 32, 64, 64, 3, 1, 1), (3, 8, 64, 128, 3, 1, 1),
                                                        (5, 4, 128, 64, 3, 1, 0), (33, 16, 128, 128, 3, 1, 0),
-                                                       (17, 32, 64, 64, 3, 1, 1), (40, 16, 64, 64, 3, 1, 0)])
+                                                       (17, 32, 64, 64, 3, 1, 1), (40, 16, 64, 64, 3, 1, 0),
+                                                       (16, 32, 64, 64, 3, 1, 1)])
 def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res, mode):
-    """mode 0 uses halo tiles where eligible (3x3 s1, Cout <= 128), mode 1 one TMA window per tap."""
+    """mode 0: fastest eligible variant (row ring / halo); 1: one TMA window per tap; 2/3: halo tiles."""
     import torch
     from hackathon_b200 import _lib as L
     pad = k // 2
