@@ -400,6 +400,8 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
     // ---------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = instr_desc(BM, a.block_n);
+      // stage descriptors = base descriptor + offset in 16-byte units
+      const uint64_t ad0 = smem_desc(smem_u32(sa)), bd0 = smem_desc(smem_u32(sb));
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -412,13 +414,11 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
         for (int kb = 0; kb < a.k_blocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, 13)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sa + (size_t)stage * a_bytes);
-          const uint32_t b_addr = smem_u32(sb + (size_t)stage * b_bytes);
+          const uint64_t ad = ad0 + (uint64_t)stage * (a_bytes >> 4);
+          const uint64_t bd = bd0 + (uint64_t)stage * (b_bytes >> 4);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            mma_bf16(d_tmem, smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32), idesc,
-                     (kb > 0 || k > 0) ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
           mma_commit(&empty[stage]);
           if (++stage == stages) { stage = 0; phase ^= 1; }
         }
@@ -559,7 +559,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int R = a.rows;
+  constexpr int R = 2;  // output rows per tile (the host sets a.rows = 2)
   const uint32_t tmem_cols = (uint32_t)(a.block_n * R * 2);
   const int WT2 = a.wt + 2;
 
@@ -631,6 +631,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = instr_desc(BM, a.block_n);
+      const uint64_t bd0 = smem_desc(smem_u32(sb));
       int hs = 0, bs = 0, acc = 0;
       uint32_t hph = 0, bph = 0, acc_phase = 0;
       bool bres_ok = true;
@@ -646,20 +647,25 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
         for (int cb = 0; cb < a.cblocks && ok; ++cb) {
           if (!mbar_wait(&hfull[hs], hph, abort_flag, 24)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t hbase = smem_u32(sh + (size_t)hs * hbytes_al);
+          // descriptors: halo base + compile-time tap/row offsets (16-byte units)
+          const uint64_t hd = smem_desc(smem_u32(sh + (size_t)hs * hbytes_al));
+          const uint64_t sstep = (uint64_t)(a.img * 128) >> 4;
+          const uint64_t rstep = (uint64_t)WT2 * sstep;
+#pragma unroll
           for (int tap = 0; tap < 9; ++tap) {
             if (!a.bres) {
               if (!mbar_wait(&bfull[bs], bph, abort_flag, 25)) { ok = false; break; }
               tc_fence_after();
             }
             const int r = tap / 3, s = tap % 3;
-            const uint32_t b_addr = smem_u32(sb + (size_t)(a.bres ? cb * 9 + tap : bs) * b_bytes);
+            const uint64_t bd = bd0 + (uint64_t)(a.bres ? cb * 9 + tap : bs) * (b_bytes >> 4);
+#pragma unroll
             for (int j = 0; j < R; ++j) {
-              const uint32_t a_addr = hbase + (uint32_t)(((j + r) * WT2 + s) * a.img) * 128u;
+              const uint64_t ad = hd + (uint64_t)(j + r) * rstep + (uint64_t)s * sstep;
 #pragma unroll
               for (int k = 0; k < BK / 16; ++k)
-                mma_bf16(d0 + (uint32_t)(j * a.block_n), smem_desc(a_addr + k * 32), smem_desc(b_addr + k * 32),
-                         idesc, (cb > 0 || tap > 0 || k > 0) ? 1u : 0u);
+                mma_bf16(d0 + (uint32_t)(j * a.block_n), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                         (cb > 0 || tap > 0 || k > 0) ? 1u : 0u);
             }
             if (!a.bres) {
               mma_commit(&bempty[bs]);
