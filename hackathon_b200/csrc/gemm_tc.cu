@@ -824,8 +824,10 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
   if (warp == 0) {
     if (lane == 0) {
       mbar_arrive_tx(&wfull[0], 9u * b_bytes);
+      // weight block order [W(2,s), W(1,s), W(0,s)] per column shift s, so that
+      // W(r,s) followed by W(r-1,s) is one 128-row B operand
       for (int tap = 0; tap < 9; ++tap)
-        tma_load_2d(sb + (size_t)tap * b_bytes, &maps.b, &wfull[0], tap * a.cin, 0);
+        tma_load_2d(sb + (size_t)((tap % 3) * 3 + 2 - tap / 3) * b_bytes, &maps.b, &wfull[0], tap * a.cin, 0);
       uint32_t c = 0;  // rows loaded so far
       for (int u = blockIdx.x; u < a.n_items; u += gridDim.x) {
         const int seg = u % a.segs;
@@ -844,7 +846,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(BM, a.block_n);
+      const uint32_t idesc64 = instr_desc(BM, 64), idesc128 = instr_desc(BM, 128);
       int acc = 0;
       uint32_t acc_phase = 0;
       uint32_t cbase = 0;
@@ -863,26 +865,33 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
           if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 34)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d0 = tmem_base + (uint32_t)(acc * 2 * a.block_n);
-          // One thread issues all 72 MMAs of the pair, so their operands are
+          // One thread issues all MMAs of the pair, so their operands are
           // precomputed descriptors plus compile-time offsets (the descriptor
-          // address field is in 16-byte units): no per-MMA division or
-          // descriptor rebuild on the issue path.
+          // address field is in 16-byte units).  Input row i of the pair feeds
+          // output row 0 through tap r = i and output row 1 through r = i - 1:
+          // rows 1 and 2 use one N=128 MMA with B = [W(i,s); W(i-1,s)] into both
+          // accumulator halves; rows 0 and 3 use N=64 MMAs into one half and go
+          // first, so that they initialise the accumulators.
           uint64_t arow[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) arow[i] = smem_desc(smem_u32(sr + (size_t)((cbase + 2 * pr + i) % NS) * rb_al));
           const uint64_t bd0 = smem_desc(smem_u32(sb));
           const uint64_t sstep = (uint64_t)(a.img * 128) >> 4;
+          constexpr uint64_t WB = (64 * BK * 2) >> 4;  // one weight block
 #pragma unroll
-          for (int tap = 0; tap < 9; ++tap) {
-            const int r = tap / 3, s = tap % 3;
-            const uint64_t bd = bd0 + (uint64_t)((tap * 64 * BK * 2) >> 4);
+          for (int step = 0; step < 4; ++step) {
+            const int i = step == 0 ? 0 : step == 1 ? 3 : step - 1;  // 0, 3, 1, 2
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const uint64_t ad = arow[j + r] + (uint64_t)s * sstep;
+            for (int s = 0; s < 3; ++s) {
+              const uint64_t ad = arow[i] + (uint64_t)s * sstep;
+              // block of W(r,s) is s*3 + 2 - r
+              const int r_top = i == 3 ? 2 : i;
+              const uint64_t bd = bd0 + (uint64_t)(s * 3 + 2 - r_top) * WB;
+              const uint32_t d = d0 + (i == 3 ? 64u : 0u);
+              const uint32_t id = (i == 0 || i == 3) ? idesc64 : idesc128;
 #pragma unroll
               for (int k = 0; k < BK / 16; ++k)
-                mma_bf16(d0 + (uint32_t)(j * 64), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
-                         (tap > 0 || k > 0) ? 1u : 0u);
+                mma_bf16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), id, (step > 1 || s > 0 || k > 0) ? 1u : 0u);
             }
           }
           mma_commit(&tfull[acc]);
