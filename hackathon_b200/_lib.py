@@ -135,7 +135,7 @@ EXPORTS = [
     "c3b_plan_add_output_slot", "c3b_plan_slot_ptr", "c3b_plan_add_h2d", "c3b_plan_add_d2h",
     "c3b_plan_add_record", "c3b_plan_add_wait", "c3b_plan_add_kernel", "c3b_plan_finalize",
     "c3b_plan_launch", "c3b_plan_sync", "c3b_plan_run", "c3b_plan_run_timed", "c3b_plan_kernel_count",
-    "c3b_plan_origin_stream",
+    "c3b_plan_origin_stream", "c3b_plan_stream",
 ]
 
 
@@ -179,6 +179,7 @@ def lib() -> C.CDLL:
     L.c3b_plan_sync.argtypes = [vp, C.c_double]
     L.c3b_plan_run.argtypes = [vp]
     L.c3b_plan_run_timed.argtypes = [vp, C.POINTER(C.c_float), i32]
+    L.c3b_plan_stream.argtypes = [vp, i32, C.POINTER(vp), C.POINTER(vp), C.POINTER(C.c_float)]
     L.c3b_plan_kernel_count.argtypes = [vp]
     L.c3b_plan_origin_stream.argtypes = [vp]
     L.c3b_plan_origin_stream.restype = vp

@@ -271,9 +271,26 @@ struct c3b_plan {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   int n_kernels = 0;
+  // streaming (c3b_plan_stream): device staging copies of the slots, one
+  // graph of the device pass per staging parity, a copy stream and its events
+  uint64_t in_total = 0, out_total = 0;
+  std::vector<uint64_t> in_base, out_base;
+  uint8_t* stg_in[2] = {nullptr, nullptr};
+  uint8_t* stg_out[2] = {nullptr, nullptr};
+  cudaGraphExec_t sexec[2] = {nullptr, nullptr};
+  cudaStream_t cstream = nullptr;
+  cudaEvent_t in_ready[2] = {nullptr, nullptr}, pass_done[2] = {nullptr, nullptr}, out_read[2] = {nullptr, nullptr};
+  cudaEvent_t t_begin = nullptr, t_end = nullptr, c_end = nullptr;
 };
 
-static int plan_enqueue(c3b_plan* p, std::vector<cudaEvent_t>* timers) {
+// Device staging for one streamed pass: slot copies read and write device
+// buffers (parity `par`) instead of the pinned host slots.
+struct Staging {
+  const c3b_plan* p;
+  int par;
+};
+
+static int plan_enqueue(c3b_plan* p, std::vector<cudaEvent_t>* timers, const Staging* stg = nullptr) {
   C3B_CHECK_CUDA(cudaEventRecord(p->fork, p->origin));
   for (auto s : p->streams) C3B_CHECK_CUDA(cudaStreamWaitEvent(s, p->fork, 0));
   int k = 0;
@@ -290,12 +307,20 @@ static int plan_enqueue(c3b_plan* p, std::vector<cudaEvent_t>* timers) {
         break;
       }
       case A_H2D:
-        C3B_CHECK_CUDA(cudaMemcpyAsync(p->arena + a.arena_off, (uint8_t*)p->in_slots[a.slot] + a.slot_off, a.bytes,
-                                       cudaMemcpyHostToDevice, s));
+        if (stg)
+          C3B_CHECK_CUDA(cudaMemcpyAsync(p->arena + a.arena_off, p->stg_in[stg->par] + p->in_base[a.slot] + a.slot_off,
+                                         a.bytes, cudaMemcpyDeviceToDevice, s));
+        else
+          C3B_CHECK_CUDA(cudaMemcpyAsync(p->arena + a.arena_off, (uint8_t*)p->in_slots[a.slot] + a.slot_off, a.bytes,
+                                         cudaMemcpyHostToDevice, s));
         break;
       case A_D2H:
-        C3B_CHECK_CUDA(cudaMemcpyAsync((uint8_t*)p->out_slots[a.slot] + a.slot_off, p->arena + a.arena_off, a.bytes,
-                                       cudaMemcpyDeviceToHost, s));
+        if (stg)
+          C3B_CHECK_CUDA(cudaMemcpyAsync(p->stg_out[stg->par] + p->out_base[a.slot] + a.slot_off, p->arena + a.arena_off,
+                                         a.bytes, cudaMemcpyDeviceToDevice, s));
+        else
+          C3B_CHECK_CUDA(cudaMemcpyAsync((uint8_t*)p->out_slots[a.slot] + a.slot_off, p->arena + a.arena_off, a.bytes,
+                                         cudaMemcpyDeviceToHost, s));
         break;
       case A_RECORD:
         C3B_CHECK_CUDA(cudaEventRecord(p->events[a.event], s));
@@ -379,6 +404,17 @@ int c3b_plan_destroy(c3b_plan* p) {
   if (!p) return C3B_OK;
   if (p->origin) cudaStreamSynchronize(p->origin);
   if (p->exec) cudaGraphExecDestroy(p->exec);
+  if (p->cstream) cudaStreamSynchronize(p->cstream);
+  for (int i = 0; i < 2; ++i) {
+    if (p->sexec[i]) cudaGraphExecDestroy(p->sexec[i]);
+    if (p->stg_in[i]) cudaFree(p->stg_in[i]);
+    if (p->stg_out[i]) cudaFree(p->stg_out[i]);
+    for (cudaEvent_t e : {p->in_ready[i], p->pass_done[i], p->out_read[i]})
+      if (e) cudaEventDestroy(e);
+  }
+  for (cudaEvent_t e : {p->t_begin, p->t_end, p->c_end})
+    if (e) cudaEventDestroy(e);
+  if (p->cstream) cudaStreamDestroy(p->cstream);
   if (p->graph) cudaGraphDestroy(p->graph);
   for (auto s : p->streams) cudaStreamDestroy(s);
   for (auto e : p->events) cudaEventDestroy(e);
@@ -570,6 +606,100 @@ int c3b_plan_run(c3b_plan* p) {
   int rc = c3b_plan_launch(p);
   if (rc) return rc;
   return c3b_plan_sync(p, 600.0);
+}
+
+// Lazily set up the streaming state: staging buffers, the two device-pass
+// graphs (captured like c3b_plan_finalize's), the copy stream and events.
+static int stream_setup(c3b_plan* p) {
+  if (p->sexec[0]) return C3B_OK;
+  p->in_base.clear();
+  p->out_base.clear();
+  p->in_total = p->out_total = 0;
+  for (uint64_t b : p->in_bytes) { p->in_base.push_back(p->in_total); p->in_total += (b + 255) & ~255ull; }
+  for (uint64_t b : p->out_bytes) { p->out_base.push_back(p->out_total); p->out_total += (b + 255) & ~255ull; }
+  for (int i = 0; i < 2; ++i) {
+    C3B_CHECK_CUDA(cudaMalloc(&p->stg_in[i], p->in_total ? p->in_total : 256));
+    C3B_CHECK_CUDA(cudaMalloc(&p->stg_out[i], p->out_total ? p->out_total : 256));
+    C3B_CHECK_CUDA(cudaEventCreateWithFlags(&p->in_ready[i], cudaEventDisableTiming));
+    C3B_CHECK_CUDA(cudaEventCreateWithFlags(&p->pass_done[i], cudaEventDisableTiming));
+    C3B_CHECK_CUDA(cudaEventCreateWithFlags(&p->out_read[i], cudaEventDisableTiming));
+  }
+  C3B_CHECK_CUDA(cudaEventCreate(&p->t_begin));
+  C3B_CHECK_CUDA(cudaEventCreate(&p->t_end));
+  C3B_CHECK_CUDA(cudaEventCreateWithFlags(&p->c_end, cudaEventDisableTiming));
+  C3B_CHECK_CUDA(cudaStreamCreateWithFlags(&p->cstream, cudaStreamNonBlocking));
+  for (int par = 0; par < 2; ++par) {
+    Staging st{p, par};
+    C3B_CHECK_CUDA(cudaStreamBeginCapture(p->origin, cudaStreamCaptureModeThreadLocal));
+    int rc = plan_enqueue(p, nullptr, &st);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(p->origin, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return fail(C3B_E_CUDA, std::string("stream capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&p->sexec[par], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(C3B_E_CUDA, std::string("stream instantiate: ") + cudaGetErrorString(e));
+  }
+  return C3B_OK;
+}
+
+int c3b_plan_stream(c3b_plan* p, int n_steps, const void* const* in_host, void* const* out_host, float* ms) {
+  if (!p || !p->finalized) return fail(C3B_E_INVALID, "plan_stream: plan not finalized");
+  if (n_steps < 0) return fail(C3B_E_INVALID, "plan_stream: n_steps < 0");
+  const int n_in = (int)p->in_slots.size(), n_out = (int)p->out_slots.size();
+  if ((n_in && !in_host) || (n_out && !out_host)) return fail(C3B_E_INVALID, "plan_stream: host pointer lists");
+  for (int64_t i = 0; i < (int64_t)n_steps * n_in; ++i)
+    if (!in_host[i]) return fail(C3B_E_INVALID, "plan_stream: null input pointer");
+  for (int64_t i = 0; i < (int64_t)n_steps * n_out; ++i)
+    if (!out_host[i]) return fail(C3B_E_INVALID, "plan_stream: null output pointer");
+  int rc = stream_setup(p);
+  if (rc) return rc;
+  if (n_steps == 0) {
+    if (ms) *ms = 0.f;
+    return C3B_OK;
+  }
+  cudaStream_t cs = p->cstream, os = p->origin;
+  auto h2d = [&](int k) -> int {
+    uint8_t* dst = p->stg_in[k & 1];
+    for (int i = 0; i < n_in; ++i)
+      C3B_CHECK_CUDA(cudaMemcpyAsync(dst + p->in_base[i], in_host[(int64_t)k * n_in + i], p->in_bytes[i],
+                                     cudaMemcpyHostToDevice, cs));
+    C3B_CHECK_CUDA(cudaEventRecord(p->in_ready[k & 1], cs));
+    return C3B_OK;
+  };
+  C3B_CHECK_CUDA(cudaEventRecord(p->t_begin, os));
+  C3B_CHECK_CUDA(cudaStreamWaitEvent(cs, p->t_begin, 0));
+  if ((rc = h2d(0))) return rc;
+  for (int k = 0; k < n_steps; ++k) {
+    const int par = k & 1;
+    // device pass k: waits for its staged inputs and for the read-back of the
+    // outputs staged two passes ago (same parity)
+    C3B_CHECK_CUDA(cudaStreamWaitEvent(os, p->in_ready[par], 0));
+    if (k >= 2) C3B_CHECK_CUDA(cudaStreamWaitEvent(os, p->out_read[par], 0));
+    C3B_CHECK_CUDA(cudaGraphLaunch(p->sexec[par], os));
+    C3B_CHECK_CUDA(cudaEventRecord(p->pass_done[par], os));
+    // copies: next inputs (their staging buffer was consumed by pass k-1),
+    // then this pass's outputs
+    if (k + 1 < n_steps) {
+      if (k >= 1) C3B_CHECK_CUDA(cudaStreamWaitEvent(cs, p->pass_done[par ^ 1], 0));
+      if ((rc = h2d(k + 1))) return rc;
+    }
+    C3B_CHECK_CUDA(cudaStreamWaitEvent(cs, p->pass_done[par], 0));
+    for (int i = 0; i < n_out; ++i)
+      C3B_CHECK_CUDA(cudaMemcpyAsync(out_host[(int64_t)k * n_out + i], p->stg_out[par] + p->out_base[i], p->out_bytes[i],
+                                     cudaMemcpyDeviceToHost, cs));
+    C3B_CHECK_CUDA(cudaEventRecord(p->out_read[par], cs));
+  }
+  C3B_CHECK_CUDA(cudaEventRecord(p->c_end, cs));
+  C3B_CHECK_CUDA(cudaStreamWaitEvent(os, p->c_end, 0));
+  C3B_CHECK_CUDA(cudaEventRecord(p->t_end, os));
+  rc = c3b_plan_sync(p, 600.0);
+  if (rc) return rc;
+  if (ms) C3B_CHECK_CUDA(cudaEventElapsedTime(ms, p->t_begin, p->t_end));
+  return C3B_OK;
 }
 
 int c3b_plan_run_timed(c3b_plan* p, float* ms, int n) {

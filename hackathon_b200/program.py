@@ -228,6 +228,38 @@ class Executor:
         self.native.run()
         return {n: self.output_view(n).copy() for n in self.prog.outputs}
 
+    def stream(self, batches: Sequence[Dict[str, np.ndarray]]) -> Tuple[List[Dict[str, np.ndarray]], float]:
+        """Run one pass per batch, back to back, with each batch's host->device
+        copy overlapped with the previous pass (``c3b_plan_stream``).  Batches
+        are staged in pinned buffers first; returns the outputs of every pass
+        and the device time of the stream in ms."""
+        if not self.copies:
+            raise RuntimeError("stream() needs an executor built with copies=True")
+        import torch
+        pins: List[List] = []
+        for feeds in batches:
+            row = []
+            for name in self.prog.inputs:
+                t = self.prog.tensors[name]
+                a = np.ascontiguousarray(feeds[name], NP_OF[t.dtype])
+                if a.shape != t.shape:
+                    raise ValueError(f"input {name!r} shape {a.shape} != planned {t.shape}")
+                h = torch.from_numpy(a).pin_memory()
+                row.append(h)
+            pins.append(row)
+        outs = [{n: torch.from_numpy(np.empty(self.prog.tensors[n].shape, NP_OF[self.prog.tensors[n].dtype])).pin_memory()
+                 for n in self.prog.outputs} for _ in pins]
+        ms = self.native.stream([[h.data_ptr() for h in row] for row in pins],
+                                [[o[n].data_ptr() for n in self.prog.outputs] for o in outs])
+        return [{n: o[n].numpy().copy() for n in self.prog.outputs} for o in outs], ms
+
+    def stream_slots(self, n_steps: int) -> float:
+        """``n_steps`` overlapped passes that all read this executor's pinned
+        input slots and write its output slots (the benchmark's e2e stream)."""
+        ins = [self.native.slot_ptr(False, self.in_slots[n]) for n in self.prog.inputs]
+        outs = [self.native.slot_ptr(True, self.out_slots[n]) for n in self.prog.outputs]
+        return self.native.stream([ins] * n_steps, [outs] * n_steps)
+
     def kernel_times(self) -> List[Tuple[str, float]]:
         ms = self.native.run_timed()
         return list(zip(self.native.kernel_labels, ms.tolist()))

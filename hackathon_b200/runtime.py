@@ -106,6 +106,25 @@ class NativePlan:
         L.check(self._L.c3b_plan_run_timed(self.h, arr, n), "plan_run_timed")
         return np.array(arr[:n], dtype=np.float64)
 
+    def stream(self, in_ptrs: Sequence[Sequence[int]], out_ptrs: Sequence[Sequence[int]]) -> float:
+        """Run ``len(in_ptrs)`` passes back to back with host copies overlapped
+        (``c3b_plan_stream``).  ``in_ptrs[k][i]`` is pass k's host source for
+        input slot i, ``out_ptrs[k][j]`` its host destination for output slot j.
+        Returns the device time of the whole stream in ms."""
+        n = len(in_ptrs)
+        if len(out_ptrs) != n:
+            raise ValueError("in_ptrs and out_ptrs need one entry per pass")
+        flat_in = [int(p) for row in in_ptrs for p in row]
+        flat_out = [int(p) for row in out_ptrs for p in row]
+        ia = (C.c_void_p * max(1, len(flat_in)))(*flat_in)
+        oa = (C.c_void_p * max(1, len(flat_out)))(*flat_out)
+        ms = C.c_float(0.0)
+        L.check(self._L.c3b_plan_stream(self.h, n, ia, oa, C.byref(ms)), "plan_stream")
+        return float(ms.value)
+
+    def slot_ptr(self, is_output: bool, slot: int) -> int:
+        return int(self._L.c3b_plan_slot_ptr(self.h, int(is_output), slot) or 0)
+
     @property
     def origin_stream(self) -> int:
         return int(self._L.c3b_plan_origin_stream(self.h) or 0)

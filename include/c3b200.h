@@ -312,6 +312,17 @@ int c3b_plan_run(c3b_plan* plan);
 /* Replay the timeline eagerly with CUDA events around every kernel action;
  * ms[i] receives the i-th kernel action's device time.  n = capacity. */
 int c3b_plan_run_timed(c3b_plan* plan, float* ms, int n);
+/* Run n_steps passes back to back with the host copies overlapped: the
+ * inputs of pass k+1 are copied (on a separate copy stream, into a device
+ * staging buffer) while pass k computes, and each pass's outputs leave through
+ * a staging buffer of their own.  in_host[k * n_in + i] is pass k's source for
+ * input slot i, out_host[k * n_out + j] its destination for output slot j
+ * (pinned memory for full overlap; the plan's own slots qualify).  Each pass
+ * runs the plan's timeline with its h2d / d2h actions reading and writing the
+ * staging buffers.  *ms (optional) = device time from the first copy to the
+ * last read-back.  No reference counterpart: the reference's run_planned
+ * executes one pass at a time (streaming extension of the plan executor). */
+int c3b_plan_stream(c3b_plan* plan, int n_steps, const void* const* in_host, void* const* out_host, float* ms);
 int c3b_plan_kernel_count(c3b_plan* plan);
 void* c3b_plan_origin_stream(c3b_plan* plan);
 

@@ -149,3 +149,24 @@ def test_kernels_only_executor_keeps_inputs_resident(wl):
     ref = Executor(lower(g, 4, "bf16")).run(feeds)["logits"]
     for o in outs:
         assert np.array_equal(o, ref)
+
+
+@pytest.mark.parametrize("model", ["resnet18", "tx_small"])
+def test_stream_matches_single_passes(wl, model):
+    """Streamed passes (host copies of pass k+1 overlapped with pass k,
+    c3b_plan_stream) give every batch exactly the outputs of a single pass."""
+    from hackathon_b200.lowering import lower
+    from hackathon_b200.program import Executor
+    g = wl.BUILDERS[model]()
+    batches = [wl.make_inputs(g, 8, seed=s) for s in (11, 12, 13, 14, 15)]
+    ex = Executor(lower(g, 8, "bf16"))
+    outs, ms = ex.stream(batches)
+    assert ms > 0 and len(outs) == len(batches)
+    single = Executor(lower(g, 8, "bf16"))
+    for feeds, o in zip(batches, outs):
+        ref = single.run(feeds)
+        for name in ref:
+            assert np.array_equal(o[name], ref[name]), name
+    # the second stream reuses the captured graphs and staging buffers
+    outs2, _ = ex.stream(batches[:2])
+    assert np.array_equal(outs2[1]["logits"], outs[1]["logits"])
