@@ -35,6 +35,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int NUM_THREADS = 192;
 constexpr int HALO_THREADS = 320;  // producer, MMA, 8 epilogue warps
+constexpr int HALO16_THREADS = 576;  // producer, MMA, 16 epilogue warps (tc_conv_halo_kernel)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 
 struct __align__(64) TmaMaps {
@@ -537,7 +538,7 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, int64_t off, int64_
 // window is a standard 1024-byte-aligned SW128 K-major operand.  Each weight
 // tap (BN x 64) is loaded once and used by all `rows` MMAs.  Versus one TMA
 // window per tap, this cuts L2->SM traffic about 3x for Cout <= 128.
-__global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __grid_constant__ TmaMaps maps,
+__global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const __grid_constant__ TmaMaps maps,
                                                                       const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -574,7 +575,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 8);
+      mbar_init(&tempty[i], 16);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -685,9 +686,22 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
     // 8 epilogue warps: warp w reads TMEM lane quarter (w % 4) and one half of
     // the tile's columns.  Residual rows are prefetched into registers before
     // waiting for the accumulator, so their latency overlaps the MMAs.
+    // 16 epilogue warps, four per TMEM lane quarter (warp % 4).  The tile's
+    // (row, 32-column chunk) pairs of a quarter are dealt round-robin, so a
+    // warp owns at most two chunks (Cout = 128) and prefetches both residual
+    // chunks before the accumulator wait: no load latency after it.
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int cols = a.block_n >> 1;  // 32 or 64 columns per warp
+    const int sub = (warp - 2) >> 2;  // 0..3
+    const int nch = a.block_n >> 5;   // chunks per row: 2 or 4
+    int jj[2], cc[2];
+    bool own[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int idx = sub + 4 * u;
+      own[u] = idx < R * nch;
+      jj[u] = own[u] ? idx / nch : 0;
+      cc[u] = own[u] ? idx % nch : 0;
+    }
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
@@ -701,42 +715,57 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_halo_kernel(const __g
       const int img = ib * a.img + (m % a.img);
       const int w = wb * a.wt + m / a.img;
       const bool img_ok = img < a.n_img;
-      const int64_t col_base = (int64_t)nb * a.block_n + half * cols;
-      // residual of the first 32 columns of both rows, prefetched
+      int64_t off[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+        off[u] = (((int64_t)img * a.ho + hb * R + jj[u]) * a.wo + w) * a.N + (int64_t)nb * a.block_n + cc[u] * 32;
       uint4 rv[2][4];
       if (a.res && img_ok) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int64_t pix = ((int64_t)img * a.ho + hb * R + j) * a.wo + w;
-          const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) +
-                                                           pix * a.N + col_base);
+        for (int u = 0; u < 2; ++u)
+          if (own[u]) {
+            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off[u]);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) rv[j][i] = rp[i];
-        }
+            for (int i = 0; i < 4; ++i) rv[u][i] = rp[i];
+          }
       }
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 26);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int64_t pix = ((int64_t)img * a.ho + hb * R + j) * a.wo + w;
+      for (int u = 0; u < 2; ++u) {
+        if (!own[u]) continue;
         const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) +
-                            (uint32_t)((acc * R + j) * a.block_n + half * cols);
+                            (uint32_t)((acc * R + jj[u]) * a.block_n + cc[u] * 32);
+        // two 16-column halves keep the live set within the 96 registers a
+        // thread gets at 576 threads per CTA
 #pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 32) {
-          if (c0 >= cols) break;
-          float v[32];
-          tmem_ld32(tb + c0, v);
+        for (int h = 0; h < 2; ++h) {
+          float v[16];
+          tmem_ld16(tb + h * 16, v);
           if (!img_ok) continue;
-          if (a.res && c0 > 0) {
-            uint4 r2[4];
-            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) +
-                                                             pix * a.N + col_base + c0);
+          const float4* bp = reinterpret_cast<const float4*>(a.bias + nb * a.block_n + cc[u] * 32 + h * 16);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) r2[i] = rp[i];
-            store32_bf16(a, pix * a.N + col_base + c0, col_base + c0, v, r2);
-          } else {
-            store32_bf16(a, pix * a.N + col_base + c0, col_base + c0, v, a.res ? rv[j] : nullptr);
+          for (int i = 0; i < 4; ++i) {
+            const float4 b = __ldg(bp + i);
+            v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+          }
+          if (a.res) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv[u][2 * h + i]);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[8 * i + e] += __bfloat162float(rb[e]);
+            }
+          }
+          act_inplace<16>(v, a.act, true);
+          uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off[u] + h * 16);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            __align__(16) __nv_bfloat16 o8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o8[e] = __float2bfloat16_rn(v[8 * i + e]);
+            op[i] = *reinterpret_cast<const uint4*>(o8);
           }
         }
       }
@@ -1253,7 +1282,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
       attr_halo = true;
     }
     int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
-    tc::tc_conv_halo_kernel<<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
+    tc::tc_conv_halo_kernel<<<grid, tc::HALO16_THREADS, smem, s>>>(maps, a);
     C3B_CHECK_CUDA(cudaGetLastError());
     return C3B_OK;
   }
