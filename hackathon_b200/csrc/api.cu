@@ -72,6 +72,9 @@ static const NameEntry kNames[] = {
     {"stem_im2col_bf16", C3B_K_STEM_IM2COL}, {"global_avgpool_nhwc", C3B_K_GAP_NHWC},
     {"stem_conv_bias_act_bf16", C3B_K_STEM_CONV},
     {"layout_copy", C3B_K_COPY},
+    // fp8 precision path (names the reference's policy emits but cannot execute)
+    {"quantize_e4m3_rows", C3B_K_QUANT_E4M3}, {"matmul_f8", C3B_K_GEMM_FP8},
+    {"gemm_bias_act_f8", C3B_K_GEMM_FP8},
 };
 
 static int find_name(const std::string& n) {
@@ -220,6 +223,18 @@ int dispatch(int kid, const c3b_tensor* in, int n_in, const c3b_tensor* out, int
       if ((rc = get_params(params, len, p))) return rc;
       C3B_REQUIRE(n_out == 1, "stem conv: one output");
       return launch_stem_conv(in, n_in, out[0], p, s);
+    }
+    case C3B_K_QUANT_E4M3: {
+      c3b_quant_params p;
+      if ((rc = get_params(params, len, p))) return rc;
+      C3B_REQUIRE(n_in == 1 && n_out == 2, "quantize e4m3: x -> q, scale");
+      return launch_quant_e4m3(in[0], out[0], out[1], p, s);
+    }
+    case C3B_K_GEMM_FP8: {
+      c3b_gemm_tc_params p;
+      if ((rc = get_params(params, len, p))) return rc;
+      C3B_REQUIRE(n_out == 1, "fp8 gemm: one output");
+      return launch_gemm_fp8(in, n_in, out[0], p, s);
     }
     case C3B_K_GAP_NHWC: {
       c3b_gap_params p;

@@ -67,6 +67,9 @@ struct TcArgs {
   int bres;  // 1: all weight taps resident in shared memory for the whole kernel
   // row-ring mode (tc_conv_rowring_kernel)
   int segs, seg_rows, ring, row_bytes, n_items;
+  // fp8 GEMM (tc_gemm_kernel<true>): per-row scale of A, per-column scale of B
+  const float* a_scale;
+  const float* b_scale;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -183,6 +186,21 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
 }
 
+// e4m3 x e4m3 -> f32 (kind::f8f6f4, K = 32 per instruction: 32 bytes, the
+// same byte step as a bf16 K = 16 instruction).
+__device__ __forceinline__ void mma_e4m3(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accum) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+
+// Instruction descriptor for kind::f8f6f4: D = f32, A = B = E4M3 (format 0), K-major.
+__host__ __device__ constexpr uint32_t instr_desc_e4m3(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -262,8 +280,19 @@ __device__ __forceinline__ void load_res32(const TcArgs& a, int64_t off, uint4* 
   }
 }
 
-// +bias -> +residual -> act -> store 32 columns of one output row (bf16 or f32).
-__device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t col0, float* v, const uint4* r) {
+// (x row scale x column scale) -> +bias -> +residual -> act -> store 32 columns
+// of one output row (bf16 or f32).  The scales are the fp8 GEMM's dequantisation.
+__device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t col0, float* v, const uint4* r,
+                                         float rs = 1.0f) {
+  if (a.b_scale) {
+    const float4* sp = reinterpret_cast<const float4*>(a.b_scale + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 c = __ldg(sp + i);
+      v[4 * i] = v[4 * i] * rs * c.x; v[4 * i + 1] = v[4 * i + 1] * rs * c.y;
+      v[4 * i + 2] = v[4 * i + 2] * rs * c.z; v[4 * i + 3] = v[4 * i + 3] * rs * c.w;
+    }
+  }
   if (a.bias) {
     const float4* bp = reinterpret_cast<const float4*>(a.bias + col0);
 #pragma unroll
@@ -306,7 +335,12 @@ __device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t c
   }
 }
 
+// F8: operands are e4m3 (128 elements per 128-byte K block, kind::f8f6f4);
+// otherwise bf16 (64 elements per block, kind::f16).  The shared-memory layout
+// and descriptor arithmetic are the same bytes either way.
+template <bool F8>
 __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
+  constexpr int KEL = F8 ? 128 : BK;  // elements per K block (one 128-byte row)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled stages.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -373,8 +407,8 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
           uint8_t* dA = sa + (size_t)stage * a_bytes;
           uint8_t* dB = sb + (size_t)stage * b_bytes;
           if (!a.conv) {
-            tma_load_2d(dA, &maps.a[0], &full[stage], kb * BK, m0);
-            tma_load_2d(dB, &maps.b, &full[stage], kb * BK, n0);
+            tma_load_2d(dA, &maps.a[0], &full[stage], kb * KEL, m0);
+            tma_load_2d(dB, &maps.b, &full[stage], kb * KEL, n0);
           } else {
             const int tap = kb / a.cblocks, cb = kb % a.cblocks;
             const int r = tap / a.ksz, s = tap % a.ksz;
@@ -400,7 +434,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(BM, a.block_n);
+      const uint32_t idesc = F8 ? instr_desc_e4m3(BM, a.block_n) : instr_desc(BM, a.block_n);
       // stage descriptors = base descriptor + offset in 16-byte units
       const uint64_t ad0 = smem_desc(smem_u32(sa)), bd0 = smem_desc(smem_u32(sb));
       int stage = 0;
@@ -418,8 +452,12 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
           const uint64_t ad = ad0 + (uint64_t)stage * (a_bytes >> 4);
           const uint64_t bd = bd0 + (uint64_t)stage * (b_bytes >> 4);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {  // four 32-byte K steps per 128-byte row
+            if (F8)
+              mma_e4m3(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
           mma_commit(&empty[stage]);
           if (++stage == stages) { stage = 0; phase ^= 1; }
         }
@@ -442,6 +480,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
       const int64_t row = (int64_t)mb * BM + q * 32 + lane;
       const int64_t col_base = (int64_t)nb * a.block_n + half * cols;
       const bool row_ok = row < a.M && col_base < a.N;
+      const float rs = (F8 && row_ok) ? __ldg(a.a_scale + row) : 1.0f;
       // Residual chunks are software-pipelined one chunk ahead (chunk 0 before
       // the accumulator wait), so their load latency hides behind the
       // previous chunk's TMEM load, math and stores.
@@ -459,7 +498,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
         tmem_ld32(tbase + c0, v);
         if (row_ok && col_base + c0 < a.N) {
           const int64_t off = row * a.N + col_base + c0;
-          finish32(a, off, col_base + c0, v, a.res ? rcur : nullptr);
+          finish32(a, off, col_base + c0, v, a.res ? rcur : nullptr, rs);
         }
         if (more) {
 #pragma unroll
@@ -1049,11 +1088,12 @@ static EncodeTiledFn get_encode() {
 }
 
 static int encode(CUtensorMap* m, void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                  const uint32_t* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+                  const uint32_t* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
+                  CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   EncodeTiledFn fn = get_encode();
   if (!fn) return fail(C3B_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, base, (const cuuint64_t*)dims,
+  CUresult r = fn(m, dt, (cuuint32_t)rank, base, (const cuuint64_t*)dims,
                   (const cuuint64_t*)strides_bytes, (const cuuint32_t*)box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(C3B_E_INVALID, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
   return C3B_OK;
@@ -1067,22 +1107,30 @@ static int pick_block_n(int64_t N, int requested) {
   return 128;
 }
 
-static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s) {
-  const size_t stage_bytes = (size_t)tc::BM * tc::BK * 2 + (size_t)a.block_n * tc::BK * 2;
+static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s, bool f8 = false) {
+  const size_t stage_bytes = (size_t)tc::BM * 128 + (size_t)a.block_n * 128;  // one 128-byte K row per operand row
   const size_t budget = 200 * 1024;
   int stages = (int)(budget / stage_bytes);
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(C3B_E_INVALID, "tc gemm: tile does not fit in shared memory");
   a.stages = stages;
   const size_t smem = 1024 + stages * stage_bytes + (2 * stages + 4) * 8 + 16;
-  static bool attr_set = false;
-  if (!attr_set) {
-    C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    attr_set = true;
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[f8]) {
+    if (f8)
+      C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          227 * 1024));
+    else
+      C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          227 * 1024));
+    attr_set[f8] = true;
   }
   int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
   if (grid < 1) return C3B_OK;
-  tc::tc_gemm_kernel<<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
+  if (f8)
+    tc::tc_gemm_kernel<true><<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
+  else
+    tc::tc_gemm_kernel<false><<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
@@ -1149,6 +1197,51 @@ int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
     if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box))) return rc;
   }
   return launch_tc(maps, a, s);
+}
+
+int launch_gemm_fp8(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p,
+                    cudaStream_t s) {
+  C3B_REQUIRE(n_in >= 4, "fp8 gemm: needs A, B, A row scales, B row scales");
+  C3B_REQUIRE(in[0].dtype == C3B_U8 && in[1].dtype == C3B_U8, "fp8 gemm: A and B must be e4m3 bytes (u8)");
+  C3B_REQUIRE(in[2].dtype == C3B_F32 && in[3].dtype == C3B_F32, "fp8 gemm: scales must be f32");
+  C3B_REQUIRE(p.K > 0 && p.K % 16 == 0, "fp8 gemm: K must be a positive multiple of 16");
+  C3B_REQUIRE(p.N > 0 && p.N % 32 == 0, "fp8 gemm: N must be a positive multiple of 32");
+  C3B_REQUIRE(p.M >= 0 && p.M < (int64_t)1 << 31, "fp8 gemm: M range");
+  C3B_REQUIRE(numel(in[0]) >= p.M * p.K && numel(in[1]) >= p.N * p.K, "fp8 gemm: operand extents");
+  C3B_REQUIRE(numel(in[2]) >= p.M && numel(in[3]) >= p.N, "fp8 gemm: scale extents");
+  C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0 && ((uintptr_t)in[3].ptr & 15) == 0,
+              "fp8 gemm: 16-byte alignment");
+  tc::TcArgs a;
+  memset(&a, 0, sizeof(a));
+  int rc = fill_epilogue(a, in, n_in, 4, p.bias_mode, p.has_residual, p.M, p.N, out);
+  if (rc) return rc;
+  if (p.M == 0) return C3B_OK;
+  a.M = p.M; a.N = p.N; a.K = p.K; a.act = p.act;
+  a.a_scale = (const float*)in[2].ptr;
+  a.b_scale = (const float*)in[3].ptr;
+  a.block_n = pick_block_n(p.N, p.block_n);
+  a.n_tiles_n = (int)((p.N + a.block_n - 1) / a.block_n);
+  a.n_tiles = (int)((p.M + tc::BM - 1) / tc::BM) * a.n_tiles_n;
+  a.k_blocks = (int)((p.K + 127) / 128);
+  tc::TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    uint64_t str[1] = {(uint64_t)p.K};
+    uint32_t box[2] = {128, tc::BM};
+    if ((rc = encode(&maps.a[0], in[0].ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_DATA_TYPE_UINT8)))
+      return rc;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
+    uint64_t str[1] = {(uint64_t)p.K};
+    uint32_t box[2] = {128, (uint32_t)a.block_n};
+    if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_DATA_TYPE_UINT8)))
+      return rc;
+  }
+  return launch_tc(maps, a, s, true);
 }
 
 int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_tc_params& p,

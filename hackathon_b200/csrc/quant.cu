@@ -1,0 +1,86 @@
+// Rowwise E4M3 quantisation for the fp8 precision path.
+//
+// One warp per row: pass 1 finds max|x| with 16-byte loads, pass 2 re-reads
+// the row (L1/L2-resident by then), divides by scale = amax / 448 and converts
+// pairs with the hardware round-to-nearest-even, saturating E4M3 conversion.
+// The division is IEEE (x / s), so a host restatement that divides in fp32 and
+// rounds to E4M3 gives the same bytes.
+#include <cuda_fp8.h>
+
+#include "common.cuh"
+
+namespace c3b {
+
+namespace {
+
+constexpr int QWARPS = 8;
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* v);
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float* v) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float* v) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(h[i]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(QWARPS * 32) quant_e4m3_kernel(const T* __restrict__ x, uint8_t* __restrict__ q,
+                                                                 float* __restrict__ scale, int64_t M, int64_t K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * QWARPS + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const T* xr = x + row * K;
+  float amax = 0.f;
+  for (int64_t k = (int64_t)lane * 8; k < K; k += 256) {
+    float v[8];
+    load8<T>(xr + k, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+  amax = warp_max(amax);
+  const float s = amax > 0.f ? amax / 448.0f : 1.0f;
+  if (lane == 0) scale[row] = s;
+  uint8_t* qr = q + row * K;
+  for (int64_t k = (int64_t)lane * 8; k < K; k += 256) {
+    float v[8];
+    load8<T>(xr + k, v);
+    __align__(8) __nv_fp8x2_storage_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = __nv_cvt_float2_to_fp8x2(make_float2(v[2 * i] / s, v[2 * i + 1] / s), __NV_SATFINITE, __NV_E4M3);
+    *reinterpret_cast<uint2*>(qr + k) = *reinterpret_cast<const uint2*>(o);
+  }
+}
+
+}  // namespace
+
+int launch_quant_e4m3(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor& scale, const c3b_quant_params& p,
+                      cudaStream_t s) {
+  C3B_REQUIRE(x.dtype == C3B_F32 || x.dtype == C3B_BF16, "quantize e4m3: input f32 or bf16");
+  C3B_REQUIRE(q.dtype == C3B_U8 && scale.dtype == C3B_F32, "quantize e4m3: outputs u8 and f32");
+  C3B_REQUIRE(p.M >= 0 && p.K > 0 && p.K % 16 == 0, "quantize e4m3: K must be a positive multiple of 16");
+  C3B_REQUIRE(numel(x) >= p.M * p.K && numel(q) >= p.M * p.K && numel(scale) >= p.M, "quantize e4m3: extents");
+  C3B_REQUIRE(((uintptr_t)x.ptr & 15) == 0 && ((uintptr_t)q.ptr & 7) == 0, "quantize e4m3: alignment");
+  if (p.M == 0) return C3B_OK;
+  const unsigned blocks = (unsigned)((p.M + QWARPS - 1) / QWARPS);
+  if (x.dtype == C3B_F32)
+    quant_e4m3_kernel<float><<<blocks, QWARPS * 32, 0, s>>>((const float*)x.ptr, (uint8_t*)q.ptr, (float*)scale.ptr,
+                                                            p.M, p.K);
+  else
+    quant_e4m3_kernel<__nv_bfloat16><<<blocks, QWARPS * 32, 0, s>>>((const __nv_bfloat16*)x.ptr, (uint8_t*)q.ptr,
+                                                                    (float*)scale.ptr, p.M, p.K);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
+
+}  // namespace c3b

@@ -192,3 +192,79 @@ def _retype(arr: Any, dt: int) -> Any:
 
 for _name in _prepared_names():
     register(_name)(_make(_name))
+
+
+# ------------------------------------------------------------- fp8 precision path
+#
+# The reference's policy selects fp8 for aligned GEMMs (c32/strategy.py:147-157)
+# and its decompositions then emit "matmul_f8" (c32/decompositions.py:18-27),
+# which the reference's lookup cannot resolve.  Here the name executes:
+# operands are quantised rowwise to E4M3 on the device (C3B_K_QUANT_E4M3) and
+# multiplied on tcgen05 kind::f8f6f4 (C3B_K_GEMM_FP8), fp32 output.  The
+# temporaries come from the caller's own array library (torch or CuPy) on the
+# caller's stream.
+
+def _scratch(like: Any, shape, np_dtype):
+    if _is_torch(like):
+        import torch
+        tmap = {np.uint8: torch.uint8, np.float32: torch.float32}
+        return torch.empty(tuple(shape), dtype=tmap[np_dtype], device=like.device)
+    import cupy
+    return cupy.empty(tuple(shape), dtype=np_dtype)
+
+
+@register("matmul_f8")
+def kernel_matmul_f8(inputs: List[Any], outputs: List[Any], params: Dict[str, Any],
+                     tuning: Optional[Dict[str, int]] = None) -> None:
+    a, b = inputs[0], inputs[1]
+    da, db = describe(a), describe(b)
+    if len(da.shape) != 2 or len(db.shape) != 2:
+        raise ValueError("matmul_f8: 2-D operands")
+    ta, tb = int(params.get("transA", 0)), int(params.get("transB", 0))
+    alpha = float(params.get("alpha", 1.0))
+    M, K = (da.shape[1], da.shape[0]) if ta else da.shape
+    N = db.shape[0] if tb else db.shape[1]
+    if (db.shape[1] if tb else db.shape[0]) != K:
+        raise ValueError("matmul_f8: inner dimensions differ")
+    if K % 16 or N % 32:
+        raise ValueError("matmul_f8: needs K % 16 == 0 and N % 32 == 0")
+    stream = _current_stream([a, b] + list(outputs))
+
+    def k_major(x, d, rows, cols, trans):
+        # [rows, cols] K-major operand; transposed through a strided copy when needed
+        if not trans:
+            return d
+        t = _scratch(x, (rows, cols), np.float32)
+        cp = L.CopyParams()
+        cp.in_offset = 0
+        cp.in_stride[0], cp.in_stride[1] = 1, rows
+        L.launch(L.K_COPY, [L.make_tensor(d.ptr, d.dtype, d.shape)], [L.make_tensor(int(t.data_ptr() if _is_torch(t)
+                 else t.data.ptr), L.F32, (rows, cols))], cp, stream)
+        keep.append(t)
+        return describe(t)
+
+    def ptr(t):
+        return int(t.data_ptr()) if _is_torch(t) else int(t.data.ptr)
+
+    keep: List[Any] = []
+    A = k_major(a, da, M, K, ta)             # A^T stored [K, M] -> [M, K]
+    Bk = k_major(b, db, N, K, not tb)        # B stored [K, N] -> [N, K]
+    qa, sa = _scratch(a, (M, K), np.uint8), _scratch(a, (M,), np.float32)
+    qb, sb = _scratch(a, (N, K), np.uint8), _scratch(a, (N,), np.float32)
+    for src, q, s, rows in ((A, qa, sa, M), (Bk, qb, sb, N)):
+        L.launch(L.K_QUANT_E4M3, [L.make_tensor(src.ptr, src.dtype, (rows, K))],
+                 [L.make_tensor(ptr(q), L.U8, (rows, K)), L.make_tensor(ptr(s), L.F32, (rows,))],
+                 L.QuantParams(rows, K), stream)
+    g = L.GemmTcParams()
+    g.M, g.N, g.K, g.bias_mode, g.act, g.has_residual, g.block_n = M, N, K, L.BIAS_NONE, 0, 0, 0
+    do = describe(outputs[0])
+    if do.numel < M * N or do.dtype != L.F32:
+        raise ValueError("matmul_f8: output must be an f32 arena of at least M*N elements")
+    L.launch(L.K_GEMM_FP8, [L.make_tensor(ptr(qa), L.U8, (M, K)), L.make_tensor(ptr(qb), L.U8, (N, K)),
+                            L.make_tensor(ptr(sa), L.F32, (M,)), L.make_tensor(ptr(sb), L.F32, (N,))],
+             [L.make_tensor(do.ptr, L.F32, (M, N))], g, stream)
+    if alpha != 1.0:
+        from .kernels import _ew_program
+        L.launch(L.K_EW, [L.make_tensor(do.ptr, L.F32, (M * N,))], [L.make_tensor(do.ptr, L.F32, (M * N,))],
+                 _ew_program([(L.OP_MUL_IMM, 0, 0)], [alpha]), stream)
+    outputs[0] = _view(outputs[0], (M, N))

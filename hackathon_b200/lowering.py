@@ -23,7 +23,12 @@ Patterns recognised on the unfused ONNX graph:
 Precision profiles: ``fp32`` keeps IEEE FP32 math everywhere (SIMT FFMA
 contractions); ``bf16`` runs contractions on tcgen05 with bf16 operands and
 fp32 accumulation, NHWC bf16 activations for convolutions, an fp32 residual
-stream and fp32 LayerNorm statistics for transformers, fp32 logits.
+stream and fp32 LayerNorm statistics for transformers, fp32 logits; ``fp8``
+is ``bf16`` with the linear layers the reference's precision policy marks fp8
+(aligned GEMMs with K, N >= 64: c32/strategy.py:147-157) run as rowwise-scaled
+E4M3 GEMMs — a quantisation step for the activation rows, E4M3 weights with
+per-output-row scales, tcgen05 ``kind::f8f6f4`` with fp32 accumulation and the
+two scales applied in the epilogue.
 """
 
 from __future__ import annotations
@@ -53,7 +58,7 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 class _State:
     def __init__(self, graph: ModelGraph, batch: int, profile: str):
-        if profile not in ("fp32", "bf16"):
+        if profile not in ("fp32", "bf16", "fp8"):
             raise ValueError(f"unknown precision profile {profile!r}")
         self.g = graph
         self.batch = batch
@@ -395,7 +400,7 @@ def _gemm_tc_launch(d: Dict[str, Desc], x, w, b, out, M, N, K, act, res=None):
 
 
 def _emit(st: _State, op: dict) -> None:
-    P, B, bf = st.prog, st.batch, st.profile == "bf16"
+    P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp8")
     k = op["kind"]
     if k == "conv":
         x = st.t(op["x"])
@@ -558,7 +563,36 @@ def _emit(st: _State, op: dict) -> None:
         use_tc = bf and N % 32 == 0 and K % 64 == 0 and P.tensors[x].dtype == L.BF16
         bname = st.weight("bias", (op["b"] * op.get("beta", 1.0)).astype(np.float32), L.F32) \
             if op["b"] is not None else None
-        if use_tc:
+        # fp8 per the reference policy for GEMMs (c32/strategy.py:150-157)
+        use_f8 = (use_tc and st.profile == "fp8" and N % 16 == 0 and K % 16 == 0 and K >= 64 and N >= 64
+                  and op.get("alpha", 1.0) == 1.0)
+        if use_f8:
+            from .fp8 import quant_rows_e4m3
+            wq, ws = quant_rows_e4m3(w)
+            wqn = st.weight("linear_e4m3", wq, L.U8)
+            wsn = st.weight("linear_e4m3_scale", ws, L.F32)
+            odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else L.BF16
+            P.add_tensor(out, (M, N), odt)
+            xq, xs = f"{out}:xq", f"{out}:xs"
+            P.add_tensor(xq, (M, K), L.U8)
+            P.add_tensor(xs, (M,), L.F32)
+
+            def build_q(d, x=x, xq=xq, xs=xs, M=M, K=K):
+                return [Launch(L.K_QUANT_E4M3, [d[x].t((M, K))], [d[xq].t(), d[xs].t()], L.QuantParams(M, K))]
+            P.add_step("quant_e4m3", [x], [xq, xs], build_q, 0.0)
+
+            def build(d, xq=xq, xs=xs, wqn=wqn, wsn=wsn, bname=bname, out=out, M=M, N=N, K=K, act=op["act"],
+                      res=res):
+                g = L.GemmTcParams()
+                g.M, g.N, g.K = M, N, K
+                g.bias_mode = L.BIAS_COL if bname else L.BIAS_NONE
+                g.act, g.has_residual, g.block_n = act, int(res is not None), 0
+                ins = [d[xq].t(), d[wqn].t(), d[xs].t(), d[wsn].t()] + ([d[bname].t()] if bname else []) + \
+                    ([d[res].t((M, N))] if res else [])
+                return [Launch(L.K_GEMM_FP8, ins, [d[out].t((M, N))], g)]
+            P.add_step("gemm_fp8", [xq, xs, wqn, wsn] + ([bname] if bname else []) + ([res] if res else []), [out],
+                       build, flops)
+        elif use_tc:
             if op.get("alpha", 1.0) != 1.0:
                 raise NotImplementedError("tc linear: alpha != 1")
             wname = st.weight("linear", bf16_bits(w), L.BF16)

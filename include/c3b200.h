@@ -85,7 +85,9 @@ enum {
   C3B_K_STEM_IM2COL = 15,/* NCHW f32 -> bf16 [N*Ho*Wo, Kpad] patch matrix */
   C3B_K_GAP_NHWC = 16,   /* NHWC mean over H,W -> [N, C]                  */
   C3B_K_STEM_CONV = 17,  /* direct small-Cin conv NCHW f32 -> NHWC bf16    */
-  C3B_K_COUNT = 18
+  C3B_K_QUANT_E4M3 = 18, /* rowwise e4m3 quantisation (fp8 precision path) */
+  C3B_K_GEMM_FP8 = 19,   /* e4m3 x e4m3 tcgen05 GEMM, scaled epilogue      */
+  C3B_K_COUNT = 20
 };
 
 /* --- C3B_K_EW: out = program(in0..in5) with NumPy broadcasting.
@@ -235,6 +237,22 @@ typedef struct {
   c3b_stem_params geom;
   int32_t cout, act;
 } c3b_stem_conv_params;
+
+/* --- C3B_K_QUANT_E4M3: x [M,K] f32|bf16 -> q [M,K] u8 (OCP E4M3 bytes) and
+ * scale [M] f32: scale[m] = max|x[m,:]| / 448 (1 for an all-zero row),
+ * q[m,k] = e4m3(x[m,k] / scale[m]) rounded to nearest even, saturating.
+ * K % 16 == 0.  No reference counterpart: the reference policy names fp8
+ * (c32/strategy.py:124-160) but has no fp8 kernel. */
+typedef struct {
+  int64_t M, K;
+} c3b_quant_params;
+
+/* --- C3B_K_GEMM_FP8: C = (A·Bᵀ) * a_scale[m] * b_scale[n] (+ bias[n]) (+ residual)
+ * then act, with A [M,K] and B [N,K] e4m3 bytes (both K-major) from
+ * C3B_K_QUANT_E4M3, fp32 accumulation in TMEM.  inputs: A, B, a_scale f32 [M],
+ * b_scale f32 [N], [bias f32 [N]], [residual [M,N] f32|bf16]; output f32|bf16.
+ * Parameters: c3b_gemm_tc_params.  K % 16 == 0, N % 32 == 0.  Executes the
+ * reference's "matmul_f8" name (which the reference cannot run). */
 
 /* --- C3B_K_GAP_NHWC: x [N, HW, C] -> y [N, C] f32 */
 typedef struct {

@@ -394,3 +394,90 @@ def test_skinny_gemm(torch_cuda):
     w2 = randn(512, 7)
     outs = call("fused_gemm_epilogue_f32", [dev(t, a), dev(t, w2)], [arena(t, 2100)], {"alpha": 0.5})
     assert rel(host(outs[0]), O.gemm_epilogue(a, w2, None, alpha=0.5)) < RTOL
+
+
+# ------------------------------------------------------------- fp8 precision path
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("M,K", [(37, 64), (300, 1024), (5, 4096), (129, 16)])
+def test_quant_e4m3_bit_exact(torch_cuda, dt, M, K):
+    """CUDA rowwise E4M3 quantiser == the oracle's restatement, byte for byte."""
+    import torch
+    from hackathon_b200 import _lib as L
+    from oracle import fp8 as F
+    x = randn(M, K) * np.float32(10.0) ** RNG.integers(-4, 3, size=(M, 1)).astype(np.float32)
+    x[0] = 0.0  # an all-zero row
+    if dt == "bf16":
+        x = round_bf16(x)
+        xd = _bf16(torch, x)
+    else:
+        xd = dev(torch, x)
+    q = torch.empty((M, K), dtype=torch.uint8, device="cuda")
+    s = torch.empty((M,), dtype=torch.float32, device="cuda")
+    L.launch(L.K_QUANT_E4M3, [L.make_tensor(xd.data_ptr(), L.F32 if dt == "f32" else L.BF16, (M, K))],
+             [L.make_tensor(q.data_ptr(), L.U8, (M, K)), L.make_tensor(s.data_ptr(), L.F32, (M,))],
+             L.QuantParams(M, K), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    qr, sr = F.quant_rows(x)
+    assert np.array_equal(host(s), sr)
+    assert np.array_equal(host(q), qr)
+
+
+@pytest.mark.parametrize("M,N,K,act,res,odt", [(128, 64, 64, 0, 0, "f32"), (300, 128, 192, 1, 0, "bf16"),
+                                               (1000, 256, 512, 2, 1, "f32"), (257, 96, 80, 0, 1, "bf16"),
+                                               (2048, 512, 1024, 1, 1, "f32")])
+def test_gemm_fp8(torch_cuda, M, N, K, act, res, odt):
+    """tcgen05 kind::f8f6f4 GEMM against the oracle on the same E4M3 bytes and
+    scales: the products of two E4M3 values are exact in fp32, so the only
+    difference is fp32 accumulation order (f32 output) or bf16 output rounding."""
+    import torch
+    from hackathon_b200 import _lib as L
+    from oracle import fp8 as F
+    a = randn(M, K)
+    w = randn(N, K) * np.float32(0.05)
+    qa, sa = F.quant_rows(a)
+    qb, sb = F.quant_rows(w)
+    bias = randn(N)
+    r = randn(M, N) if res else None
+    ref = F.gemm_fp8(qa, sa, qb, sb, bias)
+    if res:
+        ref = ref + (round_bf16(r) if odt == "bf16" else r)
+    if act == 1:
+        ref = np.maximum(ref, 0)
+    elif act == 2:
+        ref = O.gelu_erf(ref.astype(np.float32))
+    g = L.GemmTcParams()
+    g.M, g.N, g.K, g.bias_mode, g.act, g.has_residual, g.block_n = M, N, K, L.BIAS_COL, act, res, 0
+    tq, tqb, tsa, tsb, tb = dev(torch, qa), dev(torch, qb), dev(torch, sa), dev(torch, sb), dev(torch, bias)
+    ins = [L.make_tensor(tq.data_ptr(), L.U8, (M, K)), L.make_tensor(tqb.data_ptr(), L.U8, (N, K)),
+           L.make_tensor(tsa.data_ptr(), L.F32, (M,)), L.make_tensor(tsb.data_ptr(), L.F32, (N,)),
+           L.make_tensor(tb.data_ptr(), L.F32, (N,))]
+    if res:
+        tr = _bf16(torch, round_bf16(r)) if odt == "bf16" else dev(torch, r)
+        ins.append(L.make_tensor(tr.data_ptr(), L.BF16 if odt == "bf16" else L.F32, (M, N)))
+    out = torch.empty((M, N), dtype=torch.bfloat16 if odt == "bf16" else torch.float32, device="cuda")
+    L.launch(L.K_GEMM_FP8, ins, [L.make_tensor(out.data_ptr(), L.BF16 if odt == "bf16" else L.F32, (M, N))], g,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    got = out.float().cpu().numpy()
+    assert rel(got, ref) < (8e-3 if odt == "bf16" else 2e-5)
+
+
+def test_matmul_f8_registry_name(torch_cuda):
+    """The reference name "matmul_f8" (which the reference's lookup cannot
+    resolve) runs the fp8 path through the registry: f32 operands are
+    quantised rowwise on the device and multiplied on tcgen05."""
+    import torch
+    from hackathon_b200.kernel_registry import lookup
+    from oracle import fp8 as F
+    M, K, N = 96, 128, 64
+    a, b = randn(M, K), randn(K, N)
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    outs = [out]
+    lookup("matmul_f8")([dev(torch, a), dev(torch, b)], outs, {"transA": 0, "transB": 0}, None)
+    torch.cuda.synchronize()
+    qa, sa = F.quant_rows(a)
+    qb, sb = F.quant_rows(np.ascontiguousarray(b.T))
+    ref = F.gemm_fp8(qa, sa, qb, sb)
+    assert rel(host(outs[0]).reshape(M, N), ref) < 2e-5

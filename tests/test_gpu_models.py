@@ -170,3 +170,23 @@ def test_stream_matches_single_passes(wl, model):
     # the second stream reuses the captured graphs and staging buffers
     outs2, _ = ex.stream(batches[:2])
     assert np.array_equal(outs2[1]["logits"], outs[1]["logits"])
+
+
+@pytest.mark.parametrize("model,batch", [("tx_small", 8), ("tx_large", 2)])
+def test_tx_fp8_profile(wl, model, batch):
+    """fp8 profile (E4M3 GEMMs where the reference policy marks fp8) against
+    the fp32 oracle.  E4M3 keeps 3 mantissa bits, so per-GEMM relative errors
+    are ~2^-5; the gate is the logits' scaled error and no argmax flip on rows
+    whose top-2 gap exceeds twice that error."""
+    g = wl.BUILDERS[model]()
+    feeds = wl.make_inputs(g, batch)
+    ref = run_graph(g, feeds)["logits"]
+    ex, out = _run_program(g, batch, "fp8", feeds)
+    labels = {s.label for s in ex.prog.steps}
+    assert "gemm_fp8" in labels and "quant_e4m3" in labels
+    abs_err, n_flip, n_real_flip = _bf16_gate(out, ref)
+    print(f"{model} fp8: scaled max abs err {abs_err:.3e}, argmax flips {n_flip} (non-tie {n_real_flip})")
+    assert np.isfinite(out).all()
+    assert abs_err < 0.15
+    assert n_real_flip == 0
+    ex.native.close()

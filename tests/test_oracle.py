@@ -73,3 +73,40 @@ def test_oracle_fused_restatements_agree_with_unfused():
 def test_erf_approximation_error_bound():
     x = np.linspace(-4, 4, 4001, dtype=np.float32)
     assert np.abs(O.erf_as(x) - O.erf_exact(x)).max() < 2e-6  # A&S 7.1.26 bound 1.5e-7 + fp32 rounding
+
+
+def test_e4m3_encoder_pinned():
+    """The fp8 oracle's E4M3 encoder against the OCP E4M3 code points and against
+    torch's float8_e4m3fn conversion (round to nearest even), exact ties included."""
+    import torch
+    from oracle import fp8 as F
+    points = {0.0: 0x00, 1.0: 0x38, 2.0: 0x40, 448.0: 0x7E, 2.0 ** -6: 0x08, 2.0 ** -9: 0x01, -2.0: 0xC0,
+              0.5: 0x30, 1.125: 0x39, 240.0: 0x77, 7 * 2.0 ** -9: 0x07, 1000.0: 0x7E, -1e6: 0xFE}
+    for v, b in points.items():
+        assert int(F.e4m3_encode(np.float32(v))) == b, v
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(20000).astype(np.float32) * s for s in (1e-3, 0.05, 1.0, 30.0, 200.0)])
+    vals = F.e4m3_decode(np.arange(256, dtype=np.uint8))
+    vals = np.unique(vals[np.isfinite(vals)])
+    mids = ((vals[1:] + vals[:-1]) / 2).astype(np.float32)  # exact ties
+    x = np.clip(np.concatenate([x, mids, -mids]), -448, 448).astype(np.float32)
+    ref = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(F.e4m3_encode(x), ref)
+    # decode(encode(v)) == v for every finite code
+    codes = np.arange(256, dtype=np.uint8)
+    fin = np.isfinite(F.e4m3_decode(codes))
+    assert np.array_equal(F.e4m3_encode(F.e4m3_decode(codes[fin]).astype(np.float32)), codes[fin])
+
+
+def test_fp8_rowwise_scheme():
+    from oracle import fp8 as F
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((7, 64)).astype(np.float32) * np.array([1e-4, 1, 10, 100, 0, 3, 1e3], np.float32)[:, None]
+    q, s = F.quant_rows(x)
+    assert s[4] == 1.0 and not F.e4m3_decode(q[4]).any()  # all-zero row (signed zeros keep their sign bit)
+    d = F.e4m3_decode(q) * s[:, None]
+    rows = [i for i in range(7) if i != 4]
+    # E4M3 keeps 3 mantissa bits: relative error <= 2^-4 for normal values
+    big = np.abs(x) > np.max(np.abs(x), axis=1, keepdims=True) * 2.0 ** -6 * 1.01
+    assert np.all(np.abs(d - x)[rows][big[rows]] <= np.abs(x)[rows][big[rows]] * 2.0 ** -4 + 1e-30)
+    assert np.max(np.abs(q[rows].astype(np.int64) & 0x7F)) == 0x7E  # the row maximum maps to 448
