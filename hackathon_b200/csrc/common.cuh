@@ -105,6 +105,27 @@ __device__ __forceinline__ float gelu_as_fast(float x) {
   return 0.5f * x * (1.0f + erf_v);
 }
 
+// Two-wide GELU for bf16 outputs: the same A&S 7.1.26 evaluation as
+// gelu_as_fast with the multiply-adds issued as Blackwell's packed fp32 pairs
+// (__ffma2_rn / __fmul2_rn), which halves the FMA-pipe instructions of the
+// epilogues that run it on every output element.
+__device__ __forceinline__ float2 gelu2_as_fast(float2 x) {
+  const float2 z = make_float2(fabsf(x.x) * 0.70710678118654752f, fabsf(x.y) * 0.70710678118654752f);
+  const float2 d = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), z, make_float2(1.0f, 1.0f));
+  const float2 t = make_float2(__fdividef(1.0f, d.x), __fdividef(1.0f, d.y));
+  float2 p = __ffma2_rn(t, make_float2(1.061405429f, 1.061405429f), make_float2(-1.453152027f, -1.453152027f));
+  p = __ffma2_rn(t, p, make_float2(1.421413741f, 1.421413741f));
+  p = __ffma2_rn(t, p, make_float2(-0.284496736f, -0.284496736f));
+  p = __ffma2_rn(t, p, make_float2(0.254829592f, 0.254829592f));
+  p = __fmul2_rn(t, p);
+  const float2 zz = __fmul2_rn(z, z);
+  const float2 ne = make_float2(-__expf(-zz.x), -__expf(-zz.y));
+  const float2 e = __ffma2_rn(p, ne, make_float2(1.0f, 1.0f));  // erf(|x| / sqrt 2)
+  const float2 er = make_float2(x.x < 0.f ? -e.x : e.x, x.y < 0.f ? -e.y : e.y);
+  const float2 hx = __fmul2_rn(x, make_float2(0.5f, 0.5f));
+  return __ffma2_rn(hx, er, hx);  // 0.5 x (1 + erf)
+}
+
 // Activation over a register array, chosen once per call (a warp-uniform
 // branch): a per-element select lets the compiler evaluate every variant,
 // erff included, for every element — which cost the tcgen05 GEMM epilogues a
@@ -117,7 +138,12 @@ __device__ __forceinline__ void act_inplace(float* v, int act, bool bf16_out) {
   } else if (act == C3B_ACT_GELU) {
     if (bf16_out) {
 #pragma unroll
-      for (int i = 0; i < N; ++i) v[i] = gelu_as_fast(v[i]);
+      for (int i = 0; i + 1 < N; i += 2) {
+        const float2 g = gelu2_as_fast(make_float2(v[i], v[i + 1]));
+        v[i] = g.x;
+        v[i + 1] = g.y;
+      }
+      if (N & 1) v[N - 1] = gelu_as_fast(v[N - 1]);
     } else {
 #pragma unroll
       for (int i = 0; i < N; ++i) v[i] = gelu_erf(v[i]);

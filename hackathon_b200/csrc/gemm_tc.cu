@@ -35,7 +35,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int NUM_THREADS = 192;
 constexpr int HALO_THREADS = 320;  // producer, MMA, 8 epilogue warps
-constexpr int HALO16_THREADS = 576;  // producer, MMA, 16 epilogue warps (tc_conv_halo_kernel)
+constexpr int HALO16_THREADS = 576;  // producer, MMA, 16 epilogue warps (tc_gemm_kernel, tc_conv_halo_kernel)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 
 struct __align__(64) TmaMaps {
@@ -335,11 +335,76 @@ __device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t c
   }
 }
 
+// Residual of 16 consecutive columns (bf16: 32 bytes, f32: 64 bytes) as raw words.
+__device__ __forceinline__ void load_res16(const TcArgs& a, int64_t off, uint4* r) {
+  if (a.dt_res == C3B_BF16) {
+    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off);
+    r[0] = rp[0]; r[1] = rp[1];
+  } else {
+    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const float*>(a.res) + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = rp[i];
+  }
+}
+
+// 16 columns of one output row: (x row scale x column scale) -> +bias ->
+// +residual -> act -> store (bf16 or f32).
+__device__ __forceinline__ void finish16(const TcArgs& a, int64_t off, int64_t col0, float* v, const uint4* r,
+                                         float rs) {
+  // pairwise (packed fp32) arithmetic: v2[i] holds columns 2i, 2i+1
+  float2* v2 = reinterpret_cast<float2*>(v);
+  if (a.b_scale) {
+    const float4* sp = reinterpret_cast<const float4*>(a.b_scale + col0);
+    const float2 rr = make_float2(rs, rs);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 c = __ldg(sp + i);
+      v2[2 * i] = __fmul2_rn(v2[2 * i], __fmul2_rn(rr, make_float2(c.x, c.y)));
+      v2[2 * i + 1] = __fmul2_rn(v2[2 * i + 1], __fmul2_rn(rr, make_float2(c.z, c.w)));
+    }
+  }
+  if (a.bias) {
+    const float4* bp = reinterpret_cast<const float4*>(a.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 b = __ldg(bp + i);
+      v2[2 * i] = __fadd2_rn(v2[2 * i], make_float2(b.x, b.y));
+      v2[2 * i + 1] = __fadd2_rn(v2[2 * i + 1], make_float2(b.z, b.w));
+    }
+  }
+  if (r) {
+    if (a.dt_res == C3B_BF16) {
+      const __nv_bfloat162* rb = reinterpret_cast<const __nv_bfloat162*>(r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v2[i] = __fadd2_rn(v2[i], __bfloat1622float2(rb[i]));
+    } else {
+      const float2* rf = reinterpret_cast<const float2*>(r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v2[i] = __fadd2_rn(v2[i], rf[i]);
+    }
+  }
+  act_inplace<16>(v, a.act, a.dt_out == C3B_BF16);
+  if (a.dt_out == C3B_BF16) {
+    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      __align__(16) __nv_bfloat162 o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = __float22bfloat162_rn(v2[4 * i + j]);
+      op[i] = *reinterpret_cast<const uint4*>(o);
+    }
+  } else {
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) op[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+}
+
 // F8: operands are e4m3 (128 elements per 128-byte K block, kind::f8f6f4);
 // otherwise bf16 (64 elements per block, kind::f16).  The shared-memory layout
 // and descriptor arithmetic are the same bytes either way.
 template <bool F8>
-__global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
+__global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
   constexpr int KEL = F8 ? 128 : BK;  // elements per K block (one 128-byte row)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled stages.
@@ -368,7 +433,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 8);
+      mbar_init(&tempty[i], 16);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -467,42 +532,40 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_gemm_kernel(const __grid_c
       }
     }
   } else {
-    // ---------------- epilogue warps 2..9: warp w reads TMEM lane quarter
-    // (w % 4) and one half of the tile's columns; the residual of the first
-    // 32-column chunk is prefetched before waiting for the accumulator.
+    // ---------------- epilogue warps 2..17: warp w drains TMEM lane quarter
+    // (w % 4) and one quarter of the tile's columns in 16-column chunks.  Four
+    // warps per quarter keep the issue slots busy (the epilogue runs ~30
+    // instructions per element with GELU and fp8 scales); 16-column chunks keep
+    // the live set within the 96 registers of a 576-thread CTA.  The residual
+    // is prefetched one chunk ahead.
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int cols = a.block_n >> 1;
+    const int part = (warp - 2) >> 2;
+    const int cols = a.block_n >> 2;  // 16, 32 or 64 columns per warp
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
       const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
       const int64_t row = (int64_t)mb * BM + q * 32 + lane;
-      const int64_t col_base = (int64_t)nb * a.block_n + half * cols;
+      const int64_t col_base = (int64_t)nb * a.block_n + part * cols;
       const bool row_ok = row < a.M && col_base < a.N;
       const float rs = (F8 && row_ok) ? __ldg(a.a_scale + row) : 1.0f;
-      // Residual chunks are software-pipelined one chunk ahead (chunk 0 before
-      // the accumulator wait), so their load latency hides behind the
-      // previous chunk's TMEM load, math and stores.
-      uint4 rcur[8], rnext[8];
-      if (a.res && row_ok) load_res32(a, row * a.N + col_base, rcur);
+      uint4 rc[4], rn[4];
+      if (a.res && row_ok) load_res16(a, row * a.N + col_base, rc);
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 14);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.block_n + half * cols);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.block_n + part * cols);
 #pragma unroll 1
-      for (int c0 = 0; c0 < cols; c0 += 32) {
-        const bool more = a.res && row_ok && c0 + 32 < cols && col_base + c0 + 32 < a.N;
-        if (more) load_res32(a, row * a.N + col_base + c0 + 32, rnext);
-        float v[32];
-        tmem_ld32(tbase + c0, v);
-        if (row_ok && col_base + c0 < a.N) {
-          const int64_t off = row * a.N + col_base + c0;
-          finish32(a, off, col_base + c0, v, a.res ? rcur : nullptr, rs);
-        }
+      for (int c0 = 0; c0 < cols; c0 += 16) {
+        const bool more = a.res && row_ok && c0 + 16 < cols && col_base + c0 + 16 < a.N;
+        if (more) load_res16(a, row * a.N + col_base + c0 + 16, rn);
+        float v[16];
+        tmem_ld16(tbase + c0, v);
+        if (row_ok && col_base + c0 < a.N)
+          finish16(a, row * a.N + col_base + c0, col_base + c0, v, a.res ? rc : nullptr, rs);
         if (more) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) rcur[i] = rnext[i];
+          for (int i = 0; i < 4; ++i) rc[i] = rn[i];
         }
       }
       tc_fence_before();
@@ -1128,9 +1191,9 @@ static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s, boo
   int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
   if (grid < 1) return C3B_OK;
   if (f8)
-    tc::tc_gemm_kernel<true><<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
+    tc::tc_gemm_kernel<true><<<grid, tc::HALO16_THREADS, smem, s>>>(maps, a);
   else
-    tc::tc_gemm_kernel<false><<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
+    tc::tc_gemm_kernel<false><<<grid, tc::HALO16_THREADS, smem, s>>>(maps, a);
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
