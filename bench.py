@@ -40,6 +40,9 @@ WORKLOADS = {
     "tx_large_fp8": ("tx_large", 256, "fp8", "tok/s", "weak", 512,
                      "configs[4] shapes with the fp8 precision extension (E4M3 GEMMs where the reference policy "
                      "marks fp8, c32/strategy.py:147-157); not a BASELINE config"),
+    "tx_large_mixed": ("tx_large", 256, "mixed", "tok/s", "weak", 512,
+                       "configs[4] shapes with the reference policy's fp4/fp8 choices executed (W4A16 for the large "
+                       "constant-weight GEMMs, c32/strategy.py:146-157); not a BASELINE config"),
     "tx_small_fp32": ("tx_small", 64, "fp32", "tok/s", "strong", 128,
                       "BASELINE configs[2]: decoder d256 L4 H4 FFN1024 V4096 S128, batch 64"),
     "mlp_fp32": ("mlp", 256, "fp32", "samples/s", "strong", None, "BASELINE configs[0]: MLP 784-512-256-10"),

@@ -75,6 +75,9 @@ static const NameEntry kNames[] = {
     // fp8 precision path (names the reference's policy emits but cannot execute)
     {"quantize_e4m3_rows", C3B_K_QUANT_E4M3}, {"matmul_f8", C3B_K_GEMM_FP8},
     {"gemm_bias_act_f8", C3B_K_GEMM_FP8},
+    // W4A16 path (the policy's fp4 for constant-weight GEMMs)
+    {"quantize_fp4_groups", C3B_K_QUANT_FP4}, {"matmul_f4", C3B_K_GEMM_W4A16},
+    {"gemm_bias_act_w4a16", C3B_K_GEMM_W4A16},
 };
 
 static int find_name(const std::string& n) {
@@ -235,6 +238,18 @@ int dispatch(int kid, const c3b_tensor* in, int n_in, const c3b_tensor* out, int
       if ((rc = get_params(params, len, p))) return rc;
       C3B_REQUIRE(n_out == 1, "fp8 gemm: one output");
       return launch_gemm_fp8(in, n_in, out[0], p, s);
+    }
+    case C3B_K_QUANT_FP4: {
+      c3b_quant_params p;
+      if ((rc = get_params(params, len, p))) return rc;
+      C3B_REQUIRE(n_in == 1 && n_out == 2, "quantize fp4: w -> q, scale");
+      return launch_quant_fp4(in[0], out[0], out[1], p, s);
+    }
+    case C3B_K_GEMM_W4A16: {
+      c3b_gemm_tc_params p;
+      if ((rc = get_params(params, len, p))) return rc;
+      C3B_REQUIRE(n_out == 1, "w4a16 gemm: one output");
+      return launch_gemm_w4a16(in, n_in, out[0], p, s);
     }
     case C3B_K_GAP_NHWC: {
       c3b_gap_params p;

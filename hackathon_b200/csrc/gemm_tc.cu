@@ -25,6 +25,8 @@
 // an error in the device status word, stops issuing work, frees its TMEM and
 // returns, so the context stays usable.
 #include <cuda.h>
+#include <cuda_fp4.h>
+
 #include "common.cuh"
 
 namespace c3b {
@@ -67,7 +69,7 @@ struct TcArgs {
   int bres;  // 1: all weight taps resident in shared memory for the whole kernel
   // row-ring mode (tc_conv_rowring_kernel)
   int segs, seg_rows, ring, row_bytes, n_items;
-  // fp8 GEMM (tc_gemm_kernel<true>): per-row scale of A, per-column scale of B
+  // fp8 GEMM (tc_gemm_kernel<1>): per-row scale of A, per-column scale of B
   const float* a_scale;
   const float* b_scale;
 };
@@ -129,6 +131,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
           "r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 
@@ -400,24 +410,40 @@ __device__ __forceinline__ void finish16(const TcArgs& a, int64_t off, int64_t c
   }
 }
 
-// F8: operands are e4m3 (128 elements per 128-byte K block, kind::f8f6f4);
-// otherwise bf16 (64 elements per block, kind::f16).  The shared-memory layout
-// and descriptor arithmetic are the same bytes either way.
-template <bool F8>
+// MODE 0: bf16 A and B (64 elements per 128-byte K block, kind::f16).
+// MODE 1: e4m3 A and B (128 elements per K block, kind::f8f6f4); per-row and
+//         per-column scales in the epilogue.
+// MODE 2: W4A16 — bf16 A, B as packed FP4 E2M1 with an fp32 scale per 16 K
+//         elements.  TMA brings the packed tile (32 bytes per row per K block)
+//         and its scales; converter warps 10..17 expand them into the same
+//         128-byte-swizzled bf16 stage the MMA reads (kind::f16), and warps 2..9
+//         run the epilogue.
+// The shared-memory layout and descriptor arithmetic of A/B are the same bytes
+// in every mode.
+constexpr int W4_GROUP = 16;  // K elements per FP4 scale
+
+template <int MODE>
 __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
+  constexpr bool F8 = MODE == 1, W4 = MODE == 2;
   constexpr int KEL = F8 ? 128 : BK;  // elements per K block (one 128-byte row)
+  constexpr int EPIW = W4 ? 8 : 16;   // epilogue warps
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled stages.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stages = a.stages;
   const uint32_t a_bytes = BM * BK * 2;
   const uint32_t b_bytes = (uint32_t)a.block_n * BK * 2;
+  const uint32_t raw_bytes = W4 ? (uint32_t)a.block_n * (BK / 2) : 0u;                 // packed FP4
+  const uint32_t scl_bytes = W4 ? (uint32_t)a.block_n * (BK / W4_GROUP) * 4u : 0u;     // fp32 scales
   uint8_t* sa = smem;
   uint8_t* sb = smem + (size_t)stages * a_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + (size_t)stages * b_bytes);
+  uint8_t* sraw = sb + (size_t)stages * b_bytes;
+  uint8_t* sscl = sraw + (size_t)stages * raw_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sscl + (size_t)stages * scl_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + stages;
-  uint64_t* tfull = bars + 2 * stages;
+  uint64_t* bready = bars + 2 * stages;  // MODE 2: B stage expanded
+  uint64_t* tfull = bars + 3 * stages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -430,10 +456,11 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     for (int i = 0; i < stages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
+      mbar_init(&bready[i], 8);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 16);
+      mbar_init(&tempty[i], EPIW);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -468,13 +495,19 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
         }
         for (int kb = 0; kb < a.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 11)) goto producer_done;
-          mbar_arrive_tx(&full[stage], a_bytes + b_bytes);
           uint8_t* dA = sa + (size_t)stage * a_bytes;
           uint8_t* dB = sb + (size_t)stage * b_bytes;
-          if (!a.conv) {
+          if (W4) {
+            mbar_arrive_tx(&full[stage], a_bytes + raw_bytes + scl_bytes);
+            tma_load_2d(dA, &maps.a[0], &full[stage], kb * BK, m0);
+            tma_load_2d(sraw + (size_t)stage * raw_bytes, &maps.a[1], &full[stage], kb * (BK / 2), n0);
+            tma_load_3d(sscl + (size_t)stage * scl_bytes, &maps.a[2], &full[stage], 0, n0, kb);
+          } else if (!a.conv) {
+            mbar_arrive_tx(&full[stage], a_bytes + b_bytes);
             tma_load_2d(dA, &maps.a[0], &full[stage], kb * KEL, m0);
             tma_load_2d(dB, &maps.b, &full[stage], kb * KEL, n0);
           } else {
+            mbar_arrive_tx(&full[stage], a_bytes + b_bytes);
             const int tap = kb / a.cblocks, cb = kb % a.cblocks;
             const int r = tap / a.ksz, s = tap % a.ksz;
             int map = 0, ro, so;
@@ -512,7 +545,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * a.block_n);
         bool ok = true;
         for (int kb = 0; kb < a.k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, 13)) { ok = false; break; }
+          if (!mbar_wait(W4 ? &bready[stage] : &full[stage], phase, abort_flag, 13)) { ok = false; break; }
           tc_fence_after();
           const uint64_t ad = ad0 + (uint64_t)stage * (a_bytes >> 4);
           const uint64_t bd = bd0 + (uint64_t)stage * (b_bytes >> 4);
@@ -531,6 +564,42 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
+  } else if (W4 && warp >= 2 + EPIW) {
+    // ---------------- FP4 converters (warps 10..17): each K block of B is
+    // block_n rows x 64 elements; a unit is one row's 8-element chunk (4 packed
+    // bytes, one scale) written as 16 bf16 bytes at its 128-byte-swizzle slot.
+    const int ct = threadIdx.x - (2 + EPIW) * 32;  // 0..255
+    const int units = a.block_n * 8;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < a.k_blocks; ++kb) {
+        ok = mbar_wait(&full[stage], phase, abort_flag, 15);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        const uint8_t* raw = sraw + (size_t)stage * raw_bytes;
+        const float* scl = reinterpret_cast<const float*>(sscl + (size_t)stage * scl_bytes);
+        uint8_t* dst = sb + (size_t)stage * b_bytes;
+        for (int u = ct; u < units; u += 256) {
+          const int r = u >> 3, c = u & 7;
+          const uint32_t packed = *reinterpret_cast<const uint32_t*>(raw + r * 32 + c * 4);
+          const float sc = scl[r * (BK / W4_GROUP) + (c >> 1)];
+          const float2 s2 = make_float2(sc, sc);
+          __align__(16) __nv_bfloat162 o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((packed >> (8 * j)) & 0xFF), __NV_E2M1);
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+            o[j] = __float22bfloat162_rn(__fmul2_rn(f, s2));
+          }
+          *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bready[stage]);
+        if (++stage == stages) { stage = 0; phase ^= 1; }
+      }
+    }
   } else {
     // ---------------- epilogue warps 2..17: warp w drains TMEM lane quarter
     // (w % 4) and one quarter of the tile's columns in 16-column chunks.  Four
@@ -540,7 +609,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     // is prefetched one chunk ahead.
     const int q = warp & 3;
     const int part = (warp - 2) >> 2;
-    const int cols = a.block_n >> 2;  // 16, 32 or 64 columns per warp
+    const int cols = a.block_n / (EPIW / 4);  // columns per warp
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
@@ -1170,32 +1239,34 @@ static int pick_block_n(int64_t N, int requested) {
   return 128;
 }
 
-static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s, bool f8 = false) {
-  const size_t stage_bytes = (size_t)tc::BM * 128 + (size_t)a.block_n * 128;  // one 128-byte K row per operand row
+template <int MODE>
+static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s) {
+  // one 128-byte K row per operand row; MODE 2 adds the packed FP4 tile and its scales
+  size_t stage_bytes = (size_t)tc::BM * 128 + (size_t)a.block_n * 128;
+  if (MODE == 2) stage_bytes += (size_t)a.block_n * (tc::BK / 2) + (size_t)a.block_n * (tc::BK / tc::W4_GROUP) * 4;
   const size_t budget = 200 * 1024;
   int stages = (int)(budget / stage_bytes);
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(C3B_E_INVALID, "tc gemm: tile does not fit in shared memory");
   a.stages = stages;
-  const size_t smem = 1024 + stages * stage_bytes + (2 * stages + 4) * 8 + 16;
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[f8]) {
-    if (f8)
-      C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          227 * 1024));
-    else
-      C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          227 * 1024));
-    attr_set[f8] = true;
+  const size_t smem = 1024 + stages * stage_bytes + (3 * stages + 4) * 8 + 16;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        227 * 1024));
+    attr_set = true;
   }
   int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
   if (grid < 1) return C3B_OK;
-  if (f8)
-    tc::tc_gemm_kernel<true><<<grid, tc::HALO16_THREADS, smem, s>>>(maps, a);
-  else
-    tc::tc_gemm_kernel<false><<<grid, tc::HALO16_THREADS, smem, s>>>(maps, a);
+  tc::tc_gemm_kernel<MODE><<<grid, tc::HALO16_THREADS, smem, s>>>(maps, a);
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
+}
+
+static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s, int mode = 0) {
+  if (mode == 1) return launch_tc_mode<1>(maps, a, s);
+  if (mode == 2) return launch_tc_mode<2>(maps, a, s);
+  return launch_tc_mode<0>(maps, a, s);
 }
 
 static int fill_epilogue(tc::TcArgs& a, const c3b_tensor* in, int n_in, int first_extra, int bias_mode,
@@ -1304,7 +1375,56 @@ int launch_gemm_fp8(const c3b_tensor* in, int n_in, const c3b_tensor& out, const
                      CU_TENSOR_MAP_DATA_TYPE_UINT8)))
       return rc;
   }
-  return launch_tc(maps, a, s, true);
+  return launch_tc(maps, a, s, 1);
+}
+
+int launch_gemm_w4a16(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p,
+                      cudaStream_t s) {
+  C3B_REQUIRE(n_in >= 3, "w4a16 gemm: needs A, packed B, B scales");
+  C3B_REQUIRE(in[0].dtype == C3B_BF16 && in[1].dtype == C3B_U8 && in[2].dtype == C3B_F32,
+              "w4a16 gemm: A bf16, B packed FP4 (u8), scales f32");
+  C3B_REQUIRE(p.K > 0 && p.K % 64 == 0, "w4a16 gemm: K must be a positive multiple of 64");
+  C3B_REQUIRE(p.N > 0 && p.N % 32 == 0, "w4a16 gemm: N must be a positive multiple of 32");
+  C3B_REQUIRE(p.M >= 0 && p.M < (int64_t)1 << 31, "w4a16 gemm: M range");
+  C3B_REQUIRE(numel(in[0]) >= p.M * p.K && numel(in[1]) >= p.N * p.K / 2 && numel(in[2]) >= p.N * p.K / tc::W4_GROUP,
+              "w4a16 gemm: operand extents");
+  C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0 && ((uintptr_t)in[2].ptr & 15) == 0,
+              "w4a16 gemm: 16-byte alignment");
+  tc::TcArgs a;
+  memset(&a, 0, sizeof(a));
+  int rc = fill_epilogue(a, in, n_in, 3, p.bias_mode, p.has_residual, p.M, p.N, out);
+  if (rc) return rc;
+  if (p.M == 0) return C3B_OK;
+  a.M = p.M; a.N = p.N; a.K = p.K; a.act = p.act;
+  a.block_n = pick_block_n(p.N, p.block_n);
+  a.n_tiles_n = (int)((p.N + a.block_n - 1) / a.block_n);
+  a.n_tiles = (int)((p.M + tc::BM - 1) / tc::BM) * a.n_tiles_n;
+  a.k_blocks = (int)(p.K / tc::BK);
+  tc::TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    uint64_t str[1] = {(uint64_t)p.K * 2};
+    uint32_t box[2] = {tc::BK, tc::BM};
+    if ((rc = encode(&maps.a[0], in[0].ptr, 2, dims, str, box))) return rc;
+  }
+  {  // packed FP4 rows: K/2 bytes per output row, 32 bytes (64 elements) per K block
+    uint64_t dims[2] = {(uint64_t)p.K / 2, (uint64_t)p.N};
+    uint64_t str[1] = {(uint64_t)p.K / 2};
+    uint32_t box[2] = {tc::BK / 2, (uint32_t)a.block_n};
+    if ((rc = encode(&maps.a[1], in[1].ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_DATA_TYPE_UINT8)))
+      return rc;
+  }
+  {  // scales [K/64][N][4]: the four group scales of one row and K block are contiguous
+    uint64_t dims[3] = {(uint64_t)(tc::BK / tc::W4_GROUP), (uint64_t)p.N, (uint64_t)p.K / tc::BK};
+    uint64_t str[2] = {(uint64_t)(tc::BK / tc::W4_GROUP) * 4, (uint64_t)p.N * (tc::BK / tc::W4_GROUP) * 4};
+    uint32_t box[3] = {(uint32_t)(tc::BK / tc::W4_GROUP), (uint32_t)a.block_n, 1};
+    if ((rc = encode(&maps.a[2], in[2].ptr, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return rc;
+  }
+  return launch_tc(maps, a, s, 2);
 }
 
 int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_tc_params& p,

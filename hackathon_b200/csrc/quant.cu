@@ -5,6 +5,7 @@
 // pairs with the hardware round-to-nearest-even, saturating E4M3 conversion.
 // The division is IEEE (x / s), so a host restatement that divides in fp32 and
 // rounds to E4M3 gives the same bytes.
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
 #include "common.cuh"
@@ -62,7 +63,55 @@ __global__ void __launch_bounds__(QWARPS * 32) quant_e4m3_kernel(const T* __rest
   }
 }
 
+// FP4 (E2M1) weight quantisation for the W4A16 path: one thread per (row,
+// 16-element group); scale = max|x| / 6 (1 for an all-zero group), bytes =
+// E2M1(x / scale) round-to-nearest-even, saturating, element 2i in the low
+// nibble of byte i.  Scales are written [K/64][N][4] (the four groups of one
+// row and 64-wide K block together), the layout the W4A16 GEMM loads by TMA.
+template <typename T>
+__global__ void quant_fp4_kernel(const T* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scale,
+                                 int64_t N, int64_t K) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t groups = K / 16;
+  if (gid >= N * groups) return;
+  const int64_t n = gid / groups, g = gid % groups;
+  const T* xr = x + n * K + g * 16;
+  float v[16];
+  load8<T>(xr, v);
+  load8<T>(xr + 8, v + 8);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float s = amax > 0.f ? amax / 6.0f : 1.0f;
+  scale[((g >> 2) * N + n) * 4 + (g & 3)] = s;
+  __align__(8) __nv_fp4x2_storage_t o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    o[i] = __nv_cvt_float2_to_fp4x2(make_float2(v[2 * i] / s, v[2 * i + 1] / s), __NV_E2M1, cudaRoundNearest);
+  *reinterpret_cast<uint2*>(q + n * (K / 2) + g * 8) = *reinterpret_cast<const uint2*>(o);
+}
+
 }  // namespace
+
+int launch_quant_fp4(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor& scale, const c3b_quant_params& p,
+                     cudaStream_t s) {
+  C3B_REQUIRE(x.dtype == C3B_F32 || x.dtype == C3B_BF16, "quantize fp4: input f32 or bf16");
+  C3B_REQUIRE(q.dtype == C3B_U8 && scale.dtype == C3B_F32, "quantize fp4: outputs u8 and f32");
+  C3B_REQUIRE(p.M >= 0 && p.K > 0 && p.K % 64 == 0, "quantize fp4: K must be a positive multiple of 64");
+  C3B_REQUIRE(numel(x) >= p.M * p.K && numel(q) >= p.M * p.K / 2 && numel(scale) >= p.M * p.K / 16,
+              "quantize fp4: extents");
+  C3B_REQUIRE(((uintptr_t)x.ptr & 15) == 0 && ((uintptr_t)q.ptr & 7) == 0, "quantize fp4: alignment");
+  const int64_t work = p.M * (p.K / 16);
+  if (work == 0) return C3B_OK;
+  const unsigned blocks = (unsigned)((work + 255) / 256);
+  if (x.dtype == C3B_F32)
+    quant_fp4_kernel<float><<<blocks, 256, 0, s>>>((const float*)x.ptr, (uint8_t*)q.ptr, (float*)scale.ptr, p.M, p.K);
+  else
+    quant_fp4_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)x.ptr, (uint8_t*)q.ptr,
+                                                           (float*)scale.ptr, p.M, p.K);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
 
 int launch_quant_e4m3(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor& scale, const c3b_quant_params& p,
                       cudaStream_t s) {

@@ -207,7 +207,7 @@ for _name in _prepared_names():
 def _scratch(like: Any, shape, np_dtype):
     if _is_torch(like):
         import torch
-        tmap = {np.uint8: torch.uint8, np.float32: torch.float32}
+        tmap = {np.uint8: torch.uint8, np.float32: torch.float32, np.uint16: torch.bfloat16}
         return torch.empty(tuple(shape), dtype=tmap[np_dtype], device=like.device)
     import cupy
     return cupy.empty(tuple(shape), dtype=np_dtype)
@@ -267,4 +267,57 @@ def kernel_matmul_f8(inputs: List[Any], outputs: List[Any], params: Dict[str, An
         from .kernels import _ew_program
         L.launch(L.K_EW, [L.make_tensor(do.ptr, L.F32, (M * N,))], [L.make_tensor(do.ptr, L.F32, (M * N,))],
                  _ew_program([(L.OP_MUL_IMM, 0, 0)], [alpha]), stream)
+    outputs[0] = _view(outputs[0], (M, N))
+
+
+@register("matmul_f4")
+def kernel_matmul_f4(inputs: List[Any], outputs: List[Any], params: Dict[str, Any],
+                     tuning: Optional[Dict[str, int]] = None) -> None:
+    """The policy's fp4 GEMM as W4A16 (c32/strategy.py:98-119): the weight
+    operand (inputs[1]) is quantised to FP4 E2M1 in groups of 16 on the device
+    (C3B_K_QUANT_FP4), the activations are cast to bf16, and the tcgen05 GEMM
+    expands the weights next to the MMA (C3B_K_GEMM_W4A16); fp32 output."""
+    a, b = inputs[0], inputs[1]
+    da, db = describe(a), describe(b)
+    if len(da.shape) != 2 or len(db.shape) != 2:
+        raise ValueError("matmul_f4: 2-D operands")
+    ta, tb = int(params.get("transA", 0)), int(params.get("transB", 0))
+    if float(params.get("alpha", 1.0)) != 1.0:
+        raise NotImplementedError("matmul_f4: alpha != 1")
+    M, K = (da.shape[1], da.shape[0]) if ta else da.shape
+    N = db.shape[0] if tb else db.shape[1]
+    if (db.shape[1] if tb else db.shape[0]) != K:
+        raise ValueError("matmul_f4: inner dimensions differ")
+    if K % 64 or N % 32:
+        raise ValueError("matmul_f4: needs K % 64 == 0 and N % 32 == 0")
+    stream = _current_stream([a, b] + list(outputs))
+
+    def ptr(t):
+        return int(t.data_ptr()) if _is_torch(t) else int(t.data.ptr)
+
+    def copy_to(src, rows, cols, trans, dtype, np_dtype):
+        t = _scratch(a, (rows, cols), np_dtype)
+        cp = L.CopyParams()
+        if trans:
+            cp.in_stride[0], cp.in_stride[1] = 1, rows
+        else:
+            cp.in_stride[0], cp.in_stride[1] = cols, 1
+        L.launch(L.K_COPY, [L.make_tensor(src.ptr, src.dtype, src.shape)], [L.make_tensor(ptr(t), dtype, (rows, cols))],
+                 cp, stream)
+        return t
+
+    abf = copy_to(da, M, K, ta, L.BF16, np.uint16)           # bf16 activations [M, K]
+    bk = copy_to(db, N, K, not tb, L.F32, np.float32)        # weights [N, K]
+    q, s = _scratch(a, (N, K // 2), np.uint8), _scratch(a, (K // 64, N, 4), np.float32)
+    L.launch(L.K_QUANT_FP4, [L.make_tensor(ptr(bk), L.F32, (N, K))],
+             [L.make_tensor(ptr(q), L.U8, (N, K // 2)), L.make_tensor(ptr(s), L.F32, (K // 64, N, 4))],
+             L.QuantParams(N, K), stream)
+    g = L.GemmTcParams()
+    g.M, g.N, g.K, g.bias_mode, g.act, g.has_residual, g.block_n = M, N, K, L.BIAS_NONE, 0, 0, 0
+    do = describe(outputs[0])
+    if do.numel < M * N or do.dtype != L.F32:
+        raise ValueError("matmul_f4: output must be an f32 arena of at least M*N elements")
+    L.launch(L.K_GEMM_W4A16, [L.make_tensor(ptr(abf), L.BF16, (M, K)), L.make_tensor(ptr(q), L.U8, (N, K // 2)),
+                              L.make_tensor(ptr(s), L.F32, (K // 64, N, 4))],
+             [L.make_tensor(do.ptr, L.F32, (M, N))], g, stream)
     outputs[0] = _view(outputs[0], (M, N))

@@ -28,7 +28,12 @@ is ``bf16`` with the linear layers the reference's precision policy marks fp8
 (aligned GEMMs with K, N >= 64: c32/strategy.py:147-157) run as rowwise-scaled
 E4M3 GEMMs — a quantisation step for the activation rows, E4M3 weights with
 per-output-row scales, tcgen05 ``kind::f8f6f4`` with fp32 accumulation and the
-two scales applied in the epilogue.
+two scales applied in the epilogue; ``mixed`` applies the whole GEMM policy
+(c32/strategy.py:146-157) for a device that supports fp8 and fp4: constant-weight
+GEMMs with K, N >= 128, K and N multiples of 32 and K*N >= 32768 run W4A16
+(FP4 E2M1 weights in groups of 16 with fp32 scales, expanded to bf16 in
+shared memory next to the MMA), other aligned GEMMs with K, N >= 64 run fp8,
+the rest bf16.
 """
 
 from __future__ import annotations
@@ -58,7 +63,7 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 class _State:
     def __init__(self, graph: ModelGraph, batch: int, profile: str):
-        if profile not in ("fp32", "bf16", "fp8"):
+        if profile not in ("fp32", "bf16", "fp8", "mixed"):
             raise ValueError(f"unknown precision profile {profile!r}")
         self.g = graph
         self.batch = batch
@@ -400,7 +405,7 @@ def _gemm_tc_launch(d: Dict[str, Desc], x, w, b, out, M, N, K, act, res=None):
 
 
 def _emit(st: _State, op: dict) -> None:
-    P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp8")
+    P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp8", "mixed")
     k = op["kind"]
     if k == "conv":
         x = st.t(op["x"])
@@ -563,10 +568,32 @@ def _emit(st: _State, op: dict) -> None:
         use_tc = bf and N % 32 == 0 and K % 64 == 0 and P.tensors[x].dtype == L.BF16
         bname = st.weight("bias", (op["b"] * op.get("beta", 1.0)).astype(np.float32), L.F32) \
             if op["b"] is not None else None
-        # fp8 per the reference policy for GEMMs (c32/strategy.py:150-157)
-        use_f8 = (use_tc and st.profile == "fp8" and N % 16 == 0 and K % 16 == 0 and K >= 64 and N >= 64
-                  and op.get("alpha", 1.0) == 1.0)
-        if use_f8:
+        # the reference policy for GEMMs (c32/strategy.py:146-157): fp4 (W4A16)
+        # for large aligned constant-weight GEMMs, else fp8 for aligned ones
+        plain = use_tc and op.get("alpha", 1.0) == 1.0
+        use_w4 = (plain and st.profile == "mixed" and K % 64 == 0 and N % 32 == 0 and K >= 128 and N >= 128
+                  and K * N >= 32768)
+        use_f8 = (plain and not use_w4 and st.profile in ("fp8", "mixed") and N % 16 == 0 and K % 16 == 0
+                  and K >= 64 and N >= 64)
+        if use_w4:
+            from .fp4 import quant_groups_fp4
+            wq, ws = quant_groups_fp4(w)
+            wqn = st.weight("linear_fp4", wq, L.U8)
+            wsn = st.weight("linear_fp4_scale", ws, L.F32)
+            odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else L.BF16
+            P.add_tensor(out, (M, N), odt)
+
+            def build(d, x=x, wqn=wqn, wsn=wsn, bname=bname, out=out, M=M, N=N, K=K, act=op["act"], res=res):
+                g = L.GemmTcParams()
+                g.M, g.N, g.K = M, N, K
+                g.bias_mode = L.BIAS_COL if bname else L.BIAS_NONE
+                g.act, g.has_residual, g.block_n = act, int(res is not None), 0
+                ins = [d[x].t((M, K)), d[wqn].t(), d[wsn].t()] + ([d[bname].t()] if bname else []) + \
+                    ([d[res].t((M, N))] if res else [])
+                return [Launch(L.K_GEMM_W4A16, ins, [d[out].t((M, N))], g)]
+            P.add_step("gemm_w4a16", [x, wqn, wsn] + ([bname] if bname else []) + ([res] if res else []), [out],
+                       build, flops)
+        elif use_f8:
             from .fp8 import quant_rows_e4m3
             wq, ws = quant_rows_e4m3(w)
             wqn = st.weight("linear_e4m3", wq, L.U8)

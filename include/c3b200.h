@@ -87,7 +87,9 @@ enum {
   C3B_K_STEM_CONV = 17,  /* direct small-Cin conv NCHW f32 -> NHWC bf16    */
   C3B_K_QUANT_E4M3 = 18, /* rowwise e4m3 quantisation (fp8 precision path) */
   C3B_K_GEMM_FP8 = 19,   /* e4m3 x e4m3 tcgen05 GEMM, scaled epilogue      */
-  C3B_K_COUNT = 20
+  C3B_K_QUANT_FP4 = 20,  /* FP4 E2M1 weight quantisation (W4A16 path)      */
+  C3B_K_GEMM_W4A16 = 21, /* bf16 x FP4-weight tcgen05 GEMM (W4A16)         */
+  C3B_K_COUNT = 22
 };
 
 /* --- C3B_K_EW: out = program(in0..in5) with NumPy broadcasting.
@@ -253,6 +255,20 @@ typedef struct {
  * b_scale f32 [N], [bias f32 [N]], [residual [M,N] f32|bf16]; output f32|bf16.
  * Parameters: c3b_gemm_tc_params.  K % 16 == 0, N % 32 == 0.  Executes the
  * reference's "matmul_f8" name (which the reference cannot run). */
+
+/* --- C3B_K_QUANT_FP4: w [N,K] f32|bf16 -> q [N,K/2] u8 (two FP4 E2M1 codes per
+ * byte, element 2i in the low nibble) and scale f32 laid out [K/64][N][4]:
+ * scale of group g (16 K elements) of row n at ((g/4)*N + n)*4 + g%4;
+ * scale = max|group| / 6 (1 for an all-zero group), code = E2M1(w / scale)
+ * round-to-nearest-even, saturating.  K % 64 == 0.  Parameters:
+ * c3b_quant_params, with M = N rows.  No reference counterpart: the reference
+ * policy names fp4 as W4A16 (c32/strategy.py:98-119, 150-154) without a kernel.
+ *
+ * --- C3B_K_GEMM_W4A16: C = A · dequant(B)ᵀ (+ bias) (+ residual), act, with A
+ * [M,K] bf16 and B the output of C3B_K_QUANT_FP4; dequant(B)[n,k] =
+ * bf16(E2M1 value × group scale); fp32 accumulation in TMEM.  inputs: A, q, scale,
+ * [bias f32 [N]], [residual]; output f32|bf16.  Parameters: c3b_gemm_tc_params.
+ * K % 64 == 0, N % 32 == 0.  Executes the reference's "matmul_f4" name. */
 
 /* --- C3B_K_GAP_NHWC: x [N, HW, C] -> y [N, C] f32 */
 typedef struct {

@@ -481,3 +481,84 @@ def test_matmul_f8_registry_name(torch_cuda):
     qb, sb = F.quant_rows(np.ascontiguousarray(b.T))
     ref = F.gemm_fp8(qa, sa, qb, sb)
     assert rel(host(outs[0]).reshape(M, N), ref) < 2e-5
+
+
+# ------------------------------------------------------------- W4A16 (fp4) path
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("N,K", [(32, 64), (200, 512), (7, 1024)])
+def test_quant_fp4_bit_exact(torch_cuda, dt, N, K):
+    """CUDA FP4 group quantiser == the oracle's restatement, byte for byte."""
+    import torch
+    from hackathon_b200 import _lib as L
+    from oracle import fp4 as F
+    w = randn(N, K) * np.float32(10.0) ** RNG.integers(-3, 2, size=(N, 1)).astype(np.float32)
+    w[0, :16] = 0.0  # an all-zero group
+    if dt == "bf16":
+        w = round_bf16(w)
+        wd = _bf16(torch, w)
+    else:
+        wd = dev(torch, w)
+    q = torch.empty((N, K // 2), dtype=torch.uint8, device="cuda")
+    s = torch.empty((K // 64, N, 4), dtype=torch.float32, device="cuda")
+    L.launch(L.K_QUANT_FP4, [L.make_tensor(wd.data_ptr(), L.F32 if dt == "f32" else L.BF16, (N, K))],
+             [L.make_tensor(q.data_ptr(), L.U8, (N, K // 2)), L.make_tensor(s.data_ptr(), L.F32, (K // 64, N, 4))],
+             L.QuantParams(N, K), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    qr, sr = F.quant_groups(w)
+    assert np.array_equal(host(s), sr)
+    assert np.array_equal(host(q), qr)
+
+
+@pytest.mark.parametrize("M,N,K,act,res,odt", [(128, 64, 64, 0, 0, "f32"), (300, 128, 192, 1, 0, "bf16"),
+                                               (1000, 256, 512, 2, 1, "f32"), (257, 96, 128, 0, 1, "bf16"),
+                                               (2048, 512, 1024, 1, 1, "f32")])
+def test_gemm_w4a16(torch_cuda, M, N, K, act, res, odt):
+    """W4A16 tcgen05 GEMM against the oracle on the same FP4 codes and scales:
+    the expanded weights are exact bf16 values, so only fp32 accumulation order
+    (f32 output) or bf16 output rounding separates the two."""
+    import torch
+    from hackathon_b200 import _lib as L
+    from oracle import fp4 as F
+    a = round_bf16(randn(M, K))
+    w = randn(N, K) * np.float32(0.05)
+    qp, qs = F.quant_groups(w)
+    bias = randn(N)
+    r = randn(M, N) if res else None
+    ref = F.gemm_w4a16(a, qp, qs, bias)
+    if res:
+        ref = ref + (round_bf16(r) if odt == "bf16" else r)
+    if act == 1:
+        ref = np.maximum(ref, 0)
+    elif act == 2:
+        ref = O.gelu_erf(ref.astype(np.float32))
+    g = L.GemmTcParams()
+    g.M, g.N, g.K, g.bias_mode, g.act, g.has_residual, g.block_n = M, N, K, L.BIAS_COL, act, res, 0
+    ta, tq, tsc, tb = _bf16(torch, a), dev(torch, qp), dev(torch, qs), dev(torch, bias)
+    ins = [L.make_tensor(ta.data_ptr(), L.BF16, (M, K)), L.make_tensor(tq.data_ptr(), L.U8, (N, K // 2)),
+           L.make_tensor(tsc.data_ptr(), L.F32, (K // 64, N, 4)), L.make_tensor(tb.data_ptr(), L.F32, (N,))]
+    if res:
+        tr = _bf16(torch, round_bf16(r)) if odt == "bf16" else dev(torch, r)
+        ins.append(L.make_tensor(tr.data_ptr(), L.BF16 if odt == "bf16" else L.F32, (M, N)))
+    out = torch.empty((M, N), dtype=torch.bfloat16 if odt == "bf16" else torch.float32, device="cuda")
+    L.launch(L.K_GEMM_W4A16, ins, [L.make_tensor(out.data_ptr(), L.BF16 if odt == "bf16" else L.F32, (M, N))], g,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    assert rel(out.float().cpu().numpy(), ref) < (8e-3 if odt == "bf16" else 2e-5)
+
+
+def test_matmul_f4_registry_name(torch_cuda):
+    """The reference name "matmul_f4" runs W4A16 through the registry: the
+    weight operand is quantised on the device, activations cast to bf16."""
+    import torch
+    from hackathon_b200.kernel_registry import lookup
+    from oracle import fp4 as F
+    M, K, N = 96, 128, 64
+    a, b = randn(M, K), randn(K, N)
+    outs = [torch.empty((M, N), dtype=torch.float32, device="cuda")]
+    lookup("matmul_f4")([dev(torch, a), dev(torch, b)], outs, {"transA": 0, "transB": 0}, None)
+    torch.cuda.synchronize()
+    qp, qs = F.quant_groups(np.ascontiguousarray(b.T))
+    ref = F.gemm_w4a16(round_bf16(a), qp, qs)
+    assert rel(host(outs[0]).reshape(M, N), ref) < 2e-5

@@ -110,3 +110,28 @@ def test_fp8_rowwise_scheme():
     big = np.abs(x) > np.max(np.abs(x), axis=1, keepdims=True) * 2.0 ** -6 * 1.01
     assert np.all(np.abs(d - x)[rows][big[rows]] <= np.abs(x)[rows][big[rows]] * 2.0 ** -4 + 1e-30)
     assert np.max(np.abs(q[rows].astype(np.int64) & 0x7F)) == 0x7E  # the row maximum maps to 448
+
+
+def test_e2m1_encoder_pinned():
+    """The fp4 oracle's E2M1 encoder against the OCP E2M1 code points (every
+    magnitude, every tie between neighbours, saturation, sign) and the
+    package's host quantiser against the oracle's scheme, byte for byte."""
+    from oracle import fp4 as F
+    from hackathon_b200.fp4 import quant_groups_fp4
+    points = {0.0: 0, 0.5: 1, 1.0: 2, 1.5: 3, 2.0: 4, 3.0: 5, 4.0: 6, 6.0: 7,
+              0.25: 0, 0.75: 2, 1.25: 2, 1.75: 4, 2.5: 4, 3.5: 6, 5.0: 6,  # ties -> even code
+              0.26: 1, 5.01: 7, 7.0: 7, 1e9: 7, -1.0: 10, -6.0: 15, -0.6: 9}
+    for v, c in points.items():
+        assert int(F.e2m1_encode(np.float32(v))) == c, v
+    codes = np.arange(16, dtype=np.uint8)
+    assert np.array_equal(F.e2m1_encode(F.e2m1_decode(codes).astype(np.float32))[1:], codes[1:])
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((64, 320)) * rng.choice([1e-3, 1.0, 40.0], (64, 1))).astype(np.float32)[:, :256]
+    w[5, 16:32] = 0.0
+    p1, s1 = F.quant_groups(w)
+    p2, s2 = quant_groups_fp4(w)
+    assert np.array_equal(p1, p2) and np.array_equal(s1, s2)
+    d = F.dequant(p1, s1)
+    # E2M1 spacing is at most 2 (between 4 and 6) of a scale of group-max / 6
+    gmax = np.max(np.abs(w.reshape(64, 16, 16)), axis=2).repeat(16, axis=1)
+    assert np.all(np.abs(d - w) <= gmax / 6.0 + np.abs(w) * 2.0 ** -8 + 1e-30)
