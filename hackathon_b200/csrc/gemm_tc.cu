@@ -580,19 +580,35 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
         const uint8_t* raw = sraw + (size_t)stage * raw_bytes;
         const float* scl = reinterpret_cast<const float*>(sscl + (size_t)stage * scl_bytes);
         uint8_t* dst = sb + (size_t)stage * b_bytes;
-        for (int u = ct; u < units; u += 256) {
-          const int r = u >> 3, c = u & 7;
-          const uint32_t packed = *reinterpret_cast<const uint32_t*>(raw + r * 32 + c * 4);
-          const float sc = scl[r * (BK / W4_GROUP) + (c >> 1)];
-          const float2 s2 = make_float2(sc, sc);
-          __align__(16) __nv_bfloat162 o[4];
+        // all loads of this thread's units first (up to 8: block_n / 32), then
+        // the conversions and stores, so the shared-memory latencies overlap
+        uint32_t pk[8];
+        float sc[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((packed >> (8 * j)) & 0xFF), __NV_E2M1);
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
-            o[j] = __float22bfloat162_rn(__fmul2_rn(f, s2));
+        for (int i = 0; i < 8; ++i) {
+          const int u = ct + 256 * i;
+          if (u < units) {
+            const int r = u >> 3, c = u & 7;
+            pk[i] = *reinterpret_cast<const uint32_t*>(raw + r * 32 + c * 4);
+            sc[i] = scl[r * (BK / W4_GROUP) + (c >> 1)];
           }
-          *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int u = ct + 256 * i;
+          if (u < units) {
+            const int r = u >> 3, c = u & 7;
+            const float2 s2 = make_float2(sc[i], sc[i]);
+            __align__(16) __nv_bfloat162 o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const __half2_raw h =
+                  __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((pk[i] >> (8 * j)) & 0xFF), __NV_E2M1);
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+              o[j] = __float22bfloat162_rn(__fmul2_rn(f, s2));
+            }
+            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
+          }
         }
         fence_proxy_async();
         __syncwarp();
