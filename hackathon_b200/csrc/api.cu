@@ -77,7 +77,7 @@ static const NameEntry kNames[] = {
     {"gemm_bias_act_f8", C3B_K_GEMM_FP8},
     // W4A16 path (the policy's fp4 for constant-weight GEMMs)
     {"quantize_fp4_groups", C3B_K_QUANT_FP4}, {"matmul_f4", C3B_K_GEMM_W4A16},
-    {"gemm_bias_act_w4a16", C3B_K_GEMM_W4A16},
+    {"gemm_bias_act_w4a16", C3B_K_GEMM_W4A16}, {"dequantize_fp4_groups", C3B_K_DEQUANT_FP4},
 };
 
 static int find_name(const std::string& n) {
@@ -244,6 +244,12 @@ int dispatch(int kid, const c3b_tensor* in, int n_in, const c3b_tensor* out, int
       if ((rc = get_params(params, len, p))) return rc;
       C3B_REQUIRE(n_in == 1 && n_out == 2, "quantize fp4: w -> q, scale");
       return launch_quant_fp4(in[0], out[0], out[1], p, s);
+    }
+    case C3B_K_DEQUANT_FP4: {
+      c3b_quant_params p;
+      if ((rc = get_params(params, len, p))) return rc;
+      C3B_REQUIRE(n_in == 2 && n_out == 1, "dequantize fp4: q, scale -> w");
+      return launch_dequant_fp4(in[0], in[1], out[0], p, s);
     }
     case C3B_K_GEMM_W4A16: {
       c3b_gemm_tc_params p;

@@ -178,6 +178,8 @@ int launch_gemm_fp8(const c3b_tensor* in, int n_in, const c3b_tensor& out, const
                     cudaStream_t s);
 int launch_quant_fp4(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor& scale, const c3b_quant_params& p,
                      cudaStream_t s);
+int launch_dequant_fp4(const c3b_tensor& q, const c3b_tensor& scale, const c3b_tensor& w, const c3b_quant_params& p,
+                       cudaStream_t s);
 int launch_gemm_w4a16(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p,
                       cudaStream_t s);
 

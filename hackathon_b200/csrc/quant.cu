@@ -91,7 +91,48 @@ __global__ void quant_fp4_kernel(const T* __restrict__ x, uint8_t* __restrict__ 
   *reinterpret_cast<uint2*>(q + n * (K / 2) + g * 8) = *reinterpret_cast<const uint2*>(o);
 }
 
+// W4A16 weights expanded once: dequant(q, scale) -> bf16 [N, K], with the same
+// arithmetic as the GEMM's converter warps (E2M1 pair -> f16x2 -> f32 pair,
+// times the group scale, one bf16 rounding), so both paths see identical
+// weights.  One thread per (row, 16-element group).
+__global__ void dequant_fp4_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scale,
+                                   __nv_bfloat16* __restrict__ w, int64_t N, int64_t K) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t groups = K / 16;
+  if (gid >= N * groups) return;
+  const int64_t n = gid / groups, g = gid % groups;
+  const uint2 pk = __ldg(reinterpret_cast<const uint2*>(q + n * (K / 2) + g * 8));
+  const float sc = __ldg(scale + ((g >> 2) * N + n) * 4 + (g & 3));
+  const float2 s2 = make_float2(sc, sc);
+  __align__(16) __nv_bfloat162 o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t word = j < 4 ? pk.x : pk.y;
+    const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((word >> (8 * (j & 3))) & 0xFF), __NV_E2M1);
+    o[j] = __float22bfloat162_rn(__fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), s2));
+  }
+  uint4* dst = reinterpret_cast<uint4*>(w + n * K + g * 16);
+  dst[0] = reinterpret_cast<const uint4*>(o)[0];
+  dst[1] = reinterpret_cast<const uint4*>(o)[1];
+}
+
 }  // namespace
+
+int launch_dequant_fp4(const c3b_tensor& q, const c3b_tensor& scale, const c3b_tensor& w, const c3b_quant_params& p,
+                       cudaStream_t s) {
+  C3B_REQUIRE(q.dtype == C3B_U8 && scale.dtype == C3B_F32 && w.dtype == C3B_BF16,
+              "dequantize fp4: inputs u8 codes and f32 scales, output bf16");
+  C3B_REQUIRE(p.M >= 0 && p.K > 0 && p.K % 64 == 0, "dequantize fp4: K must be a positive multiple of 64");
+  C3B_REQUIRE(numel(q) >= p.M * p.K / 2 && numel(scale) >= p.M * p.K / 16 && numel(w) >= p.M * p.K,
+              "dequantize fp4: extents");
+  C3B_REQUIRE(((uintptr_t)q.ptr & 7) == 0 && ((uintptr_t)w.ptr & 15) == 0, "dequantize fp4: alignment");
+  const int64_t work = p.M * (p.K / 16);
+  if (work == 0) return C3B_OK;
+  dequant_fp4_kernel<<<(unsigned)((work + 255) / 256), 256, 0, s>>>((const uint8_t*)q.ptr, (const float*)scale.ptr,
+                                                                   (__nv_bfloat16*)w.ptr, p.M, p.K);
+  C3B_CHECK_CUDA(cudaGetLastError());
+  return C3B_OK;
+}
 
 int launch_quant_fp4(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor& scale, const c3b_quant_params& p,
                      cudaStream_t s) {

@@ -50,6 +50,15 @@ from .kernels import Desc, Launch, conv_geometry
 from .program import Program
 
 
+# W4A16 GEMMs with at least this many rows expand their FP4 weights to bf16
+# once per pass (C3B_K_DEQUANT_FP4, ~N*K*2.5 bytes of traffic) and run the bf16
+# GEMM; fewer rows use the fused kernel, whose converter warps re-expand the
+# weights for every 128-row tile but read only the packed FP4 bytes.  Measured
+# on B200: fused Tx-large QKV (M = 131072) 1.58 ms vs bf16 GEMM 0.73 ms, the
+# expansion ~3 us; the fused path wins only where weight bandwidth dominates.
+W4A16_EXPAND_ROWS = 2048
+
+
 def bf16_bits(x: np.ndarray) -> np.ndarray:
     """float32 -> bfloat16 bit patterns (round to nearest even), as uint16."""
     u = np.ascontiguousarray(x, np.float32).view(np.uint32)
@@ -583,16 +592,32 @@ def _emit(st: _State, op: dict) -> None:
             odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else L.BF16
             P.add_tensor(out, (M, N), odt)
 
-            def build(d, x=x, wqn=wqn, wsn=wsn, bname=bname, out=out, M=M, N=N, K=K, act=op["act"], res=res):
-                g = L.GemmTcParams()
-                g.M, g.N, g.K = M, N, K
-                g.bias_mode = L.BIAS_COL if bname else L.BIAS_NONE
-                g.act, g.has_residual, g.block_n = act, int(res is not None), 0
-                ins = [d[x].t((M, K)), d[wqn].t(), d[wsn].t()] + ([d[bname].t()] if bname else []) + \
-                    ([d[res].t((M, N))] if res else [])
-                return [Launch(L.K_GEMM_W4A16, ins, [d[out].t((M, N))], g)]
-            P.add_step("gemm_w4a16", [x, wqn, wsn] + ([bname] if bname else []) + ([res] if res else []), [out],
-                       build, flops)
+            if M >= W4A16_EXPAND_ROWS:
+                # many rows: expand the FP4 weights to bf16 once (a transient
+                # arena tensor) and run the bf16 GEMM, instead of re-expanding
+                # them next to the MMA for every 128-row tile
+                wdq = f"{out}:w_bf16"
+                P.add_tensor(wdq, (N, K), L.BF16)
+
+                def build_dq(d, wqn=wqn, wsn=wsn, wdq=wdq, N=N, K=K):
+                    return [Launch(L.K_DEQUANT_FP4, [d[wqn].t(), d[wsn].t()], [d[wdq].t()], L.QuantParams(N, K))]
+                P.add_step("dequant_fp4", [wqn, wsn], [wdq], build_dq, 0.0)
+
+                def build(d, x=x, wdq=wdq, bname=bname, out=out, M=M, N=N, K=K, act=op["act"], res=res):
+                    return [_gemm_tc_launch(d, x, wdq, bname, out, M, N, K, act, res)]
+                P.add_step("gemm_tc", [x, wdq] + ([bname] if bname else []) + ([res] if res else []), [out],
+                           build, flops)
+            else:
+                def build(d, x=x, wqn=wqn, wsn=wsn, bname=bname, out=out, M=M, N=N, K=K, act=op["act"], res=res):
+                    g = L.GemmTcParams()
+                    g.M, g.N, g.K = M, N, K
+                    g.bias_mode = L.BIAS_COL if bname else L.BIAS_NONE
+                    g.act, g.has_residual, g.block_n = act, int(res is not None), 0
+                    ins = [d[x].t((M, K)), d[wqn].t(), d[wsn].t()] + ([d[bname].t()] if bname else []) + \
+                        ([d[res].t((M, N))] if res else [])
+                    return [Launch(L.K_GEMM_W4A16, ins, [d[out].t((M, N))], g)]
+                P.add_step("gemm_w4a16", [x, wqn, wsn] + ([bname] if bname else []) + ([res] if res else []), [out],
+                           build, flops)
         elif use_f8:
             from .fp8 import quant_rows_e4m3
             wq, ws = quant_rows_e4m3(w)

@@ -89,7 +89,8 @@ enum {
   C3B_K_GEMM_FP8 = 19,   /* e4m3 x e4m3 tcgen05 GEMM, scaled epilogue      */
   C3B_K_QUANT_FP4 = 20,  /* FP4 E2M1 weight quantisation (W4A16 path)      */
   C3B_K_GEMM_W4A16 = 21, /* bf16 x FP4-weight tcgen05 GEMM (W4A16)         */
-  C3B_K_COUNT = 22
+  C3B_K_DEQUANT_FP4 = 22,/* FP4 weights -> bf16 (W4A16 at large M)         */
+  C3B_K_COUNT = 23
 };
 
 /* --- C3B_K_EW: out = program(in0..in5) with NumPy broadcasting.
@@ -268,7 +269,13 @@ typedef struct {
  * [M,K] bf16 and B the output of C3B_K_QUANT_FP4; dequant(B)[n,k] =
  * bf16(E2M1 value × group scale); fp32 accumulation in TMEM.  inputs: A, q, scale,
  * [bias f32 [N]], [residual]; output f32|bf16.  Parameters: c3b_gemm_tc_params.
- * K % 64 == 0, N % 32 == 0.  Executes the reference's "matmul_f4" name. */
+ * K % 64 == 0, N % 32 == 0.  Executes the reference's "matmul_f4" name.
+ *
+ * --- C3B_K_DEQUANT_FP4: (q, scale) from C3B_K_QUANT_FP4 -> w [N,K] bf16, the
+ * same effective weights the W4A16 GEMM expands next to its MMA.  With many
+ * rows per call (M in the thousands) expanding once and running C3B_K_GEMM_TC
+ * costs less than re-expanding the weights for every 128-row tile.
+ * Parameters: c3b_quant_params, with M = N rows.  No reference counterpart. */
 
 /* --- C3B_K_GAP_NHWC: x [N, HW, C] -> y [N, C] f32 */
 typedef struct {

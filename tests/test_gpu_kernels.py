@@ -562,3 +562,23 @@ def test_matmul_f4_registry_name(torch_cuda):
     qp, qs = F.quant_groups(np.ascontiguousarray(b.T))
     ref = F.gemm_w4a16(round_bf16(a), qp, qs)
     assert rel(host(outs[0]).reshape(M, N), ref) < 2e-5
+
+
+@pytest.mark.parametrize("N,K", [(32, 64), (300, 1024)])
+def test_dequant_fp4_bit_exact(torch_cuda, N, K):
+    """The once-per-pass FP4 expansion gives the oracle's effective bf16 weights
+    (and therefore the fused W4A16 kernel's), bit for bit."""
+    import torch
+    from hackathon_b200 import _lib as L
+    from oracle import fp4 as F
+    from oracle.bf16 import round_bf16 as rb
+    w = randn(N, K) * np.float32(0.05)
+    qp, qs = F.quant_groups(w)
+    tq, ts = dev(torch, qp), dev(torch, qs)
+    out = torch.empty((N, K), dtype=torch.bfloat16, device="cuda")
+    L.launch(L.K_DEQUANT_FP4, [L.make_tensor(tq.data_ptr(), L.U8, (N, K // 2)),
+                               L.make_tensor(ts.data_ptr(), L.F32, (K // 64, N, 4))],
+             [L.make_tensor(out.data_ptr(), L.BF16, (N, K))], L.QuantParams(N, K),
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.float().cpu().numpy(), rb(F.dequant(qp, qs)))

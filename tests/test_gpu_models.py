@@ -197,8 +197,9 @@ def _w4a16_weights(g):
     return g2
 
 
-@pytest.mark.parametrize("profile", ["fp8", "mixed"])
-@pytest.mark.parametrize("model,batch", [("tx_small", 8), ("tx_large", 2)])
+@pytest.mark.parametrize("profile,model,batch", [("fp8", "tx_small", 8), ("fp8", "tx_large", 2),
+                                                 ("mixed", "tx_small", 8), ("mixed", "tx_large", 2),
+                                                 ("mixed", "tx_small", 32)])  # 4096 rows: expand-once path
 def test_tx_low_precision_profiles(wl, model, batch, profile):
     """fp8 profile (E4M3 GEMMs where the reference policy marks fp8) against the
     fp32 oracle: E4M3 keeps 3 mantissa bits, so the gate is a scaled logits error
@@ -210,7 +211,11 @@ def test_tx_low_precision_profiles(wl, model, batch, profile):
     ref = run_graph(_w4a16_weights(g) if profile == "mixed" else g, feeds)["logits"]
     ex, out = _run_program(g, batch, profile, feeds)
     labels = {s.label for s in ex.prog.steps}
-    assert ("gemm_fp8" in labels and "quant_e4m3" in labels) if profile == "fp8" else "gemm_w4a16" in labels
+    if profile == "fp8":
+        assert "gemm_fp8" in labels and "quant_e4m3" in labels
+    else:
+        assert "gemm_w4a16" in labels
+        assert ("dequant_fp4" in labels) == (batch * g.meta["seq"] >= 2048)
     abs_err, n_flip, n_real_flip = _bf16_gate(out, ref)
     print(f"{model} {profile}: scaled max abs err {abs_err:.3e}, argmax flips {n_flip} (non-tie {n_real_flip})")
     assert np.isfinite(out).all()
