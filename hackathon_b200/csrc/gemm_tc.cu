@@ -72,6 +72,9 @@ struct TcArgs {
   // fp8 GEMM (tc_gemm_kernel<1>): per-row scale of A, per-column scale of B
   const float* a_scale;
   const float* b_scale;
+  // tc_gemm_kernel: bf16 output through per-warp shared-memory tiles and TMA
+  // stores (maps.out: 16 columns x 32 rows, 32-byte swizzle)
+  int tma_out;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -345,6 +348,15 @@ __device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t c
   }
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+// The shared-memory source of all but the most recent committed bulk store has been read.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
 // Residual of 16 consecutive columns (bf16: 32 bytes, f32: 64 bytes) as raw words.
 __device__ __forceinline__ void load_res16(const TcArgs& a, int64_t off, uint4* r) {
   if (a.dt_res == C3B_BF16) {
@@ -359,8 +371,8 @@ __device__ __forceinline__ void load_res16(const TcArgs& a, int64_t off, uint4* 
 
 // 16 columns of one output row: (x row scale x column scale) -> +bias ->
 // +residual -> act -> store (bf16 or f32).
-__device__ __forceinline__ void finish16(const TcArgs& a, int64_t off, int64_t col0, float* v, const uint4* r,
-                                         float rs) {
+// finish16's arithmetic without the store: (x scales) -> +bias -> +residual -> act.
+__device__ __forceinline__ void epi16(const TcArgs& a, int64_t col0, float* v, const uint4* r, float rs) {
   // pairwise (packed fp32) arithmetic: v2[i] holds columns 2i, 2i+1
   float2* v2 = reinterpret_cast<float2*>(v);
   if (a.b_scale) {
@@ -394,6 +406,12 @@ __device__ __forceinline__ void finish16(const TcArgs& a, int64_t off, int64_t c
     }
   }
   act_inplace<16>(v, a.act, a.dt_out == C3B_BF16);
+}
+
+__device__ __forceinline__ void finish16(const TcArgs& a, int64_t off, int64_t col0, float* v, const uint4* r,
+                                         float rs) {
+  epi16(a, col0, v, r, rs);
+  float2* v2 = reinterpret_cast<float2*>(v);
   if (a.dt_out == C3B_BF16) {
     uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
 #pragma unroll
@@ -439,7 +457,10 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   uint8_t* sb = smem + (size_t)stages * a_bytes;
   uint8_t* sraw = sb + (size_t)stages * b_bytes;
   uint8_t* sscl = sraw + (size_t)stages * raw_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sscl + (size_t)stages * scl_bytes);
+  // per-warp output tiles (2 x 1 KB per epilogue warp, 1024-byte aligned)
+  uint8_t* stg = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(sscl + (size_t)stages * scl_bytes) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stg + (a.tma_out ? (size_t)EPIW * 2048 : 0));
   uint64_t* full = bars;
   uint64_t* empty = bars + stages;
   uint64_t* bready = bars + 2 * stages;  // MODE 2: B stage expanded
@@ -628,9 +649,12 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     const int cols = a.block_n / (EPIW / 4);  // columns per warp
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint8_t* my_stg = stg + (size_t)(warp - 2) * 2048;
+    uint32_t n_st = 0;  // TMA stores this warp has issued
     for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
       const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
       const int64_t row = (int64_t)mb * BM + q * 32 + lane;
+      const int64_t row0 = (int64_t)mb * BM + q * 32;  // first row of this warp's lanes
       const int64_t col_base = (int64_t)nb * a.block_n + part * cols;
       const bool row_ok = row < a.M && col_base < a.N;
       const float rs = (F8 && row_ok) ? __ldg(a.a_scale + row) : 1.0f;
@@ -646,8 +670,34 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
         if (more) load_res16(a, row * a.N + col_base + c0 + 16, rn);
         float v[16];
         tmem_ld16(tbase + c0, v);
-        if (row_ok && col_base + c0 < a.N)
+        if (a.tma_out) {
+          // bf16 rows through the warp's tile: 32 rows x 32 bytes with the
+          // 32-byte swizzle (16-byte chunk bit 4 ^= address bit 7, conflict
+          // free), then one TMA store of 16 columns x 32 rows; rows past M
+          // are clipped by the tensor map
+          if (row0 < a.M && col_base + c0 < a.N) {
+            epi16(a, col_base + c0, v, a.res ? rc : nullptr, rs);
+            uint8_t* tile = my_stg + (n_st & 1) * 1024;
+            if (lane == 0) bulk_wait_read1();  // the store that last used this tile has read it
+            __syncwarp();
+            __align__(16) __nv_bfloat162 o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = __float22bfloat162_rn(make_float2(v[2 * j], v[2 * j + 1]));
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              *reinterpret_cast<uint4*>(tile + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4)) =
+                  reinterpret_cast<const uint4*>(o)[h];
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&maps.out, tile, (int)(col_base + c0), (int)row0);
+              bulk_commit();
+            }
+            ++n_st;
+          }
+        } else if (row_ok && col_base + c0 < a.N) {
           finish16(a, row * a.N + col_base + c0, col_base + c0, v, a.res ? rc : nullptr, rs);
+        }
         if (more) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) rc[i] = rn[i];
@@ -658,6 +708,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
       if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (a.tma_out && lane == 0) bulk_wait0();
   }
 
   tc_fence_before();
@@ -1255,17 +1306,39 @@ static int pick_block_n(int64_t N, int requested) {
   return 128;
 }
 
+// bf16 GEMM outputs leave through TMA stores (tc_gemm_kernel's per-warp
+// tiles) when the K loop is short (<= 16 blocks): there the epilogue sets the
+// pace (Tx-large fp8 QKV 0.62 -> 0.39 ms, ResNet 1x1 shortcuts up to 1.5x), while
+// long-K convolutions lose more from the stage slot the tiles take (-7 %).
+// C3B200_GEMM_TMA_OUT=0 keeps the per-lane stores everywhere (A/B timing).
+static int enable_tma_out(tc::TmaMaps& maps, tc::TcArgs& a) {
+  static const bool on = [] {
+    const char* e = getenv("C3B200_GEMM_TMA_OUT");
+    return !(e && e[0] == '0');
+  }();
+  a.tma_out = 0;
+  if (!on || a.dt_out != C3B_BF16 || a.N % 16 || a.k_blocks > 16) return C3B_OK;
+  uint64_t dims[2] = {(uint64_t)a.N, (uint64_t)a.M};
+  uint64_t str[1] = {(uint64_t)a.N * 2};
+  uint32_t box[2] = {16, 32};
+  int rc = encode(&maps.out, a.out, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  a.tma_out = 1;
+  return C3B_OK;
+}
+
 template <int MODE>
 static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s) {
   // one 128-byte K row per operand row; MODE 2 adds the packed FP4 tile and its scales
   size_t stage_bytes = (size_t)tc::BM * 128 + (size_t)a.block_n * 128;
   if (MODE == 2) stage_bytes += (size_t)a.block_n * (tc::BK / 2) + (size_t)a.block_n * (tc::BK / tc::W4_GROUP) * 4;
-  const size_t budget = 200 * 1024;
+  const size_t out_tiles = a.tma_out ? (size_t)(MODE == 2 ? 8 : 16) * 2048 + 1024 : 0;  // + alignment
+  const size_t budget = 200 * 1024 - out_tiles;
   int stages = (int)(budget / stage_bytes);
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(C3B_E_INVALID, "tc gemm: tile does not fit in shared memory");
   a.stages = stages;
-  const size_t smem = 1024 + stages * stage_bytes + (3 * stages + 4) * 8 + 16;
+  const size_t smem = 1024 + stages * stage_bytes + out_tiles + (3 * stages + 4) * 8 + 16;
   static bool attr_set = false;
   if (!attr_set) {
     C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1346,6 +1419,7 @@ int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
     uint32_t box[2] = {tc::BK, (uint32_t)a.block_n};
     if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box))) return rc;
   }
+  if ((rc = enable_tma_out(maps, a))) return rc;
   return launch_tc(maps, a, s);
 }
 
@@ -1391,6 +1465,7 @@ int launch_gemm_fp8(const c3b_tensor* in, int n_in, const c3b_tensor& out, const
                      CU_TENSOR_MAP_DATA_TYPE_UINT8)))
       return rc;
   }
+  if ((rc = enable_tma_out(maps, a))) return rc;
   return launch_tc(maps, a, s, 1);
 }
 
@@ -1440,6 +1515,7 @@ int launch_gemm_w4a16(const c3b_tensor* in, int n_in, const c3b_tensor& out, con
                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
       return rc;
   }
+  if ((rc = enable_tma_out(maps, a))) return rc;
   return launch_tc(maps, a, s, 2);
 }
 
@@ -1593,6 +1669,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
         if ((rc = encode(&maps.a[pr * 2 + ps], base, 4, dims, str, box))) return rc;
       }
   }
+  if ((rc = enable_tma_out(maps, a))) return rc;
   return launch_tc(maps, a, s);
 }
 
