@@ -795,6 +795,8 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // output tiles (a.tma_out): 1 KB per epilogue warp, 1024-byte aligned after the barriers
+  uint8_t* stg = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(abort_flag + 1) + 1023) & ~uintptr_t(1023));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -981,7 +983,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
         for (int h = 0; h < 2; ++h) {
           float v[16];
           tmem_ld16(tb + h * 16, v);
-          if (!img_ok) continue;
+          if (!img_ok && !a.tma_out) continue;
           const float4* bp = reinterpret_cast<const float4*>(a.bias + nb * a.block_n + cc[u] * 32 + h * 16);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -997,6 +999,28 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
             }
           }
           act_inplace<16>(v, a.act, true);
+          if (a.tma_out) {
+            // the warp's 32 pixels x 16 channels through its tile (32-byte
+            // swizzle) and one TMA store; images past the batch are clipped
+            uint8_t* tile = stg + (size_t)(warp - 2) * 1024;
+            if (lane == 0) bulk_wait_read0();  // the previous store has read the tile
+            __syncwarp();
+            __align__(16) __nv_bfloat162 o2[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o2[e] = __float22bfloat162_rn(make_float2(v[2 * e], v[2 * e + 1]));
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh)
+              *reinterpret_cast<uint4*>(tile + lane * 32 + ((hh ^ ((lane >> 2) & 1)) << 4)) =
+                  reinterpret_cast<const uint4*>(o2)[hh];
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_4d(&maps.out, tile, nb * a.block_n + cc[u] * 32 + h * 16, ib * a.img,
+                           wb * a.wt + q * (32 / a.img), hb * R + jj[u]);
+              bulk_commit();
+            }
+            continue;
+          }
           uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off[u] + h * 16);
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
@@ -1012,6 +1036,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
       if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (a.tma_out && lane == 0) bulk_wait0();
   }
 
   tc_fence_before();
@@ -1642,7 +1667,19 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
       int bst = (int)((budget - 2 * hb) / bb);
       a.stages = bst > 8 ? 8 : bst;
     }
-    const size_t smem = 1024 + 2 * hb + a.stages * bb + (2 * 2 + 2 * a.stages + 4) * 8 + 16;
+    size_t smem = 1024 + 2 * hb + a.stages * bb + (2 * 2 + 2 * a.stages + 4) * 8 + 16;
+    // bf16 output through per-warp tiles and TMA stores when 16 KB of tiles fit
+    // (residual layers of stage 2: the per-lane stores scatter one 16-byte piece
+    // per image)
+    a.tma_out = 0;
+    if (32 % a.img == 0 && smem + 1024 + 16 * 1024 <= 227 * 1024) {
+      uint64_t odims[4] = {(uint64_t)p.cout, (uint64_t)p.n, (uint64_t)p.wo, (uint64_t)p.ho};
+      uint64_t ostr[3] = {(uint64_t)p.ho * p.wo * p.cout * 2, (uint64_t)p.cout * 2, (uint64_t)p.wo * p.cout * 2};
+      uint32_t obox[4] = {16, (uint32_t)a.img, (uint32_t)(32 / a.img), 1};
+      if ((rc = encode(&maps.out, out.ptr, 4, odims, ostr, obox, CU_TENSOR_MAP_SWIZZLE_32B))) return rc;
+      a.tma_out = 1;
+      smem += 1024 + 16 * 1024;
+    }
     static bool attr_halo = false;
     if (!attr_halo) {
       C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_conv_halo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
