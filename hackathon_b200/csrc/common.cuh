@@ -184,5 +184,7 @@ int launch_gemm_w4a16(const c3b_tensor* in, int n_in, const c3b_tensor& out, con
                       cudaStream_t s);
 
 int sm_count();
+bool launch_stem_tc(const c3b_tensor* in, const c3b_tensor& out, const c3b_stem_conv_params& p, cudaStream_t s,
+                    int* rc);
 
 }  // namespace c3b

@@ -1291,6 +1291,194 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
   }
 }
 
+// Stem convolution on tcgen05: NCHW f32 input with Cin*kh*kw <= 32, 64 output
+// channels, NHWC bf16 output = act(conv + bias).  Persistent CTAs walk tiles of
+// 128 consecutive output pixels.  Warps 0-7, in two groups taking alternate
+// tiles, gather a tile's patch rows (one pixel per lane, lanes on consecutive
+// pixels so the NCHW loads coalesce) as bf16 K values 0..31 of a 128-byte
+// swizzled row; warp 12 issues two M=128,
+// N=64, K=16 MMAs per tile against the weights, resident in shared memory as
+// a [64][K] K-major operand; warps 8-11 drain their TMEM lane quarter, add
+// bias, apply the activation and TMA-store 32 pixels x 128 bytes.  Patch
+// tiles (4 stages) and accumulators (2 x 64 columns) are double-buffered.
+constexpr int STEM_THREADS = 416;  // 8 gather warps, 4 epilogue warps, 1 MMA warp
+constexpr int STEM_STAGES = 4;
+
+__global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_constant__ TmaMaps maps,
+                                                                  const float* __restrict__ x,
+                                                                  const float* __restrict__ wt,
+                                                                  const float* __restrict__ bias, c3b_stem_params g,
+                                                                  int act, int64_t M, int n_tiles) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;                                   // STEM_STAGES x 16 KB patch tiles
+  uint8_t* sbw = sa + STEM_STAGES * 16384;              // weights [64][64] bf16, 8 KB
+  uint8_t* so = sbw + 8192;                             // 4 epilogue warps x 4 KB output tiles
+  int4* ktab = reinterpret_cast<int4*>(so + 4 * 4096);  // per K index: input offset, row step, col step, valid
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ktab + 32);
+  uint64_t* afull = bars;
+  uint64_t* aempty = afull + STEM_STAGES;
+  uint64_t* tfull = aempty + STEM_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = g.c * g.g.kh * g.g.kw;
+
+  // weights -> B operand: row n (output channel), K-major, zero beyond K
+  for (int i = threadIdx.x; i < 64 * 8; i += STEM_THREADS) {
+    const int n = i >> 3, c = i & 7;  // 16-byte chunk c = K elements 8c..8c+7
+    __align__(16) __nv_bfloat162 o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k0 = c * 8 + 2 * j;
+      o[j] = __floats2bfloat162_rn(k0 < K ? wt[k0 * 64 + n] : 0.f, k0 + 1 < K ? wt[(k0 + 1) * 64 + n] : 0.f);
+    }
+    *reinterpret_cast<uint4*>(sbw + n * 128 + ((c ^ (n & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
+  }
+  if (threadIdx.x < 32) {
+    const int k = threadIdx.x;
+    const int KHW0 = g.g.kh * g.g.kw;
+    const int c = k / KHW0, rr = (k / g.g.kw) % g.g.kh, ss = k % g.g.kw;
+    ktab[k] = k < K ? make_int4((c * g.h + rr * g.g.dh) * g.w + ss * g.g.dw, rr * g.g.dh, ss * g.g.dw, 1)
+                    : make_int4(0, 0, 0, 0);
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STEM_STAGES; ++i) {
+      mbar_init(&afull[i], 4);
+      mbar_init(&aempty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  fence_proxy_async();  // the weight rows are read by the MMA (async proxy)
+  if (warp == 12) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(128));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int HW = g.ho * g.wo;
+
+  if (warp < 8) {
+    // ---------------- patch gather: two groups of 4 warps take alternate
+    // tiles (two tiles' loads in flight); row r of a tile = one output pixel
+    const int grp = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    for (int i = grp;; i += 2) {
+      const int t = blockIdx.x + i * gridDim.x;
+      if (t >= n_tiles) break;
+      const int stage = i % STEM_STAGES;
+      const uint32_t phase = (uint32_t)(i / STEM_STAGES) & 1u;
+      if (!mbar_wait(&aempty[stage], phase ^ 1, abort_flag, 51)) break;
+      const int64_t m = (int64_t)t * 128 + r;
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = 0.f;
+      if (m < M) {
+        const int img = (int)(m / HW), rem = (int)(m % HW);
+        const int oh = rem / g.wo, ow = rem % g.wo;
+        const int ih0 = oh * g.g.sh - g.g.ph0, iw0 = ow * g.g.sw - g.g.pw0;
+        const float* xb = x + (int64_t)img * g.c * g.h * g.w + (int64_t)ih0 * g.w + iw0;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int4 e = ktab[k];  // broadcast read
+          const int ih = ih0 + e.y, iw = iw0 + e.z;
+          if (e.w && ih >= 0 && ih < g.h && iw >= 0 && iw < g.w) v[k] = __ldg(xb + e.x);
+        }
+      }
+      uint8_t* row = sa + (size_t)stage * 16384 + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        __align__(16) __nv_bfloat162 o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(v[c * 8 + 2 * j], v[c * 8 + 2 * j + 1]);
+        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[stage]);
+    }
+  } else if (warp < 12) {
+    // ---------------- epilogue: TMEM lane quarter q = warp % 4
+    const int q = warp & 3;
+    uint8_t* tile = so + (size_t)q * 4096;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 52);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      float v[64];
+      tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 64), v);
+      tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 64 + 32), v + 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(bias) + i);
+        v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+      }
+      act_inplace<64>(v, act, true);
+      if (lane == 0) bulk_wait_read0();  // the previous store has read the tile
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        __align__(16) __nv_bfloat162 o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(v[c * 8 + 2 * j], v[c * 8 + 2 * j + 1]);
+        *reinterpret_cast<uint4*>(tile + lane * 128 + ((c ^ (lane & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      const int64_t row0 = (int64_t)t * 128 + q * 32;
+      if (lane == 0 && row0 < M) {
+        tma_store_2d(&maps.out, tile, 0, (int)row0);
+        bulk_commit();
+      }
+    }
+    if (lane == 0) bulk_wait0();
+  } else if (lane == 0) {
+    // ---------------- MMA issue
+    const uint32_t idesc = instr_desc(BM, 64);
+    const uint64_t ad0 = smem_desc(smem_u32(sa)), bd = smem_desc(smem_u32(sbw));
+    int stage = 0, acc = 0;
+    uint32_t phase = 0, acc_phase = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 53)) break;
+      if (!mbar_wait(&afull[stage], phase, abort_flag, 54)) break;
+      tc_fence_after();
+      const uint64_t ad = ad0 + (uint64_t)stage * (16384 >> 4);
+      const uint32_t d = tmem_base + (uint32_t)(acc * 64);
+      mma_bf16(d, ad, bd, idesc, 0u);
+      mma_bf16(d, ad + 2, bd + 2, idesc, 1u);  // K 16..31 (32 bytes further)
+      mma_commit(&aempty[stage]);
+      mma_commit(&tfull[acc]);
+      if (++stage == STEM_STAGES) { stage = 0; phase ^= 1; }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  if (warp == 12) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(128));
+  }
+}
+
 }  // namespace tc
 
 // ------------------------------------------------------------------ host side
@@ -1708,6 +1896,45 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   }
   if ((rc = enable_tma_out(maps, a))) return rc;
   return launch_tc(maps, a, s);
+}
+
+// Tensor-core stem (tc_stem_kernel): Cout 64, Cin*kh*kw <= 32, bf16 output.
+// Returns false when the shape is not eligible (the caller falls back).
+// C3B200_STEM=mma selects the mma.sync stem instead (A/B timing).
+bool launch_stem_tc(const c3b_tensor* in, const c3b_tensor& out, const c3b_stem_conv_params& p, cudaStream_t s,
+                    int* rc) {
+  static const bool off = [] {
+    const char* e = getenv("C3B200_STEM");
+    return e && std::string(e) == "mma";
+  }();
+  const c3b_stem_params& g = p.geom;
+  *rc = C3B_OK;
+  if (off || p.cout != 64 || g.c * g.g.kh * g.g.kw > 32 || ((uintptr_t)in[2].ptr & 15)) return false;
+  const int64_t M = (int64_t)g.n * g.ho * g.wo;
+  if (M >= ((int64_t)1 << 31)) return false;
+  tc::TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  uint64_t dims[2] = {64, (uint64_t)M};
+  uint64_t str[1] = {128};
+  uint32_t box[2] = {64, 32};
+  if ((*rc = encode(&maps.out, out.ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return true;
+  const size_t smem = 1024 + tc::STEM_STAGES * 16384 + 8192 + 4 * 4096 + 32 * 16 + (2 * tc::STEM_STAGES + 4) * 8 + 16;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(tc::tc_stem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      *rc = fail(C3B_E_CUDA, std::string("stem attribute: ") + cudaGetErrorString(e));
+      return true;
+    }
+    attr = true;
+  }
+  const int n_tiles = (int)((M + 127) / 128);
+  const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
+  tc::tc_stem_kernel<<<grid, tc::STEM_THREADS, smem, s>>>(maps, (const float*)in[0].ptr, (const float*)in[1].ptr,
+                                                          (const float*)in[2].ptr, g, p.act, M, n_tiles);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) *rc = fail(C3B_E_CUDA, std::string("stem launch: ") + cudaGetErrorString(e));
+  return true;
 }
 
 }  // namespace c3b

@@ -880,7 +880,9 @@ int launch_stem_conv(const c3b_tensor* in, int n_in, const c3b_tensor& out, cons
   C3B_REQUIRE((uintptr_t)out.ptr % 16 == 0, "stem conv: output alignment");
   if (M == 0) return C3B_OK;
   C3B_REQUIRE((uintptr_t)in[1].ptr % 16 == 0, "stem conv: weight alignment");
-  if (launch_stem_mma(in, out, p, s)) {  // tensor-core path (Cout 64, K <= 32)
+  int trc = C3B_OK;
+  if (launch_stem_tc(in, out, p, s, &trc)) return trc;  // tcgen05 path (Cout 64, K <= 32)
+  if (launch_stem_mma(in, out, p, s)) {  // mma.sync path (Cout 64, K <= 32)
     C3B_CHECK_CUDA(cudaGetLastError());
     return C3B_OK;
   }
