@@ -1195,6 +1195,47 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
         cbase += SR + 2;
       }
     }
+  } else if (!a.res) {
+    // Epilogue without a residual: direct 16-byte stores from registers.
+    // (Measured ~4% faster than the staged tiles below, which leave shared
+    // memory bandwidth to the MMAs; with a residual the staged path is 23%
+    // faster because the residual arrives in whole rows.)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int cols = a.block_n >> 1;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool run = true;
+    for (int u = blockIdx.x; u < a.n_items && run; u += gridDim.x) {
+      const int seg = u % a.segs;
+      const int strip = u / a.segs;
+      const int wb = strip % a.wblocks, ib = strip / a.wblocks;
+      const int m = q * 32 + lane;
+      const int img = ib * a.img + (m % a.img);
+      const int w = wb * a.wt + m / a.img;
+      const bool img_ok = img < a.n_img;
+      const int64_t col_base = half * cols;
+      for (int pr = 0; pr < SR / 2; ++pr) {
+        const int hrow = seg * SR + 2 * pr;
+        const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 35);
+        if (!__all_sync(0xffffffffu, ok)) { run = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int64_t pix = ((int64_t)img * a.ho + hrow + j) * a.wo + w;
+          const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) +
+                              (uint32_t)((acc * 2 + j) * a.block_n + half * cols);
+          float v[32];
+          tmem_ld32(tb, v);
+          if (img_ok) store32_bf16(a, pix * a.N + col_base, col_base, v, nullptr);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+
   } else {
     // Epilogue: warp (q, half) owns TMEM lanes 32q..32q+31 (pixels) and
     // channels 32*half..+31 of both output rows.  Its residual rows arrive by
