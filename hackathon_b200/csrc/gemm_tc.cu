@@ -500,6 +500,10 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the prologue above (barriers, TMEM, tensor
+  // maps, constant weights) may overlap the previous kernel's tail; every
+  // activation read and every global write comes after it has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -834,6 +838,10 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the prologue above (barriers, TMEM, tensor
+  // maps, constant weights) may overlap the previous kernel's tail; every
+  // activation read and every global write comes after it has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1112,6 +1120,10 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the prologue above (barriers, TMEM, tensor
+  // maps, constant weights) may overlap the previous kernel's tail; every
+  // activation read and every global write comes after it has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1406,6 +1418,10 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the prologue above (barriers, TMEM, tensor
+  // maps, constant weights) may overlap the previous kernel's tail; every
+  // activation read and every global write comes after it has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int HW = g.ho * g.wo;
 
   if (warp < 8) {
@@ -1540,6 +1556,29 @@ static EncodeTiledFn get_encode() {
   return fn;
 }
 
+// Launch with programmatic stream serialisation (the kernels wait on
+// griddepcontrol before touching activations), so a kernel's prologue overlaps
+// the tail of the one before it.  C3B200_PDL=0 launches plainly (A/B timing).
+template <typename Kern, typename... Args>
+static int launch_pdl(Kern kernel, int grid, int block, size_t smem, cudaStream_t s, Args... args) {
+  static const bool pdl = [] {
+    const char* e = getenv("C3B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  C3B_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...));
+  return C3B_OK;
+}
+
 static int encode(CUtensorMap* m, void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                   const uint32_t* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
                   CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
@@ -1601,7 +1640,7 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
   }
   int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
   if (grid < 1) return C3B_OK;
-  tc::tc_gemm_kernel<MODE><<<grid, tc::HALO16_THREADS, smem, s>>>(maps, a);
+  if (int rc = launch_pdl(tc::tc_gemm_kernel<MODE>, grid, tc::HALO16_THREADS, smem, s, maps, a)) return rc;
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
@@ -1870,7 +1909,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
             attr_ring = true;
           }
           int grid = a.n_items < sm_count() ? a.n_items : sm_count();
-          tc::tc_conv_rowring_kernel<<<grid, tc::HALO_THREADS, smem, s>>>(maps, a);
+          if ((rc = launch_pdl(tc::tc_conv_rowring_kernel, grid, tc::HALO_THREADS, smem, s, maps, a))) return rc;
           C3B_CHECK_CUDA(cudaGetLastError());
           return C3B_OK;
         }
@@ -1916,7 +1955,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
       attr_halo = true;
     }
     int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
-    tc::tc_conv_halo_kernel<<<grid, tc::HALO16_THREADS, smem, s>>>(maps, a);
+    if ((rc = launch_pdl(tc::tc_conv_halo_kernel, grid, tc::HALO16_THREADS, smem, s, maps, a))) return rc;
     C3B_CHECK_CUDA(cudaGetLastError());
     return C3B_OK;
   }
@@ -1971,10 +2010,8 @@ bool launch_stem_tc(const c3b_tensor* in, const c3b_tensor& out, const c3b_stem_
   }
   const int n_tiles = (int)((M + 127) / 128);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
-  tc::tc_stem_kernel<<<grid, tc::STEM_THREADS, smem, s>>>(maps, (const float*)in[0].ptr, (const float*)in[1].ptr,
-                                                          (const float*)in[2].ptr, g, p.act, M, n_tiles);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) *rc = fail(C3B_E_CUDA, std::string("stem launch: ") + cudaGetErrorString(e));
+  *rc = launch_pdl(tc::tc_stem_kernel, grid, tc::STEM_THREADS, smem, s, maps, (const float*)in[0].ptr,
+                   (const float*)in[1].ptr, (const float*)in[2].ptr, g, p.act, M, n_tiles);
   return true;
 }
 
