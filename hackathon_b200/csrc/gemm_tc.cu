@@ -1875,7 +1875,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
       // row ring: strips of IMG images x WT columns, segments of seg_rows rows
       const int strips = ((p.n + a.img - 1) / a.img) * a.wblocks;
       int segs = 1;
-      while (strips * segs < 8 * sm_count() && segs * 2 <= p.ho / 2) segs *= 2;
+      while (strips * segs < 4 * sm_count() && segs * 2 <= p.ho / 2) segs *= 2;  // ~4 items per CTA (measured best of 2, 4, 8)
       if (p.ho % (2 * segs) == 0) {
         a.segs = segs;
         a.seg_rows = p.ho / segs;
