@@ -1444,11 +1444,33 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
         const int oh = rem / g.wo, ow = rem % g.wo;
         const int ih0 = oh * g.g.sh - g.g.ph0, iw0 = ow * g.g.sw - g.g.pw0;
         const float* xb = x + (int64_t)img * g.c * g.h * g.w + (int64_t)ih0 * g.w + iw0;
+        if (g.g.kh == 3 && g.g.kw == 3 && g.g.dh == 1 && g.g.dw == 1) {
+          // 3x3, dilation 1 (C <= 3): three row and three column flags per
+          // pixel, then one predicated load per element at a fixed offset
+          bool rok[3], cok[3];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const int4 e = ktab[k];  // broadcast read
-          const int ih = ih0 + e.y, iw = iw0 + e.z;
-          if (e.w && ih >= 0 && ih < g.h && iw >= 0 && iw < g.w) v[k] = __ldg(xb + e.x);
+          for (int i = 0; i < 3; ++i) {
+            rok[i] = ih0 + i >= 0 && ih0 + i < g.h;
+            cok[i] = iw0 + i >= 0 && iw0 + i < g.w;
+          }
+          const int64_t hw = (int64_t)g.h * g.w;
+#pragma unroll
+          for (int c = 0; c < 3; ++c) {
+            if (c < g.c) {
+#pragma unroll
+              for (int r = 0; r < 3; ++r)
+#pragma unroll
+                for (int q = 0; q < 3; ++q)
+                  if (rok[r] && cok[q]) v[c * 9 + r * 3 + q] = __ldg(xb + c * hw + r * g.w + q);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const int4 e = ktab[k];  // broadcast read
+            const int ih = ih0 + e.y, iw = iw0 + e.z;
+            if (e.w && ih >= 0 && ih < g.h && iw >= 0 && iw < g.w) v[k] = __ldg(xb + e.x);
+          }
         }
       }
       uint8_t* row = sa + (size_t)stage * 16384 + r * 128;

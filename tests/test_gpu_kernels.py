@@ -582,3 +582,31 @@ def test_dequant_fp4_bit_exact(torch_cuda, N, K):
              torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert np.array_equal(out.float().cpu().numpy(), rb(F.dequant(qp, qs)))
+
+
+@pytest.mark.parametrize("n,c,hw,k,stride,pad", [(3, 1, 30, 5, 2, 2), (2, 3, 31, 3, 2, 1), (5, 2, 20, 3, 1, 1)])
+def test_stem_conv_geometries(torch_cuda, n, c, hw, k, stride, pad):
+    """The tcgen05 stem on other geometries: 5x5 stride 2 with one channel
+    (K offsets from the table), 3x3 stride 2 on odd sizes, two channels; pixel
+    counts that leave a partial last 128-pixel tile."""
+    import torch
+    from hackathon_b200 import _lib as L
+    cout = 64
+    x, w, b = randn(n, c, hw, hw), randn(cout, c, k, k) * 0.3, randn(cout)
+    ref = np.maximum(O.conv2d(x, w, b, strides=[stride, stride], pads=[pad] * 4), 0)
+    ho = ref.shape[2]
+    wk = np.ascontiguousarray(w.reshape(cout, -1).T)
+    tx, tw, tb = dev(torch, x), dev(torch, wk), dev(torch, b)
+    M = n * ho * ho
+    out = torch.empty((M, cout), dtype=torch.bfloat16, device="cuda")
+    sp = L.StemParams()
+    sp.n, sp.c, sp.h, sp.w, sp.ho, sp.wo, sp.kpad = n, c, hw, hw, ho, ho, 0
+    sp.g = L.ConvGeom(k, k, stride, stride, pad, pad, pad, pad, 1, 1)
+    L.launch(L.K_STEM_CONV, [L.make_tensor(tx.data_ptr(), L.F32, x.shape), L.make_tensor(tw.data_ptr(), L.F32, wk.shape),
+                             L.make_tensor(tb.data_ptr(), L.F32, b.shape)],
+             [L.make_tensor(out.data_ptr(), L.BF16, (M, cout))], L.StemConvParams(sp, cout, 1),
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    got = out.float().cpu().numpy().reshape(n, ho, ho, cout).transpose(0, 3, 1, 2)
+    assert rel(got, ref) < 8e-3
