@@ -14,6 +14,7 @@
 //   ATTN      fused_attention_scores (engine.py:1250-1380)
 //   GATHER    gather (kernel_registry.py:744-752)
 #include <algorithm>
+#include <cuda_fp8.h>
 #include "common.cuh"
 
 namespace c3b {
@@ -457,6 +458,91 @@ __global__ void __launch_bounds__(256) layernorm_vec_kernel(const TI* __restrict
   }
 }
 
+// LayerNorm with the fp8 path's rowwise E4M3 quantisation fused into the
+// store: the normalised fp32 row (one warp, in registers) gives
+// scale = max|y| / 448 (1 for an all-zero row) and bytes E4M3(y / scale),
+// round-to-nearest-even, saturating — C3B_K_QUANT_E4M3's scheme applied to
+// the fp32 values instead of a stored bf16 copy.
+template <typename TI, int V>
+__global__ void __launch_bounds__(256) layernorm_e4m3_kernel(const TI* __restrict__ x, const TI* __restrict__ res,
+                                                             const float* __restrict__ scale,
+                                                             const float* __restrict__ bias, uint8_t* __restrict__ q,
+                                                             float* __restrict__ qscale, int64_t rows, float eps) {
+  constexpr int COLS = 128 * V;
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {
+    const int64_t base = row * COLS;
+    float v[V][4];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = i * 128 + lane * 4;
+      ld4(x + base + c, v[i]);
+      if (res) {
+        float r[4];
+        ld4(res + base + c, r);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] += r[j];
+      }
+      s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+    }
+    const float mean = warp_sum(s) * (1.0f / COLS);
+    float qq = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float d = v[i][j] - mean;
+        qq += d * d;
+      }
+    const float inv = rsqrtf(warp_sum(qq) * (1.0f / COLS) + eps);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = i * 128 + lane * 4;
+      const float4 g = *reinterpret_cast<const float4*>(scale + c);
+      float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (bias) b = *reinterpret_cast<const float4*>(bias + c);
+      v[i][0] = (v[i][0] - mean) * inv * g.x + b.x;
+      v[i][1] = (v[i][1] - mean) * inv * g.y + b.y;
+      v[i][2] = (v[i][2] - mean) * inv * g.z + b.z;
+      v[i][3] = (v[i][3] - mean) * inv * g.w + b.w;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+    }
+    amax = warp_max(amax);
+    const float sc = amax > 0.f ? amax / 448.0f : 1.0f;
+    if (lane == 0) qscale[row] = sc;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = i * 128 + lane * 4;
+      __align__(4) __nv_fp8x2_storage_t o[2];
+      o[0] = __nv_cvt_float2_to_fp8x2(make_float2(v[i][0] / sc, v[i][1] / sc), __NV_SATFINITE, __NV_E4M3);
+      o[1] = __nv_cvt_float2_to_fp8x2(make_float2(v[i][2] / sc, v[i][3] / sc), __NV_SATFINITE, __NV_E4M3);
+      *reinterpret_cast<uint32_t*>(q + base + c) = *reinterpret_cast<const uint32_t*>(o);
+    }
+  }
+}
+
+template <typename TI>
+static bool launch_ln_e4m3(const void* x, const void* r, const float* sc, const float* b, void* q, void* qs,
+                           int64_t rows, int64_t cols, float eps, cudaStream_t s, int grid) {
+#define C3B_LNQ(V)                                                                                       \
+  layernorm_e4m3_kernel<TI, V><<<grid, 256, 0, s>>>((const TI*)x, (const TI*)r, sc, b, (uint8_t*)q, (float*)qs, \
+                                                    rows, eps);                                            \
+  return true;
+  switch (cols) {
+    case 128: C3B_LNQ(1)
+    case 256: C3B_LNQ(2)
+    case 512: C3B_LNQ(4)
+    case 1024: C3B_LNQ(8)
+    case 2048: C3B_LNQ(16)
+  }
+#undef C3B_LNQ
+  return false;
+}
+
 template <typename TI, typename TO>
 static bool launch_ln_vec(const void* x, const void* r, const float* sc, const float* b, void* y, int64_t rows,
                           int64_t cols, float eps, cudaStream_t s, int grid) {
@@ -478,6 +564,34 @@ int launch_layernorm(const c3b_tensor* in, int n_in, const c3b_tensor* out, int 
                      const c3b_layernorm_params& p, cudaStream_t s) {
   int need = 2 + p.has_residual + p.has_bias;
   C3B_REQUIRE(n_in == need, "layernorm: input count does not match flags");
+  if (n_out >= 1 && out[0].dtype == C3B_U8) {
+    // fp8 path: outputs E4M3 bytes [rows, cols] and the row scales f32 [rows]
+    C3B_REQUIRE(n_out == 2 && !p.write_sum && out[1].dtype == C3B_F32, "layernorm e4m3: outputs q (u8), scale (f32)");
+    const c3b_tensor& x = in[0];
+    const c3b_tensor* res = p.has_residual ? &in[1] : nullptr;
+    const c3b_tensor& sc = in[1 + p.has_residual];
+    const c3b_tensor* bi = p.has_bias ? &in[2 + p.has_residual] : nullptr;
+    C3B_REQUIRE(numel(x) == p.rows * p.cols && numel(out[0]) >= p.rows * p.cols && numel(out[1]) >= p.rows,
+                "layernorm e4m3: extents");
+    C3B_REQUIRE((x.dtype == C3B_F32 || x.dtype == C3B_BF16) && (!res || res->dtype == x.dtype) &&
+                    sc.dtype == C3B_F32 && (!bi || bi->dtype == C3B_F32),
+                "layernorm e4m3: f32/bf16 input, f32 scale and bias");
+    C3B_REQUIRE((uintptr_t)x.ptr % 16 == 0 && (!res || (uintptr_t)res->ptr % 16 == 0) && (uintptr_t)sc.ptr % 16 == 0 &&
+                    (!bi || (uintptr_t)bi->ptr % 16 == 0) && (uintptr_t)out[0].ptr % 4 == 0,
+                "layernorm e4m3: alignment");
+    if (p.rows == 0) return C3B_OK;
+    const int gv = (int)std::min<int64_t>((p.rows * 32 + 255) / 256, (int64_t)sm_count() * 16);
+    const void* rp = res ? res->ptr : nullptr;
+    const float* bp = bi ? (const float*)bi->ptr : nullptr;
+    const bool ok = x.dtype == C3B_F32
+                        ? launch_ln_e4m3<float>(x.ptr, rp, (const float*)sc.ptr, bp, out[0].ptr, out[1].ptr, p.rows,
+                                                p.cols, p.epsilon, s, gv)
+                        : launch_ln_e4m3<__nv_bfloat16>(x.ptr, rp, (const float*)sc.ptr, bp, out[0].ptr, out[1].ptr,
+                                                        p.rows, p.cols, p.epsilon, s, gv);
+    C3B_REQUIRE(ok, "layernorm e4m3: cols must be 128, 256, 512, 1024 or 2048");
+    C3B_CHECK_CUDA(cudaGetLastError());
+    return C3B_OK;
+  }
   C3B_REQUIRE(n_out == 1 + (p.write_sum ? 1 : 0), "layernorm: output count does not match flags");
   const c3b_tensor& x = in[0];
   const c3b_tensor* res = p.has_residual ? &in[1] : nullptr;

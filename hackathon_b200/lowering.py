@@ -86,6 +86,7 @@ class _State:
         self.layout: Dict[str, str] = {}  # program tensor -> "nchw" | "nhwc" | "rows"
         self.lshape: Dict[str, Tuple[int, ...]] = {}  # logical (ONNX) shape of a program tensor
         self.ops: List[dict] = []         # fused ops before topological ordering
+        self.fused_q: Dict[str, Tuple[str, str]] = {}  # LayerNorm output -> (E4M3 bytes, row scales)
         self.wcount = 0
 
     def node(self, i):
@@ -413,6 +414,25 @@ def _gemm_tc_launch(d: Dict[str, Desc], x, w, b, out, M, N, K, act, res=None):
     return Launch(L.K_GEMM_TC, ins, [d[out].t((M, N))], g)
 
 
+def _f8_linear(st: _State, op: dict, K: int) -> bool:
+    """The fp8 rule of the linear lowering (c32/strategy.py:150-157) for ``op``."""
+    N = op["w"].shape[0]
+    return (st.profile == "fp8" and N % 32 == 0 and K % 64 == 0 and N % 16 == 0 and K >= 64 and N >= 64
+            and op.get("alpha", 1.0) == 1.0)
+
+
+def _ln_feeds_f8_linear(st: _State, op: dict, cols: int) -> bool:
+    """True when the LayerNorm output's only consumer is a linear that takes the
+    fp8 path, so the LayerNorm can write E4M3 bytes for it directly."""
+    if st.profile != "fp8" or cols not in (128, 256, 512, 1024, 2048):
+        return False
+    out = op["out"]
+    if any(o.name == out for o in st.g.outputs):
+        return False
+    users = [o for o in st.ops if out in (o.get("x"), o.get("res")) or out in (o.get("xs") or [])]
+    return len(users) == 1 and users[0]["kind"] == "linear" and users[0]["x"] == out and _f8_linear(st, users[0], cols)
+
+
 def _emit(st: _State, op: dict) -> None:
     P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp8", "mixed")
     k = op["kind"]
@@ -541,8 +561,23 @@ def _emit(st: _State, op: dict) -> None:
         sname = st.weight("ln_scale", op["scale"].astype(np.float32), L.F32)
         bname = st.weight("ln_bias", op["bias"].astype(np.float32), L.F32) if op["bias"] is not None else None
         out = op["out"]
-        P.add_tensor(out, (rows, cols), L.BF16 if bf else L.F32)
         lp = L.LayerNormParams(rows, cols, op["eps"], 0, int(bname is not None), 0)
+        if _ln_feeds_f8_linear(st, op, cols):
+            # the only consumer is an fp8 linear: LayerNorm writes its E4M3
+            # bytes and row scales directly (no bf16 copy, no quant step)
+            xq, xs = f"{out}:xq", f"{out}:xs"
+            P.add_tensor(xq, (rows, cols), L.U8)
+            P.add_tensor(xs, (rows,), L.F32)
+            st.fused_q[out] = (xq, xs)
+
+            def build_q(d, x=x, sname=sname, bname=bname, xq=xq, xs=xs, lp=lp, rows=rows, cols=cols):
+                ins = [d[x].t((rows, cols)), d[sname].t()] + ([d[bname].t()] if bname else [])
+                return [Launch(L.K_LAYERNORM, ins, [d[xq].t(), d[xs].t()], lp)]
+            P.add_step("layernorm_e4m3", [x, sname] + ([bname] if bname else []), [xq, xs], build_q, 0.0)
+            st.layout[out] = "rows"
+            st.lshape[out] = shp
+            return
+        P.add_tensor(out, (rows, cols), L.BF16 if bf else L.F32)
 
         def build(d, x=x, sname=sname, bname=bname, out=out, lp=lp, rows=rows, cols=cols):
             ins = [d[x].t((rows, cols)), d[sname].t()] + ([d[bname].t()] if bname else [])
@@ -574,7 +609,7 @@ def _emit(st: _State, op: dict) -> None:
         res = st.t(op["res"]) if op["res"] else None
         out = op["out"]
         flops = 2.0 * M * N * K
-        use_tc = bf and N % 32 == 0 and K % 64 == 0 and P.tensors[x].dtype == L.BF16
+        use_tc = bf and N % 32 == 0 and K % 64 == 0 and (x in st.fused_q or P.tensors[x].dtype == L.BF16)
         bname = st.weight("bias", (op["b"] * op.get("beta", 1.0)).astype(np.float32), L.F32) \
             if op["b"] is not None else None
         # the reference policy for GEMMs (c32/strategy.py:146-157): fp4 (W4A16)
@@ -625,13 +660,16 @@ def _emit(st: _State, op: dict) -> None:
             wsn = st.weight("linear_e4m3_scale", ws, L.F32)
             odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else L.BF16
             P.add_tensor(out, (M, N), odt)
-            xq, xs = f"{out}:xq", f"{out}:xs"
-            P.add_tensor(xq, (M, K), L.U8)
-            P.add_tensor(xs, (M,), L.F32)
+            if x in st.fused_q:  # quantised by the producing LayerNorm
+                xq, xs = st.fused_q[x]
+            else:
+                xq, xs = f"{out}:xq", f"{out}:xs"
+                P.add_tensor(xq, (M, K), L.U8)
+                P.add_tensor(xs, (M,), L.F32)
 
-            def build_q(d, x=x, xq=xq, xs=xs, M=M, K=K):
-                return [Launch(L.K_QUANT_E4M3, [d[x].t((M, K))], [d[xq].t(), d[xs].t()], L.QuantParams(M, K))]
-            P.add_step("quant_e4m3", [x], [xq, xs], build_q, 0.0)
+                def build_q(d, x=x, xq=xq, xs=xs, M=M, K=K):
+                    return [Launch(L.K_QUANT_E4M3, [d[x].t((M, K))], [d[xq].t(), d[xs].t()], L.QuantParams(M, K))]
+                P.add_step("quant_e4m3", [x], [xq, xs], build_q, 0.0)
 
             def build(d, xq=xq, xs=xs, wqn=wqn, wsn=wsn, bname=bname, out=out, M=M, N=N, K=K, act=op["act"],
                       res=res):

@@ -153,7 +153,10 @@ typedef struct {
 } c3b_gemm_params;
 
 /* --- C3B_K_LAYERNORM: rows x cols, optional residual (LN(x + r)), bias.
- * inputs: x, [residual], scale, [bias] ; outputs: y, [x+r when write_sum]. */
+ * inputs: x, [residual], scale, [bias] ; outputs: y, [x+r when write_sum].
+ * fp8 path: when outputs[0] is u8 the outputs are E4M3 bytes [rows, cols] and
+ * f32 row scales [rows] with C3B_K_QUANT_E4M3's rowwise scheme applied to the
+ * fp32 normalised values (cols 128, 256, 512, 1024 or 2048). */
 typedef struct {
   int64_t rows, cols;
   float epsilon;

@@ -610,3 +610,35 @@ def test_stem_conv_geometries(torch_cuda, n, c, hw, k, stride, pad):
     assert L.device_status() == 0
     got = out.float().cpu().numpy().reshape(n, ho, ho, cout).transpose(0, 3, 1, 2)
     assert rel(got, ref) < 8e-3
+
+
+@pytest.mark.parametrize("dt,cols", [("f32", 1024), ("bf16", 256), ("f32", 2048)])
+def test_layernorm_e4m3(torch_cuda, dt, cols):
+    """LayerNorm writing E4M3 bytes and row scales (fp8 path) against the
+    oracle LayerNorm followed by the oracle's rowwise E4M3 scheme: scales to
+    fp32 rounding, values to E4M3 precision (3 mantissa bits; below 2^-6 of the
+    scale, the subnormal spacing 2^-9)."""
+    import torch
+    from hackathon_b200 import _lib as L
+    from oracle import fp8 as F
+    rows = 300
+    x = randn(rows, cols) * np.float32(3.0) + np.float32(0.5)
+    if dt == "bf16":
+        x = round_bf16(x)
+    g, b = randn(cols), randn(cols) * np.float32(0.1)
+    ref = O.layer_norm(x, g, b, epsilon=1e-5).astype(np.float32)
+    _, sref = F.quant_rows(ref)
+    xd = _bf16(torch, x) if dt == "bf16" else dev(torch, x)
+    tg, tb = dev(torch, g), dev(torch, b)
+    q = torch.empty((rows, cols), dtype=torch.uint8, device="cuda")
+    s = torch.empty((rows,), dtype=torch.float32, device="cuda")
+    L.launch(L.K_LAYERNORM, [L.make_tensor(xd.data_ptr(), L.BF16 if dt == "bf16" else L.F32, (rows, cols)),
+                             L.make_tensor(tg.data_ptr(), L.F32, (cols,)), L.make_tensor(tb.data_ptr(), L.F32, (cols,))],
+             [L.make_tensor(q.data_ptr(), L.U8, (rows, cols)), L.make_tensor(s.data_ptr(), L.F32, (rows,))],
+             L.LayerNormParams(rows, cols, 1e-5, 0, 1, 0), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    sg = host(s)
+    assert np.allclose(sg, sref, rtol=1e-5, atol=0)
+    deq = F.e4m3_decode(host(q)) * sg[:, None]
+    err = np.abs(deq - ref)
+    assert np.all(err <= np.abs(ref) * 2.0 ** -4 + sg[:, None] * 2.0 ** -9 * 1.01)
