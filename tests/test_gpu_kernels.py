@@ -339,7 +339,7 @@ def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res, mode):
 
 
 @pytest.mark.parametrize("dt", ["f32", "bf16"])
-@pytest.mark.parametrize("B,S,H", [(2, 128, 4), (1, 200, 2), (3, 64, 1)])
+@pytest.mark.parametrize("B,S,H", [(2, 128, 4), (1, 200, 2), (3, 64, 1), (2, 512, 3), (1, 384, 16)])
 def test_flash_attention(torch_cuda, dt, B, S, H):
     import torch
     from hackathon_b200 import _lib as L
@@ -356,6 +356,7 @@ def test_flash_attention(torch_cuda, dt, B, S, H):
     L.launch(L.K_FLASH_ATTN, [L.make_tensor(tq.data_ptr(), code, (B, S, 3, H, D))],
              [L.make_tensor(out.data_ptr(), code, (B, S, H * D))], fp, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
+    assert L.device_status() == 0
     got = out.float().cpu().numpy()
     assert rel(got, ref) < (RTOL if dt == "f32" else 2e-2)
 
