@@ -80,7 +80,9 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // Byte offset of (row, 16-byte chunk) in a 64x64 bf16 tile with XOR swizzle.
 __device__ __forceinline__ uint32_t swz(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
 
-__global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16* __restrict__ qkv,
+// MINB = resident CTAs per SM the register allocation is capped for.
+template <int MINB>
+__global__ void __launch_bounds__(fam::NT, MINB) flash_mma_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                             __nv_bfloat16* __restrict__ out, c3b_flash_params p) {
   using namespace fam;
   __shared__ __align__(128) uint8_t Ks[2][KB * D * 2];
@@ -166,7 +168,8 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
         mma16816(s[nb], qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], b2, b3);
       }
     }
-    // scale, mask, running max
+    // Mask and running max on the raw scores; the scale (positive) is applied
+    // to the maxima and folded into the exponent's FMA below.
     const int k0 = kt * KB;
     // Only the diagonal tile (causal) and the sequence tail need masking.
     const bool need_mask = (p.causal && k0 + KB > qb * QB) || (k0 + KB > p.seq);
@@ -175,23 +178,20 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
     for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const int key = k0 + nb * 8 + 2 * t + j;
-        float v0 = s[nb][j] * sl2, v1 = s[nb][2 + j] * sl2;
         if (need_mask) {
-          if (key >= p.seq || (p.causal && key > row0)) v0 = -INFINITY;
-          if (key >= p.seq || (p.causal && key > row1)) v1 = -INFINITY;
+          const int key = k0 + nb * 8 + 2 * t + j;
+          if (key >= p.seq || (p.causal && key > row0)) s[nb][j] = -INFINITY;
+          if (key >= p.seq || (p.causal && key > row1)) s[nb][2 + j] = -INFINITY;
         }
-        s[nb][j] = v0;
-        s[nb][2 + j] = v1;
-        mx0 = fmaxf(mx0, v0);
-        mx1 = fmaxf(mx1, v1);
+        mx0 = fmaxf(mx0, s[nb][j]);
+        mx1 = fmaxf(mx1, s[nb][2 + j]);
       }
     }
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float mn0 = fmaxf(m0, mx0 * sl2), mn1 = fmaxf(m1, mx1 * sl2);
     const float c0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
     const float c1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
     m0 = mn0;
@@ -205,15 +205,15 @@ __global__ void __launch_bounds__(fam::NT) flash_mma_kernel(const __nv_bfloat16*
       // sm_100 (ncu: XU pipe 72% busy with all exponentials on the SFU).
       float p00, p01, p10, p11;
       if ((nb & 3) != 0) {
-        p00 = exp2_fma(s[nb][0] - mn0);
-        p01 = exp2_fma(s[nb][1] - mn0);
-        p10 = exp2_fma(s[nb][2] - mn1);
-        p11 = exp2_fma(s[nb][3] - mn1);
+        p00 = exp2_fma(fmaf(s[nb][0], sl2, -mn0));
+        p01 = exp2_fma(fmaf(s[nb][1], sl2, -mn0));
+        p10 = exp2_fma(fmaf(s[nb][2], sl2, -mn1));
+        p11 = exp2_fma(fmaf(s[nb][3], sl2, -mn1));
       } else {
-        p00 = exp2f(s[nb][0] - mn0);
-        p01 = exp2f(s[nb][1] - mn0);
-        p10 = exp2f(s[nb][2] - mn1);
-        p11 = exp2f(s[nb][3] - mn1);
+        p00 = exp2f(fmaf(s[nb][0], sl2, -mn0));
+        p01 = exp2f(fmaf(s[nb][1], sl2, -mn0));
+        p10 = exp2f(fmaf(s[nb][2], sl2, -mn1));
+        p11 = exp2f(fmaf(s[nb][3], sl2, -mn1));
       }
       if (mn0 == -INFINITY) p00 = p01 = 0.f;
       if (mn1 == -INFINITY) p10 = p11 = 0.f;
@@ -269,7 +269,16 @@ int launch_flash_mma(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_fla
   C3B_REQUIRE(((uintptr_t)qkv.ptr & 15) == 0 && ((uintptr_t)out.ptr & 3) == 0, "flash attention: alignment");
   const int64_t blocks = (int64_t)p.batch * p.heads * ((p.seq + fam::QB - 1) / fam::QB);
   C3B_REQUIRE(blocks < ((int64_t)1 << 31), "flash attention: grid too large");
-  flash_mma_kernel<<<(unsigned)blocks, fam::NT, 0, s>>>((const __nv_bfloat16*)qkv.ptr, (__nv_bfloat16*)out.ptr, p);
+  // C3B200_FLASH_OCC=1 selects the uncapped register allocation (3 CTAs per
+  // SM) for A/B comparisons; the default caps registers for 4 CTAs per SM.
+  static const int occ = [] {
+    const char* e = getenv("C3B200_FLASH_OCC");
+    return (e && atoi(e) == 1) ? 1 : 4;
+  }();
+  if (occ == 1)
+    flash_mma_kernel<1><<<(unsigned)blocks, fam::NT, 0, s>>>((const __nv_bfloat16*)qkv.ptr, (__nv_bfloat16*)out.ptr, p);
+  else
+    flash_mma_kernel<4><<<(unsigned)blocks, fam::NT, 0, s>>>((const __nv_bfloat16*)qkv.ptr, (__nv_bfloat16*)out.ptr, p);
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
