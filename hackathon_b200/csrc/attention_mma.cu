@@ -50,11 +50,15 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// 2^x for x <= 0 on the FMA/ALU pipes: Cody-Waite split x = n + f with
+// 2^x for x <= 8 on the FMA/ALU pipes: Cody-Waite split x = n + f with
 // f in [-0.5, 0.5] (round-to-nearest through the 1.5*2^23 shifter), Taylor
 // polynomial of 2^f = e^(f ln 2) to degree 5 (relative error < 4e-6 in fp32
 // arithmetic, far below the bf16 rounding the result goes through), and 2^n applied
-// by adding n to the exponent field.  Inputs below -126 flush to 0.
+// by adding n to the exponent field.  The shifter's bit pattern is
+// 0x4B400000 + n, and 0x4B400000 * 2^23 wraps to 0 in 32 bits, so that add is
+// one integer multiply-add of the shifter's bits.  Inputs are clamped at -126,
+// so masked scores (-inf) give 2^-126 instead of 0: at most 64 * 2^-126 of a
+// row sum that is at least 1.
 __device__ __forceinline__ float exp2_fma(float x) {
   x = fmaxf(x, -126.0f);
   const float shifter = 12582912.0f;  // 1.5 * 2^23
@@ -67,9 +71,14 @@ __device__ __forceinline__ float exp2_fma(float x) {
   p = fmaf(p, f, 2.4022650695910071e-1f);  // ln2^2 / 2!
   p = fmaf(p, f, 6.9314718055994531e-1f);  // ln2
   p = fmaf(p, f, 1.0f);
-  const int ni = __float_as_int(t) - 0x4B400000;
-  const float r = __int_as_float(__float_as_int(p) + (ni << 23));
-  return x > -126.0f ? r : 0.0f;
+  return __int_as_float(__float_as_int(t) * (1 << 23) + __float_as_int(p));
+}
+
+// 2^x on the SFU (ex2.approx, flush-to-zero); 2^-inf = 0.
+__device__ __forceinline__ float exp2_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -191,11 +200,27 @@ __global__ void __launch_bounds__(fam::NT, MINB) flash_mma_kernel(const __nv_bfl
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0 * sl2), mn1 = fmaxf(m1, mx1 * sl2);
-    const float c0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
-    const float c1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
-    m0 = mn0;
-    m1 = mn1;
+    // Lazy rescaling: the reference maximum m of a row only moves when the
+    // tile's maximum exceeds it by more than 8 (log2 units), so P <= 2^8 and
+    // most tiles skip the O / l rescale.  The decision is warp-uniform.
+    const float ms0 = mx0 * sl2, ms1 = mx1 * sl2;
+    if (__any_sync(0xffffffffu, ms0 > m0 + 8.0f || ms1 > m1 + 8.0f)) {
+      const float mn0 = fmaxf(m0, ms0), mn1 = fmaxf(m1, ms1);
+      const float c0 = mn0 == -INFINITY ? 1.f : exp2_sfu(m0 - mn0);
+      const float c1 = mn1 == -INFINITY ? 1.f : exp2_sfu(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      l0 *= c0;
+      l1 *= c1;
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        o[nb][0] *= c0; o[nb][1] *= c0;
+        o[nb][2] *= c1; o[nb][3] *= c1;
+      }
+    }
+    // A row with no visible key so far keeps m = -inf; its exponent base is 0
+    // then, and its (masked, -inf) scores still give ~0.
+    const float nm0 = m0 == -INFINITY ? 0.f : -m0, nm1 = m1 == -INFINITY ? 0.f : -m1;
     float ls0 = 0.f, ls1 = 0.f;
     uint32_t pa[4][4];
 #pragma unroll
@@ -205,31 +230,24 @@ __global__ void __launch_bounds__(fam::NT, MINB) flash_mma_kernel(const __nv_bfl
       // sm_100 (ncu: XU pipe 72% busy with all exponentials on the SFU).
       float p00, p01, p10, p11;
       if ((nb & 3) != 0) {
-        p00 = exp2_fma(fmaf(s[nb][0], sl2, -mn0));
-        p01 = exp2_fma(fmaf(s[nb][1], sl2, -mn0));
-        p10 = exp2_fma(fmaf(s[nb][2], sl2, -mn1));
-        p11 = exp2_fma(fmaf(s[nb][3], sl2, -mn1));
+        p00 = exp2_fma(fmaf(s[nb][0], sl2, nm0));
+        p01 = exp2_fma(fmaf(s[nb][1], sl2, nm0));
+        p10 = exp2_fma(fmaf(s[nb][2], sl2, nm1));
+        p11 = exp2_fma(fmaf(s[nb][3], sl2, nm1));
       } else {
-        p00 = exp2f(fmaf(s[nb][0], sl2, -mn0));
-        p01 = exp2f(fmaf(s[nb][1], sl2, -mn0));
-        p10 = exp2f(fmaf(s[nb][2], sl2, -mn1));
-        p11 = exp2f(fmaf(s[nb][3], sl2, -mn1));
+        p00 = exp2_sfu(fmaf(s[nb][0], sl2, nm0));
+        p01 = exp2_sfu(fmaf(s[nb][1], sl2, nm0));
+        p10 = exp2_sfu(fmaf(s[nb][2], sl2, nm1));
+        p11 = exp2_sfu(fmaf(s[nb][3], sl2, nm1));
       }
-      if (mn0 == -INFINITY) p00 = p01 = 0.f;
-      if (mn1 == -INFINITY) p10 = p11 = 0.f;
       ls0 += p00 + p01;
       ls1 += p10 + p11;
       const int kk = nb >> 1, hi = nb & 1;
       pa[kk][hi * 2 + 0] = pack_bf16(p00, p01);
       pa[kk][hi * 2 + 1] = pack_bf16(p10, p11);
     }
-    l0 = l0 * c0 + ls0;
-    l1 = l1 * c1 + ls1;
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      o[nb][0] *= c0; o[nb][1] *= c0;
-      o[nb][2] *= c1; o[nb][3] *= c1;
-    }
+    l0 += ls0;
+    l1 += ls1;
     // O += P V : A = P (16 x 64 keys), B = V (64 keys x 64 dims)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
