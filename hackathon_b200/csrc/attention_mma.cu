@@ -74,6 +74,25 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return __int_as_float(__float_as_int(t) * (1 << 23) + __float_as_int(p));
 }
 
+// exp2_fma on a pair of values with the packed fp32 pair instructions of
+// sm_100 (one FFMA2 / FADD2 does two lanes' worth of the polynomial).
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float shifter = 12582912.0f;  // 1.5 * 2^23
+  const float2 t = __fadd2_rn(x, make_float2(shifter, shifter));
+  const float2 n = __fadd2_rn(t, make_float2(-shifter, -shifter));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = __ffma2_rn(make_float2(1.3333558146428443e-3f, 1.3333558146428443e-3f), f,
+                        make_float2(9.6181291076284772e-3f, 9.6181291076284772e-3f));
+  p = __ffma2_rn(p, f, make_float2(5.5504108664821580e-2f, 5.5504108664821580e-2f));
+  p = __ffma2_rn(p, f, make_float2(2.4022650695910071e-1f, 2.4022650695910071e-1f));
+  p = __ffma2_rn(p, f, make_float2(6.9314718055994531e-1f, 6.9314718055994531e-1f));
+  p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+  return make_float2(__int_as_float(__float_as_int(t.x) * (1 << 23) + __float_as_int(p.x)),
+                     __int_as_float(__float_as_int(t.y) * (1 << 23) + __float_as_int(p.y)));
+}
+
 // 2^x on the SFU (ex2.approx, flush-to-zero); 2^-inf = 0.
 __device__ __forceinline__ float exp2_sfu(float x) {
   float y;
@@ -90,7 +109,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __device__ __forceinline__ uint32_t swz(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
 
 // MINB = resident CTAs per SM the register allocation is capped for.
-template <int MINB>
+// PK: softmax arithmetic on packed fp32 pairs (FFMA2 / FADD2).
+template <int MINB, bool PK>
 __global__ void __launch_bounds__(fam::NT, MINB) flash_mma_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                             __nv_bfloat16* __restrict__ out, c3b_flash_params p) {
   using namespace fam;
@@ -221,33 +241,61 @@ __global__ void __launch_bounds__(fam::NT, MINB) flash_mma_kernel(const __nv_bfl
     // A row with no visible key so far keeps m = -inf; its exponent base is 0
     // then, and its (masked, -inf) scores still give ~0.
     const float nm0 = m0 == -INFINITY ? 0.f : -m0, nm1 = m1 == -INFINITY ? 0.f : -m1;
-    float ls0 = 0.f, ls1 = 0.f;
     uint32_t pa[4][4];
+    if constexpr (PK) {
+      const float2 sl2v = make_float2(sl2, sl2), nm0v = make_float2(nm0, nm0), nm1v = make_float2(nm1, nm1);
+      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      // A quarter of the exponentials on the SFU, three quarters as a
-      // polynomial on the FMA pipe: the SFU is the bottleneck of this loop on
-      // sm_100 (ncu: XU pipe 72% busy with all exponentials on the SFU).
-      float p00, p01, p10, p11;
-      if ((nb & 3) != 0) {
-        p00 = exp2_fma(fmaf(s[nb][0], sl2, nm0));
-        p01 = exp2_fma(fmaf(s[nb][1], sl2, nm0));
-        p10 = exp2_fma(fmaf(s[nb][2], sl2, nm1));
-        p11 = exp2_fma(fmaf(s[nb][3], sl2, nm1));
-      } else {
-        p00 = exp2_sfu(fmaf(s[nb][0], sl2, nm0));
-        p01 = exp2_sfu(fmaf(s[nb][1], sl2, nm0));
-        p10 = exp2_sfu(fmaf(s[nb][2], sl2, nm1));
-        p11 = exp2_sfu(fmaf(s[nb][3], sl2, nm1));
+      for (int nb = 0; nb < 8; ++nb) {
+        // the exponent arguments of a row pair, one FFMA2 each
+        const float2 x0 = __ffma2_rn(make_float2(s[nb][0], s[nb][1]), sl2v, nm0v);
+        const float2 x1 = __ffma2_rn(make_float2(s[nb][2], s[nb][3]), sl2v, nm1v);
+        float2 p0, p1;
+        // a quarter of the exponentials on the SFU, three quarters as the
+        // packed polynomial on the FMA pipe
+        if ((nb & 3) != 0) {
+          p0 = exp2_fma2(x0);
+          p1 = exp2_fma2(x1);
+        } else {
+          p0 = make_float2(exp2_sfu(x0.x), exp2_sfu(x0.y));
+          p1 = make_float2(exp2_sfu(x1.x), exp2_sfu(x1.y));
+        }
+        ls0 = __fadd2_rn(ls0, p0);
+        ls1 = __fadd2_rn(ls1, p1);
+        const int kk = nb >> 1, hi = nb & 1;
+        pa[kk][hi * 2 + 0] = pack_bf16(p0.x, p0.y);
+        pa[kk][hi * 2 + 1] = pack_bf16(p1.x, p1.y);
       }
-      ls0 += p00 + p01;
-      ls1 += p10 + p11;
-      const int kk = nb >> 1, hi = nb & 1;
-      pa[kk][hi * 2 + 0] = pack_bf16(p00, p01);
-      pa[kk][hi * 2 + 1] = pack_bf16(p10, p11);
+      l0 += ls0.x + ls0.y;
+      l1 += ls1.x + ls1.y;
+    } else {
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        // A quarter of the exponentials on the SFU, three quarters as a
+        // polynomial on the FMA pipe: the SFU is the bottleneck of this loop on
+        // sm_100 (ncu: XU pipe 72% busy with all exponentials on the SFU).
+        float p00, p01, p10, p11;
+        if ((nb & 3) != 0) {
+          p00 = exp2_fma(fmaf(s[nb][0], sl2, nm0));
+          p01 = exp2_fma(fmaf(s[nb][1], sl2, nm0));
+          p10 = exp2_fma(fmaf(s[nb][2], sl2, nm1));
+          p11 = exp2_fma(fmaf(s[nb][3], sl2, nm1));
+        } else {
+          p00 = exp2_sfu(fmaf(s[nb][0], sl2, nm0));
+          p01 = exp2_sfu(fmaf(s[nb][1], sl2, nm0));
+          p10 = exp2_sfu(fmaf(s[nb][2], sl2, nm1));
+          p11 = exp2_sfu(fmaf(s[nb][3], sl2, nm1));
+        }
+        ls0 += p00 + p01;
+        ls1 += p10 + p11;
+        const int kk = nb >> 1, hi = nb & 1;
+        pa[kk][hi * 2 + 0] = pack_bf16(p00, p01);
+        pa[kk][hi * 2 + 1] = pack_bf16(p10, p11);
+      }
+      l0 += ls0;
+      l1 += ls1;
     }
-    l0 += ls0;
-    l1 += ls1;
     // O += P V : A = P (16 x 64 keys), B = V (64 keys x 64 dims)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
@@ -287,16 +335,22 @@ int launch_flash_mma(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_fla
   C3B_REQUIRE(((uintptr_t)qkv.ptr & 15) == 0 && ((uintptr_t)out.ptr & 3) == 0, "flash attention: alignment");
   const int64_t blocks = (int64_t)p.batch * p.heads * ((p.seq + fam::QB - 1) / fam::QB);
   C3B_REQUIRE(blocks < ((int64_t)1 << 31), "flash attention: grid too large");
-  // C3B200_FLASH_OCC=1 selects the uncapped register allocation (3 CTAs per
-  // SM) for A/B comparisons; the default caps registers for 4 CTAs per SM.
-  static const int occ = [] {
+  // A/B switches: C3B200_FLASH_OCC=1 selects the uncapped register allocation
+  // (the default caps registers for 4 CTAs per SM); C3B200_FLASH_PACKED=0 runs
+  // the softmax on scalar fp32 instead of packed pairs.
+  static const int variant = [] {
     const char* e = getenv("C3B200_FLASH_OCC");
-    return (e && atoi(e) == 1) ? 1 : 4;
+    const char* k = getenv("C3B200_FLASH_PACKED");
+    return ((e && atoi(e) == 1) ? 1 : 0) | ((k && k[0] == '0') ? 2 : 0);
   }();
-  if (occ == 1)
-    flash_mma_kernel<1><<<(unsigned)blocks, fam::NT, 0, s>>>((const __nv_bfloat16*)qkv.ptr, (__nv_bfloat16*)out.ptr, p);
-  else
-    flash_mma_kernel<4><<<(unsigned)blocks, fam::NT, 0, s>>>((const __nv_bfloat16*)qkv.ptr, (__nv_bfloat16*)out.ptr, p);
+  const __nv_bfloat16* q = (const __nv_bfloat16*)qkv.ptr;
+  __nv_bfloat16* o = (__nv_bfloat16*)out.ptr;
+  switch (variant) {
+    case 0: flash_mma_kernel<4, true><<<(unsigned)blocks, fam::NT, 0, s>>>(q, o, p); break;
+    case 1: flash_mma_kernel<1, true><<<(unsigned)blocks, fam::NT, 0, s>>>(q, o, p); break;
+    case 2: flash_mma_kernel<4, false><<<(unsigned)blocks, fam::NT, 0, s>>>(q, o, p); break;
+    default: flash_mma_kernel<1, false><<<(unsigned)blocks, fam::NT, 0, s>>>(q, o, p); break;
+  }
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
