@@ -677,4 +677,10 @@ def test_flash_attention_growing_scores(torch_cuda, dt, growth, qscale):
     assert L.device_status() == 0
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all()
-    assert rel(got, ref) < (RTOL if dt == "f32" else 2e-2)
+    # An fp32 score of magnitude |s| carries about eps32*|s| of absolute rounding
+    # that depends on summation order, and exp() turns it into the same relative
+    # error in P; at these magnitudes (up to ~1400) that exceeds RTOL, so the fp32
+    # bound grows with the largest score.  bf16 keeps its 2e-2 gate.
+    smax = float(np.abs(np.matmul(q, k.transpose(0, 1, 3, 2))).max()) / 8.0
+    tol = max(RTOL, 4.0 * float(np.finfo(np.float32).eps) * smax)
+    assert rel(got, ref) < (tol if dt == "f32" else 2e-2)
