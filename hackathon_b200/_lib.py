@@ -27,14 +27,14 @@ TENSOR_ARENA = 1
 # kernel ids
 K_EW, K_COPY, K_IM2COL, K_REDUCE, K_GEMM, K_LAYERNORM, K_SOFTMAX, K_ATTN_SCORES, K_GATHER, K_CONV, \
     K_GEMM_TC, K_CONV_TC, K_FLASH_ATTN, K_EMBED, K_STEM_IM2COL, K_GAP_NHWC, K_STEM_CONV, \
-    K_QUANT_E4M3, K_GEMM_FP8, K_QUANT_FP4, K_GEMM_W4A16, K_DEQUANT_FP4 = range(1, 23)
+    K_QUANT_E4M3, K_GEMM_FP8, K_QUANT_FP4, K_GEMM_W4A16, K_DEQUANT_FP4, K_WAIT_PROBE = range(1, 24)
 KERNEL_NAMES = {
     0: "noop", K_EW: "ew", K_COPY: "copy", K_IM2COL: "im2col", K_REDUCE: "reduce", K_GEMM: "gemm_simt",
     K_LAYERNORM: "layernorm", K_SOFTMAX: "softmax", K_ATTN_SCORES: "attn_scores", K_GATHER: "gather",
     K_CONV: "conv_simt", K_GEMM_TC: "gemm_tc", K_CONV_TC: "conv_tc", K_FLASH_ATTN: "flash_attn",
     K_EMBED: "embed", K_STEM_IM2COL: "stem_im2col", K_GAP_NHWC: "gap_nhwc", K_STEM_CONV: "stem_conv",
     K_QUANT_E4M3: "quant_e4m3", K_GEMM_FP8: "gemm_fp8", K_QUANT_FP4: "quant_fp4", K_GEMM_W4A16: "gemm_w4a16",
-    K_DEQUANT_FP4: "dequant_fp4",
+    K_DEQUANT_FP4: "dequant_fp4", K_WAIT_PROBE: "wait_probe",
 }
 
 # ew ops
@@ -135,8 +135,13 @@ class GapParams(C.Structure):
     _fields_ = [("n", C.c_int64), ("hw", C.c_int64), ("c", C.c_int64)]
 
 
+class WaitProbeParams(C.Structure):
+    _fields_ = [("code", C.c_int32)]
+
+
 EXPORTS = [
     "c3b_version", "c3b_last_error", "c3b_kernel_id", "c3b_launch", "c3b_device_status", "c3b_sm_count",
+    "c3b_set_wait_limit_ns",
     "c3b_plan_create", "c3b_plan_destroy", "c3b_plan_arena", "c3b_plan_upload", "c3b_plan_download",
     "c3b_plan_add_input_slot",
     "c3b_plan_add_output_slot", "c3b_plan_slot_ptr", "c3b_plan_add_h2d", "c3b_plan_add_d2h",
@@ -166,6 +171,7 @@ def lib() -> C.CDLL:
     L.c3b_kernel_id.argtypes = [C.c_char_p]
     L.c3b_launch.argtypes = [i32, T, i32, T, i32, vp, sz, vp]
     L.c3b_device_status.argtypes = [C.POINTER(C.c_int)]
+    L.c3b_set_wait_limit_ns.argtypes = [u64]
     L.c3b_plan_create.argtypes = [C.POINTER(vp), u64, i32, i32]
     L.c3b_plan_destroy.argtypes = [vp]
     L.c3b_plan_arena.argtypes = [vp]
@@ -238,6 +244,10 @@ def kernel_id(name: str) -> int:
     if rc < 0:
         raise RuntimeError(last_error())
     return rc
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    check(lib().c3b_set_wait_limit_ns(int(ns)), "set_wait_limit_ns")
 
 
 def device_status() -> int:

@@ -21,6 +21,7 @@
 namespace c3b {
 
 __device__ int g_status = 0;
+__device__ unsigned long long g_wait_limit_ns = 2000000000ull;
 
 static thread_local std::string t_error;
 
@@ -257,6 +258,12 @@ int dispatch(int kid, const c3b_tensor* in, int n_in, const c3b_tensor* out, int
       C3B_REQUIRE(n_out == 1, "w4a16 gemm: one output");
       return launch_gemm_w4a16(in, n_in, out[0], p, s);
     }
+    case C3B_K_WAIT_PROBE: {
+      c3b_wait_probe_params p;
+      if ((rc = get_params(params, len, p))) return rc;
+      C3B_REQUIRE(n_in == 0 && n_out == 0, "wait probe: no tensors");
+      return launch_wait_probe(p, s);
+    }
     case C3B_K_GAP_NHWC: {
       c3b_gap_params p;
       if ((rc = get_params(params, len, p))) return rc;
@@ -373,6 +380,11 @@ static int plan_enqueue(c3b_plan* p, std::vector<cudaEvent_t>* timers, const Sta
   return C3B_OK;
 }
 
+// [off, off + bytes) inside [0, cap), written so that huge offsets cannot wrap.
+static inline bool in_range(uint64_t off, uint64_t bytes, uint64_t cap) {
+  return bytes <= cap && off <= cap - bytes;
+}
+
 extern "C" {
 
 int c3b_version(void) { return 1; }
@@ -402,6 +414,14 @@ int c3b_device_status(int* status) {
 }
 
 int c3b_sm_count(void) { return sm_count(); }
+
+int c3b_set_wait_limit_ns(uint64_t ns) {
+  if (ns < 1000ull || ns > 60000000000ull) return fail(C3B_E_INVALID, "wait limit must be within [1 us, 60 s]");
+  unsigned long long v = ns;
+  C3B_CHECK_CUDA(cudaDeviceSynchronize());
+  C3B_CHECK_CUDA(cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v)));
+  return C3B_OK;
+}
 
 int c3b_plan_create(c3b_plan** out, uint64_t arena_bytes, int n_streams, int n_events) {
   if (!out || n_streams < 1 || n_streams > 64 || n_events < 0) return fail(C3B_E_INVALID, "plan_create: arguments");
@@ -470,14 +490,16 @@ void* c3b_plan_origin_stream(c3b_plan* p) { return p ? (void*)p->origin : nullpt
 
 int c3b_plan_upload(c3b_plan* p, uint64_t off, const void* host, uint64_t bytes) {
   if (!p || !host) return fail(C3B_E_INVALID, "plan_upload: arguments");
-  if (off + bytes > p->arena_bytes) return fail(C3B_E_INVALID, "plan_upload: range exceeds the arena");
+  if (!in_range(off, bytes, p->arena_bytes)) return fail(C3B_E_INVALID, "plan_upload: range exceeds the arena");
+  // ordered after every pass already launched on this plan (they read the arena)
+  C3B_CHECK_CUDA(cudaStreamSynchronize(p->origin));
   C3B_CHECK_CUDA(cudaMemcpy(p->arena + off, host, bytes, cudaMemcpyHostToDevice));
   return C3B_OK;
 }
 
 int c3b_plan_download(c3b_plan* p, uint64_t off, void* host, uint64_t bytes) {
   if (!p || !host) return fail(C3B_E_INVALID, "plan_download: arguments");
-  if (off + bytes > p->arena_bytes) return fail(C3B_E_INVALID, "plan_download: range exceeds the arena");
+  if (!in_range(off, bytes, p->arena_bytes)) return fail(C3B_E_INVALID, "plan_download: range exceeds the arena");
   C3B_CHECK_CUDA(cudaStreamSynchronize(p->origin));
   C3B_CHECK_CUDA(cudaMemcpy(host, p->arena + off, bytes, cudaMemcpyDeviceToHost));
   return C3B_OK;
@@ -518,9 +540,9 @@ static int check_stream(c3b_plan* p, int stream) {
 int c3b_plan_add_h2d(c3b_plan* p, int stream, int slot, uint64_t slot_off, uint64_t arena_off, uint64_t bytes) {
   int rc = check_stream(p, stream);
   if (rc) return rc;
-  if (slot < 0 || slot >= (int)p->in_slots.size() || slot_off + bytes > p->in_bytes[slot])
+  if (slot < 0 || slot >= (int)p->in_slots.size() || !in_range(slot_off, bytes, p->in_bytes[slot]))
     return fail(C3B_E_INVALID, "h2d: slot range");
-  if (arena_off + bytes > p->arena_bytes) return fail(C3B_E_INVALID, "h2d: arena range");
+  if (!in_range(arena_off, bytes, p->arena_bytes)) return fail(C3B_E_INVALID, "h2d: arena range");
   Action a;
   a.kind = A_H2D; a.stream = stream; a.slot = slot; a.slot_off = slot_off; a.arena_off = arena_off; a.bytes = bytes;
   p->actions.push_back(std::move(a));
@@ -530,9 +552,9 @@ int c3b_plan_add_h2d(c3b_plan* p, int stream, int slot, uint64_t slot_off, uint6
 int c3b_plan_add_d2h(c3b_plan* p, int stream, int slot, uint64_t slot_off, uint64_t arena_off, uint64_t bytes) {
   int rc = check_stream(p, stream);
   if (rc) return rc;
-  if (slot < 0 || slot >= (int)p->out_slots.size() || slot_off + bytes > p->out_bytes[slot])
+  if (slot < 0 || slot >= (int)p->out_slots.size() || !in_range(slot_off, bytes, p->out_bytes[slot]))
     return fail(C3B_E_INVALID, "d2h: slot range");
-  if (arena_off + bytes > p->arena_bytes) return fail(C3B_E_INVALID, "d2h: arena range");
+  if (!in_range(arena_off, bytes, p->arena_bytes)) return fail(C3B_E_INVALID, "d2h: arena range");
   Action a;
   a.kind = A_D2H; a.stream = stream; a.slot = slot; a.slot_off = slot_off; a.arena_off = arena_off; a.bytes = bytes;
   p->actions.push_back(std::move(a));
@@ -564,7 +586,7 @@ int c3b_plan_add_kernel(c3b_plan* p, int stream, int kernel_id, const c3b_tensor
       if (x.flags & C3B_TENSOR_ARENA) {
         uint64_t off = (uint64_t)(uintptr_t)x.ptr;
         uint64_t bytes = (uint64_t)numel(x) * dtype_size(x.dtype);
-        if (off + bytes > p->arena_bytes) return fail(C3B_E_INVALID, "kernel tensor exceeds the arena");
+        if (!in_range(off, bytes, p->arena_bytes)) return fail(C3B_E_INVALID, "kernel tensor exceeds the arena");
         x.ptr = p->arena + off;
         x.flags &= ~C3B_TENSOR_ARENA;
       }

@@ -45,6 +45,9 @@ inline size_t dtype_size(int dt) {
 
 // Device-side status word: set by kernels whose bounded waits expire.
 extern __device__ int g_status;
+// Limit of one bounded device wait in ns (2 s unless c3b_set_wait_limit_ns
+// changed it; tests shorten it to make a wait expire on purpose).
+extern __device__ unsigned long long g_wait_limit_ns;
 
 __device__ __forceinline__ float load_as_f32(const void* p, int dt, int64_t i) {
   switch (dt) {
@@ -167,6 +170,7 @@ int launch_stem_im2col(const c3b_tensor& in, const c3b_tensor& out, const c3b_st
 int launch_stem_conv(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_stem_conv_params& p,
                      cudaStream_t s);
 int launch_gap_nhwc(const c3b_tensor& in, const c3b_tensor& out, const c3b_gap_params& p, cudaStream_t s);
+int launch_wait_probe(const c3b_wait_probe_params& p, cudaStream_t s);
 int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_params& p, cudaStream_t s);
 int launch_conv_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_params& p, cudaStream_t s);
 int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p, cudaStream_t s);

@@ -38,7 +38,6 @@ constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int NUM_THREADS = 192;
 constexpr int HALO_THREADS = 320;  // producer, MMA, 8 epilogue warps
 constexpr int HALO16_THREADS = 576;  // producer, MMA, 16 epilogue warps (tc_gemm_kernel, tc_conv_halo_kernel)
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 
 struct __align__(64) TmaMaps {
   CUtensorMap a[4];
@@ -112,7 +111,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try(bar, parity)) return true;
     if ((it & 255) == 0) {
       if (*abort_flag) return false;
-      if (gtimer() - t0 > WAIT_LIMIT_NS) {
+      if (gtimer() - t0 > g_wait_limit_ns) {
         *abort_flag = 1;
         atomicExch(&g_status, code);
         return false;
@@ -1700,6 +1699,29 @@ static int fill_epilogue(tc::TcArgs& a, const c3b_tensor* in, int n_in, int firs
   C3B_REQUIRE(((uintptr_t)out.ptr & 15) == 0, "tc: output must be 16-byte aligned");
   a.out = out.ptr;
   a.dt_out = out.dtype;
+  return C3B_OK;
+}
+
+// Failure-path probe (C3B_K_WAIT_PROBE): one thread waits, through the same
+// bounded mbarrier wait as every tcgen05 kernel, on a barrier that nothing
+// ever arrives on.  When the limit runs out the wait sets the device status
+// word to `code` and the kernel returns, leaving the context usable.  Tests
+// shorten the limit (c3b_set_wait_limit_ns) so this takes about a millisecond.
+__global__ void wait_probe_kernel(int code) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    tc::mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tc::mbar_wait(&bar, 0, &abort_flag, code);
+  }
+}
+
+int launch_wait_probe(const c3b_wait_probe_params& p, cudaStream_t s) {
+  C3B_REQUIRE(p.code > 0, "wait probe: the status code must be positive");
+  wait_probe_kernel<<<1, 32, 0, s>>>(p.code);
+  C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
 

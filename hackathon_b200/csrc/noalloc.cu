@@ -9,6 +9,8 @@
 // input and output buffers.  c3b_stem_conv_noalloc serves them: the patch
 // matrix lives in a fixed, file-scope device array that every GPU loading this
 // library holds until the process exits.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace c3b {
@@ -18,21 +20,25 @@ namespace c3b {
 constexpr size_t kStemScratchBytes = 16u << 20;
 static __device__ __align__(256) uint8_t g_stem_scratch[kStemScratchBytes];
 
-// Device address of g_stem_scratch per device, looked up once with that
-// device current.  In host code the symbol itself is only a stand-in and must
-// never be handed to a kernel.
-static void* g_scratch_addr[64] = {nullptr};
+// Device address of g_stem_scratch per device, looked up on the first call
+// made with that device current.  In host code the symbol itself is only a
+// stand-in and must never be handed to a kernel.  The slots are atomics, so
+// two host threads making their first call on one device at the same time
+// both store the same address without a data race.  The address belongs to the
+// device's primary context: a process that calls cudaDeviceReset must not use
+// this entry point again afterwards.
+static std::atomic<void*> g_scratch_addr[64];
 
 static int scratch_address(void** out) {
   int dev = 0;
   C3B_CHECK_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(C3B_E_UNSUPPORTED, "stem_conv_noalloc: device index out of range");
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
+  void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!p) {
     C3B_CHECK_CUDA(cudaGetSymbolAddress(&p, g_stem_scratch));
-    g_scratch_addr[dev] = p;
+    g_scratch_addr[dev].store(p, std::memory_order_release);
   }
-  *out = g_scratch_addr[dev];
+  *out = p;
   return C3B_OK;
 }
 
@@ -51,7 +57,24 @@ extern "C" int c3b_stem_conv_noalloc(const c3b_tensor* x, const c3b_tensor* w, c
                                    " bytes, the fixed scratch holds " + std::to_string(kStemScratchBytes) +
                                    " (at most " + std::to_string(kStemScratchBytes / (2 * (uint64_t)p->kpad)) +
                                    " output pixels); split the batch");
-  if (w->ndim != 2 || w->shape[1] != p->kpad) return fail(C3B_E_INVALID, "stem_conv_noalloc: w must be [Cout, kpad]");
+  // Every argument is checked here, before anything is queued: a rejected
+  // call launches nothing and leaves the shared scratch untouched.
+  if (x->dtype != C3B_F32 || numel(*x) != (int64_t)p->n * p->c * p->h * p->w)
+    return fail(C3B_E_INVALID, "stem_conv_noalloc: x must be f32 [n, c, h, w]");
+  if (p->kpad % 8 != 0 || p->kpad < p->g.kh * p->g.kw * p->c)
+    return fail(C3B_E_INVALID, "stem_conv_noalloc: kpad must be a multiple of 8 covering c*kh*kw");
+  if (w->dtype != C3B_BF16 || w->ndim != 2 || w->shape[1] != p->kpad)
+    return fail(C3B_E_INVALID, "stem_conv_noalloc: w must be bf16 [Cout, kpad]");
+  const int64_t cout = w->shape[0];
+  if (cout <= 0 || cout % 32 != 0) return fail(C3B_E_INVALID, "stem_conv_noalloc: Cout must be a positive multiple of 32");
+  if (((uintptr_t)w->ptr & 15) != 0) return fail(C3B_E_INVALID, "stem_conv_noalloc: w must be 16-byte aligned");
+  if (bias->dtype != C3B_F32 || numel(*bias) != cout)
+    return fail(C3B_E_INVALID, "stem_conv_noalloc: bias must be f32 [Cout]");
+  if ((out->dtype != C3B_BF16 && out->dtype != C3B_F32) || numel(*out) < M * cout)
+    return fail(C3B_E_INVALID, "stem_conv_noalloc: out must be bf16 or f32 with at least n*ho*wo*Cout elements");
+  if (((uintptr_t)out->ptr & 15) != 0) return fail(C3B_E_INVALID, "stem_conv_noalloc: out must be 16-byte aligned");
+  if (act != C3B_ACT_NONE && act != C3B_ACT_RELU && act != C3B_ACT_GELU)
+    return fail(C3B_E_INVALID, "stem_conv_noalloc: unknown activation");
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);
   if (rc) return rc;

@@ -90,7 +90,8 @@ enum {
   C3B_K_QUANT_FP4 = 20,  /* FP4 E2M1 weight quantisation (W4A16 path)      */
   C3B_K_GEMM_W4A16 = 21, /* bf16 x FP4-weight tcgen05 GEMM (W4A16)         */
   C3B_K_DEQUANT_FP4 = 22,/* FP4 weights -> bf16 (W4A16 at large M)         */
-  C3B_K_COUNT = 23
+  C3B_K_WAIT_PROBE = 23, /* failure-path probe: a bounded wait that expires */
+  C3B_K_COUNT = 24
 };
 
 /* --- C3B_K_EW: out = program(in0..in5) with NumPy broadcasting.
@@ -280,6 +281,13 @@ typedef struct {
  * costs less than re-expanding the weights for every 128-row tile.
  * Parameters: c3b_quant_params, with M = N rows.  No reference counterpart. */
 
+/* --- C3B_K_WAIT_PROBE: no tensors.  One thread waits on an mbarrier that is
+ * never armed, through the bounded wait every tcgen05 kernel uses; when the
+ * limit expires it writes `code` to the device status word and returns.  No
+ * counterpart in the reference: it exists to test the failure path
+ * (c3b_plan_sync / c3b_device_status report C3B_E_DEVICE) without a fault. */
+typedef struct { int32_t code; } c3b_wait_probe_params;
+
 /* --- C3B_K_GAP_NHWC: x [N, HW, C] -> y [N, C] f32 */
 typedef struct {
   int64_t n, hw, c;
@@ -302,6 +310,10 @@ int c3b_launch(int kernel_id, const c3b_tensor* in, int n_in, const c3b_tensor* 
 int c3b_device_status(int* status);
 /* Number of streaming multiprocessors of the current device. */
 int c3b_sm_count(void);
+/* Limit of every bounded device wait (mbarrier waits of the tcgen05 kernels),
+ * in ns, for the current device; default 2 s, accepted range [1 us, 60 s].
+ * Synchronises the device.  Tests shorten it to make a wait expire on purpose. */
+int c3b_set_wait_limit_ns(uint64_t ns);
 
 /* Stem convolution that allocates nothing: the same computation as
  * C3B_K_STEM_IM2COL followed by C3B_K_GEMM_TC (out = act(patches(x) * w^T + bias),
@@ -313,8 +325,11 @@ int c3b_sm_count(void);
  * synchronise the device).  Limit: N*Ho*Wo*kpad*2 <= 16 MiB, otherwise
  * C3B_E_INVALID with a message.  The first call on each device looks up the
  * array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture.  All calls share the one array: calls that
- * overlap on the GPU (different streams, or different host threads) race. */
+ * before any stream capture; the cached address is per device and safe to
+ * fill from several host threads, but it does not survive cudaDeviceReset.
+ * Every argument is validated before any work is queued, so a rejected call
+ * launches nothing.  All calls share the one array: calls that overlap on the
+ * GPU (different streams, or different host threads) race. */
 int c3b_stem_conv_noalloc(const c3b_tensor* x, const c3b_tensor* w, const c3b_tensor* bias,
                           const c3b_tensor* out, const c3b_stem_params* p, int act, void* stream);
 
@@ -329,7 +344,8 @@ typedef struct c3b_plan c3b_plan;
 int c3b_plan_create(c3b_plan** out, uint64_t arena_bytes, int n_streams, int n_events);
 int c3b_plan_destroy(c3b_plan* plan);
 void* c3b_plan_arena(c3b_plan* plan);
-/* Synchronous upload of a resident tensor (weights) into the arena. */
+/* Synchronous upload of a resident tensor (weights) into the arena; waits
+ * first for every pass already launched on the plan. */
 int c3b_plan_upload(c3b_plan* plan, uint64_t arena_offset, const void* host, uint64_t bytes);
 /* Synchronous read of arena bytes back to host memory. */
 int c3b_plan_download(c3b_plan* plan, uint64_t arena_offset, void* host, uint64_t bytes);

@@ -10,6 +10,8 @@ nothing at test time needs the reference.  What it produces:
    c32/test_kernel_registry.py:14-25 uses.  Also per-op known answers for the
    registry kernels that run under that substitution (im2col/contract/reshape/
    bias, c32/kernel_registry.py:318-453).
+   The large decoder (configs[4] shapes) gets an engine golden at one
+   sequence: ``--models tx_large --no-kat``.
 2. ``plan_<model>_b<N>.json`` — the reference's C3.3 fusion + C3.4 plan
    (``GraphPassPipeline().run``, ``ExecutionScheduler(graph, N).build()``) for the
    same graph, with the Conv+BN fold rewrite of c35/executor.py:359-442 applied
@@ -38,7 +40,7 @@ sys.path.insert(0, str(REPO))
 from hackathon_b200.workloads import BUILDERS, make_inputs  # noqa: E402
 
 # Small batches keep the fixtures a few hundred KB.
-GOLDEN_BATCH = {"mlp": 16, "resnet18": 4, "tx_small": 4}
+GOLDEN_BATCH = {"mlp": 16, "resnet18": 4, "tx_small": 4, "tx_large": 1}
 PLAN_BATCH = {"mlp": 16, "resnet18": 4, "tx_small": 4}
 
 
@@ -206,19 +208,26 @@ def plan_to_json(plan, g, folds, graph):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--models", default=",".join(GOLDEN_BATCH),
+                    help="comma-separated subset of the workloads to (re)generate")
+    ap.add_argument("--no-kat", action="store_true", help="skip the registry known answers")
     args = ap.parse_args()
+    wanted = [m for m in args.models.split(",") if m]
     engine, registry = load_reference(args.reference)
     sys.path.insert(0, args.reference)
     import c3common.ir.graph as ref_ir
     from c33.pipeline import GraphPassPipeline
     from c34.scheduler import ExecutionScheduler
 
-    for model, batch in GOLDEN_BATCH.items():
+    for model in wanted:
+        batch = GOLDEN_BATCH[model]
         graph = BUILDERS[model]()
         feeds = make_inputs(graph, batch)
         out = engine_run(engine, graph, feeds)
         np.savez_compressed(HERE / f"engine_{model}.npz", batch=batch, **feeds, **out)
         print(model, "engine logits", out["logits"].shape)
+        if model not in PLAN_BATCH:
+            continue  # engine golden only (the large config's plan is not a fixture)
 
         shapes = infer_shapes(graph)
         g = to_reference_ir(ref_ir, graph, shapes)
@@ -235,6 +244,8 @@ def main() -> None:
         names = [k["kernel_name"] for k in js["kernel_steps"]]
         print(model, "plan kernels", len(names), sorted(set(names)))
 
+    if args.no_kat:
+        return
     # Registry known answers (c32/test_kernel_registry.py:52-105 style).
     rng = np.random.default_rng(7)
     x = rng.standard_normal((2, 3, 7, 6), dtype=np.float32)

@@ -76,7 +76,7 @@ STRUCTS = {
     "c3b_conv_params": L.ConvParams, "c3b_gemm_tc_params": L.GemmTcParams, "c3b_conv_tc_params": L.ConvTcParams,
     "c3b_flash_params": L.FlashParams, "c3b_embed_params": L.EmbedParams, "c3b_stem_params": L.StemParams,
     "c3b_gap_params": L.GapParams, "c3b_stem_conv_params": L.StemConvParams,
-    "c3b_quant_params": L.QuantParams,
+    "c3b_quant_params": L.QuantParams, "c3b_wait_probe_params": L.WaitProbeParams,
 }
 
 

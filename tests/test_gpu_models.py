@@ -3,10 +3,19 @@
 * The reference's own C3.4 plans (committed fixtures, built by the reference
   scheduler from the same graphs) replayed natively against the logits of the
   reference's engine ops (tests/golden/engine_*.npz): 1e-4 relative.
-* The backend's fused programs against the oracle: fp32 profile 1e-4
-  relative; bf16 profile within the bf16 gate (2e-2 absolute on logits scaled
-  to unit max, identical argmax on all but near-tied rows) and tight against
-  the oracle evaluated on the same bf16-rounded operands.
+* The backend's fused programs against the oracle at the configs' stated
+  sizes: fp32 profile 1e-4 relative (C0 b256, C1 b256, C2 b64); bf16 profile
+  against the stated gate -- logits within 2e-2 ABSOLUTE of the fp32 result and
+  an identical argmax.  Where a config cannot meet that gate with bf16
+  operands, the test asserts the measured bound instead and says so:
+  - ResNet-18 (C3): logits reach |34|, so 2e-2 absolute is 6e-4 relative,
+    below what bf16 weights alone allow (each bf16 rounding is up to 2^-9
+    relative); measured 0.23 absolute (7e-3 of the largest logit), argmax
+    identical on every compared row, including rows of the 4096-image pass.
+  - Transformer-small (C2): error within the gate, but 3 of 64 rows have a
+    top-2 gap of 2e-4 .. 5e-3, smaller than the error itself; only those
+    near-tied rows may flip.
+  - Transformer-large (C4): within the gate, argmax identical.
 * Full-size properties at BASELINE sizes: determinism, finiteness and shard
   consistency (a batch slice equals the same rows run alone).
 """
@@ -63,8 +72,9 @@ def _run_program(g, batch, profile, feeds):
     return ex, out[ex.prog.outputs[0]]
 
 
-@pytest.mark.parametrize("model,batch", [("mlp", 256), ("resnet18", 32), ("tx_small", 8)])
+@pytest.mark.parametrize("model,batch", [("mlp", 256), ("resnet18", 256), ("tx_small", 64)])
 def test_fp32_programs(wl, model, batch):
+    """configs[0..2] at their stated batch sizes, fp32 profile: 1e-4 relative."""
     g = wl.BUILDERS[model]()
     feeds = wl.make_inputs(g, batch)
     ref = run_graph(g, feeds)["logits"]
@@ -73,47 +83,88 @@ def test_fp32_programs(wl, model, batch):
     ex.native.close()
 
 
-def _bf16_gate(out, ref):
-    scale = np.abs(ref).max()
-    abs_err = np.abs(out - ref).max() / scale
+BF16_GATE_ABS = 2e-2  # stated gate for bf16/fp16 profiles: logits within 2e-2 absolute
+
+
+def _bf16_gate(tag, out, ref):
+    """Absolute logits error, argmax agreement, and the rows whose argmax
+    differs although their top-2 gap exceeds twice the error (real flips)."""
+    d = np.abs(out.astype(np.float64) - ref.astype(np.float64))
+    abs_err = float(d.max())
     am_o, am_r = out.argmax(-1), ref.argmax(-1)
     srt = np.sort(ref, axis=-1)
-    gap = (srt[:, -1] - srt[:, -2]) / scale
-    flips = (am_o != am_r) & (gap > 2 * abs_err)
-    return abs_err, int((am_o != am_r).sum()), int(flips.sum())
+    gap = srt[:, -1] - srt[:, -2]
+    flips = am_o != am_r
+    real = flips & (gap > 2 * abs_err)
+    print(f"{tag}: max abs err {abs_err:.4e} (gate {BF16_GATE_ABS}), max |logit| {np.abs(ref).max():.3f}, "
+          f"argmax flips {int(flips.sum())}/{len(ref)} (top-2 gaps of flipped rows: {gap[flips][:8]})")
+    return abs_err, int(flips.sum()), int(real.sum())
 
 
 def test_resnet_bf16(wl):
+    """C3 network at 64 images.  Gate NOT met as stated (see module doc):
+    asserts the measured absolute bound and an identical argmax."""
     g = wl.BUILDERS["resnet18"]()
     feeds = wl.make_inputs(g, 64)
     ref = run_graph(g, feeds)["logits"]
     ex, out = _run_program(g, 64, "bf16", feeds)
-    abs_err, n_flip, n_real_flip = _bf16_gate(out, ref)
-    print(f"resnet bf16: scaled max abs err {abs_err:.3e}, argmax flips {n_flip} (non-tie {n_real_flip})")
-    assert abs_err < 2e-2
-    assert n_real_flip == 0
+    abs_err, n_flip, _ = _bf16_gate("resnet18 bf16 b64", out, ref)
+    assert abs_err < 0.35
+    assert n_flip == 0
     ex.native.close()
 
 
-def test_tx_large_bf16_small_batch(wl):
+def test_resnet_bf16_b4096_rows_against_oracle(wl):
+    """The headline pass itself (C3, 4096 images in one pass) compared with
+    the oracle on 384 of its rows: the first, a middle and the last 128
+    (persistent-tile wraparound and the M tail are in play only at this size)."""
+    g = wl.BUILDERS["resnet18"]()
+    feeds = wl.make_inputs(g, 4096)
+    ex, out = _run_program(g, 4096, "bf16", feeds)
+    ex.native.close()
+    idx = np.concatenate([np.arange(0, 128), np.arange(2048, 2176), np.arange(3968, 4096)])
+    ref = run_graph(g, {k: v[idx] for k, v in feeds.items()})["logits"]
+    abs_err, n_flip, _ = _bf16_gate("resnet18 bf16 b4096 (384 rows)", out[idx], ref)
+    assert abs_err < 0.35
+    assert n_flip == 0
+
+
+@pytest.mark.parametrize("batch", [2, 8])
+def test_tx_large_bf16(wl, batch):
+    """C4 network (d1024, 12 blocks, vocab 32000) at 2 and 8 sequences: the
+    stated gate, 2e-2 absolute and identical argmax."""
     g = wl.BUILDERS["tx_large"]()
-    feeds = wl.make_inputs(g, 2)
+    feeds = wl.make_inputs(g, batch)
     ref = run_graph(g, feeds)["logits"]
-    ex, out = _run_program(g, 2, "bf16", feeds)
-    abs_err, n_flip, n_real_flip = _bf16_gate(out, ref)
-    print(f"tx_large bf16: scaled max abs err {abs_err:.3e}, argmax flips {n_flip} (non-tie {n_real_flip})")
-    assert abs_err < 2e-2
-    assert n_real_flip == 0
+    ex, out = _run_program(g, batch, "bf16", feeds)
+    abs_err, n_flip, _ = _bf16_gate(f"tx_large bf16 b{batch}", out, ref)
+    assert abs_err < BF16_GATE_ABS
+    assert n_flip == 0
+    ex.native.close()
+
+
+def test_tx_large_bf16_against_reference_golden(wl):
+    """The reference's own engine ops (tests/golden/engine_tx_large.npz, one
+    sequence) against the bf16 program: the stated gate."""
+    gold = np.load(os.path.join(HERE, "golden", "engine_tx_large.npz"))
+    g = wl.BUILDERS["tx_large"]()
+    feeds = {vi.name: gold[vi.name] for vi in g.inputs}
+    ex, out = _run_program(g, int(gold["batch"]), "bf16", feeds)
+    abs_err, n_flip, _ = _bf16_gate("tx_large bf16 vs reference golden", out, gold["logits"])
+    assert abs_err < BF16_GATE_ABS and n_flip == 0
     ex.native.close()
 
 
 def test_tx_small_bf16(wl):
+    """C2 network at its stated batch (64) in the bf16 profile: the stated
+    absolute gate; argmax may differ only on near-tied rows (top-2 gap below
+    twice the error)."""
     g = wl.BUILDERS["tx_small"]()
-    feeds = wl.make_inputs(g, 8)
+    feeds = wl.make_inputs(g, 64)
     ref = run_graph(g, feeds)["logits"]
-    ex, out = _run_program(g, 8, "bf16", feeds)
-    abs_err, n_flip, n_real_flip = _bf16_gate(out, ref)
-    assert abs_err < 2e-2 and n_real_flip == 0
+    ex, out = _run_program(g, 64, "bf16", feeds)
+    abs_err, n_flip, n_real_flip = _bf16_gate("tx_small bf16 b64", out, ref)
+    assert abs_err < BF16_GATE_ABS and n_real_flip == 0
     ex.native.close()
 
 
@@ -205,7 +256,9 @@ def test_tx_low_precision_profiles(wl, model, batch, profile):
     fp32 oracle: E4M3 keeps 3 mantissa bits, so the gate is a scaled logits error
     of 0.15 and no argmax flip on rows whose top-2 gap exceeds twice that error.
     mixed profile (W4A16 for the large constant-weight GEMMs) against the oracle
-    run on the same effective FP4 weights: the bf16 gate (2e-2)."""
+    run on the same effective FP4 weights: 2e-2 of the largest logit (these
+    extension profiles are gated relative to the logit scale; the absolute gate
+    is asserted for the bf16 profile above)."""
     g = wl.BUILDERS[model]()
     feeds = wl.make_inputs(g, batch)
     ref = run_graph(_w4a16_weights(g) if profile == "mixed" else g, feeds)["logits"]
@@ -216,9 +269,9 @@ def test_tx_low_precision_profiles(wl, model, batch, profile):
     else:
         assert "gemm_w4a16" in labels
         assert ("dequant_fp4" in labels) == (batch * g.meta["seq"] >= 2048)
-    abs_err, n_flip, n_real_flip = _bf16_gate(out, ref)
-    print(f"{model} {profile}: scaled max abs err {abs_err:.3e}, argmax flips {n_flip} (non-tie {n_real_flip})")
+    abs_err, n_flip, n_real_flip = _bf16_gate(f"{model} {profile} b{batch}", out, ref)
+    scaled = abs_err / np.abs(ref).max()
     assert np.isfinite(out).all()
-    assert abs_err < (0.15 if profile == "fp8" else 2e-2)
+    assert scaled < (0.15 if profile == "fp8" else 2e-2)
     assert n_real_flip == 0
     ex.native.close()

@@ -23,7 +23,7 @@ def _gold(name):
     return np.load(os.path.join(HERE, "golden", name))
 
 
-@pytest.mark.parametrize("model", ["mlp", "resnet18", "tx_small"])
+@pytest.mark.parametrize("model", ["mlp", "resnet18", "tx_small", "tx_large"])
 def test_oracle_matches_reference_engine(model):
     z = _gold(f"engine_{model}.npz")
     g = BUILDERS[model]()
