@@ -46,6 +46,10 @@ WORKLOADS = {
     "tx_small_fp32": ("tx_small", 64, "fp32", "tok/s", "strong", 128,
                       "BASELINE configs[2]: decoder d256 L4 H4 FFN1024 V4096 S128, batch 64"),
     "mlp_fp32": ("mlp", 256, "fp32", "samples/s", "strong", None, "BASELINE configs[0]: MLP 784-512-256-10"),
+    "resnet18_bf16_plan": ("resnet18", 4096, "bf16", "img/s", "strong", None,
+                           "BASELINE configs[3] through the reference's own C3.3 pipeline + the backend's extra "
+                           "C3.3 passes + the reference C3.4 scheduler with the bf16 profile "
+                           "(tests/golden/plan_resnet18_b<N>_b200_bf16.json), replayed by C34PlanRunner"),
 }
 METRIC = {"img/s": "ResNet-18 img/s", "tok/s": "Transformer tok/s", "samples/s": "MLP samples/s"}
 CPU_SAMPLE = {"resnet18": 64, "tx_large": 1, "tx_small": 8, "mlp": 256}
@@ -208,8 +212,104 @@ def run_reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def measure_plan(args, workload, ws, rank, local, with_cpu_baseline):
+    """A workload replayed from a C3.4 plan (the reference's planning path with
+    the backend's passes and precision profile).  The plan's own timeline
+    copies the input in and the logits out every pass, so ``value`` (device
+    time of the captured timeline) already includes those copies; ``e2e`` is
+    the host wall clock of C34PlanRunner.run (NumPy in, NumPy out)."""
+    import torch
+    from hackathon_b200.c34_plan import C34PlanRunner
+    from hackathon_b200.workloads import BUILDERS, make_inputs
+    from hackathon_b200.dist import rows_for
+    key, gbatch, profile, unit, scaling, ups, note = WORKLOADS[workload]
+    g = BUILDERS[key]()
+    total, start, per = rows_for(scaling, gbatch, ws, rank)
+    path = os.path.join(ROOT, "tests", "golden", f"plan_{key}_b{per}_b200_bf16.json")
+    if not os.path.exists(path):
+        raise SystemExit(f"no committed plan for per-GPU batch {per}: {path}")
+    plan = json.load(open(path))
+    feeds_all = make_inputs(g, total)
+    feeds = {k: v[start:start + per] for k, v in feeds_all.items()}
+    r = C34PlanRunner(plan, g.initializers, {k: (v.shape, v.dtype) for k, v in feeds.items()})
+    r.run(feeds)
+    origin = torch.cuda.ExternalStream(r.native.origin_stream)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        r.native.launch()
+        r.native.sync()
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)
+    barrier(ws)
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(origin)
+        r.native.launch()
+        e1.record(origin)
+        r.native.sync()
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r.run(feeds)
+    wall_ms = 1000.0 * (time.perf_counter() - t0)
+    barrier(ws)
+    clocks = clk.stop()
+    dev_ms_max = max_over_ranks(ws, tot)
+    wall_ms_max = max_over_ranks(ws, wall_ms)
+    step_ms = dev_ms_max / args.steps
+    value = total * args.steps / (dev_ms_max / 1000.0)
+    # family shares from one eager pass with events around every kernel
+    ms = r.native.run_timed()
+    fam_eager, fam_flops = {}, {}
+    for lab, t, fl in zip(r.native.kernel_labels, ms.tolist(), r.launch_flops):
+        fam_eager[lab] = fam_eager.get(lab, 0.0) + t
+        fam_flops[lab] = fam_flops.get(lab, 0.0) + fl
+    eager_total = sum(fam_eager.values())
+    fam_ms = {k: step_ms * v / eager_total for k, v in fam_eager.items()}
+    top = max(fam_ms, key=fam_ms.get)
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops"))
+    achieved = fam_flops[top] / (fam_ms[top] / 1e3) / 1e12 if fam_ms[top] > 0 else 0.0
+    in_b = sum(v.nbytes for v in feeds.values())
+    out_b = sum(int(np.prod(shp)) * np.dtype(dt).itemsize for _, shp, dt in r.output_slots.values())
+    line = {
+        "metric": METRIC[unit], "value": value, "unit": unit, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": profile, "data": "synthetic (seeded, random-init weights)",
+        "config": {"workload": workload, "model": key, "note": note, "global_batch": total, "per_gpu_batch": per,
+                   "precision_profile": profile, "parallelism": f"dp{ws} (batch shards, no collectives)",
+                   "l2": "256 MB buffer written between timed steps (L2 is 126 MB)",
+                   "cuda_graph": True, "timed_region": "whole C3.4 timeline: H2D of the input, kernels, D2H"},
+        "clocks": clocks,
+        "e2e": {"value": total * args.steps / (wall_ms_max / 1000.0), "unit": unit,
+                "h2d_bytes_per_step": in_b * ws, "d2h_bytes_per_step": out_b * ws,
+                "ms_per_step": wall_ms_max / args.steps,
+                "how": "host perf_counter around C34PlanRunner.run (NumPy -> pinned slot -> plan -> NumPy)"},
+        "gpu_launches": len(r.native.kernel_ids) * args.steps * 2,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak if peak else None, "traffic": None, "kernel": top,
+                     "kernel_ms_per_step": fam_ms[top], "peak_source": f"{src} bf16_tflops (burst)",
+                     "kernel_time_source": "eager-pass family share x timed graph replay"},
+        "kernels_ms_per_step": {k: round(v, 4) for k, v in sorted(fam_ms.items(), key=lambda kv: -kv[1])},
+        "cpu_baseline": None,
+    }
+    r.native.close()
+    del flush
+    torch.cuda.empty_cache()
+    return line if rank == 0 else None
+
+
 def measure(args, workload, ws, rank, local, with_cpu_baseline):
     """One workload at this world size: returns the JSON record (rank 0) or None."""
+    if workload.endswith("_plan"):
+        return measure_plan(args, workload, ws, rank, local, with_cpu_baseline)
     import torch
     from hackathon_b200.lowering import lower
     from hackathon_b200.program import Executor

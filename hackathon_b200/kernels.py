@@ -30,6 +30,9 @@ class Desc:
     shape: Tuple[int, ...]
     arena: bool = False
     host: Optional[np.ndarray] = None  # host copy of small constants (shapes, split sizes)
+    # "nhwc": a logical [N, C, H, W] tensor stored channels-last ([N*H*W, C]),
+    # as the tensor-core convolutions read and write it
+    layout: str = "plain"
 
     @property
     def numel(self) -> int:
@@ -430,6 +433,29 @@ def _b_matmul_bias(ins, outs, p):
     return _gemm_epilogue(ins, outs, p, True)
 
 
+@builder("b200linearepilogue_f32")
+def _b_b200_linear(ins, outs, p):
+    """The fused node of hackathon_b200.c33_passes.fuse_linear_epilogue in fp32:
+    MatMul + bias [+ exact-erf GELU | + residual] in one launch (the GELU
+    chain's constants are checked by the caller)."""
+    a, b = ins[0], ins[1]
+    lead = tuple(a.shape[:-1])
+    M, K = int(np.prod(lead, dtype=np.int64)), a.shape[-1]
+    if b.shape[0] != K:
+        raise ValueError(f"linear: inner dimensions differ: {K} and {b.shape[0]}")
+    N = b.shape[1]
+    ri = p.get("_residual_input_index")
+    res = ins[int(ri)] if ri is not None else None
+    bias = ins[2] if len(ins) > 2 and ins[2] is not None else None
+    act = {"Relu": L.ACT_RELU, "Gelu": L.ACT_GELU}.get(p.get("_activation"), L.ACT_NONE)
+    g = _gemm_params(M, N, K, bias=L.BIAS_COL if bias is not None else L.BIAS_NONE, act=act,
+                     res=int(res is not None))
+    tin = [a.t((M, K)), b.t()] + ([bias.t((N,))] if bias is not None else []) + \
+        ([res.t((M, N))] if res is not None else [])
+    shape = lead + (N,)
+    return Prepared([Launch(L.K_GEMM, tin, [_out(outs, 0, shape)], g)], [shape])
+
+
 # ------------------------------------------------------------ convolution
 
 def conv_geometry(p: Dict[str, Any], H: int, W: int, kh: int, kw: int) -> Tuple[L.ConvGeom, int, int]:
@@ -503,6 +529,17 @@ def _b_winograd(ins, outs, p):
 def _b_conv_f32(ins, outs, p):
     bias = ins[2] if len(ins) > 2 and ins[2] is not None else None
     res = ins[3] if len(ins) > 3 else None
+    act = L.ACT_RELU if p.get("_activation") == "Relu" else L.ACT_NONE
+    return _conv_nchw(ins[0], ins[1], bias, res, outs, p, act)
+
+
+@builder("b200convbiasact_f32")
+def _b_b200_conv(ins, outs, p):
+    """The fused node of hackathon_b200.c33_passes.fuse_conv_bias_act in fp32:
+    conv (BN folded into w, b) + bias [+ residual] [+ ReLU] in one launch."""
+    ri = p.get("_residual_input_index")
+    res = ins[int(ri)] if ri is not None else None
+    bias = ins[2] if len(ins) > 2 and ins[2] is not None else None
     act = L.ACT_RELU if p.get("_activation") == "Relu" else L.ACT_NONE
     return _conv_nchw(ins[0], ins[1], bias, res, outs, p, act)
 
@@ -604,6 +641,48 @@ def _b_attn(ins, outs, p):
 
 # ------------------------------------------------------------ data movement
 # kernel_registry.py:669-759, engine.py:1383-1445
+
+def flash_params_from_node(qkv: Desc, heads_shape: Desc, divisor: Desc, mask: Desc, p) -> L.FlashParams:
+    """FlashParams for a B200FlashAttention node (hackathon_b200.c33_passes):
+    qkv [B, S, 3*H*D] split into Q, K, V in that order along the last axis,
+    heads from the Reshape target [., S, H, D], scale 1/divisor, and a mask
+    that must be all zero or causal (0 on and below the diagonal, -1e9 above;
+    the seeded graphs' mask, c35/engine.py:1250-1380 adds it before softmax)."""
+    if list(p.get("_qkv_order", [0, 1, 2])) != [0, 1, 2]:
+        raise ValueError("flash attention: Q, K, V must be the Split outputs 0, 1, 2")
+    hs = _host_ints(heads_shape)
+    if hs is None or len(hs) != 4 or divisor.host is None or mask.host is None:
+        raise ValueError("flash attention: heads shape, divisor and mask must be constants")
+    if len(qkv.shape) != 3:
+        raise ValueError("flash attention: qkv must be [B, S, 3*H*D]")
+    B, S, three_hd = qkv.shape
+    H, D = hs[2], hs[3]
+    if 3 * H * D != three_hd:
+        raise ValueError("flash attention: qkv width is not 3 * heads * head_dim")
+    m = np.asarray(mask.host, np.float32)
+    if m.size == S * S:
+        m2 = m.reshape(S, S)
+        causal = np.array_equal(m2, np.triu(np.full((S, S), -1e9, np.float32), 1))
+        if not causal and np.any(m2):
+            raise ValueError("flash attention: only an all-zero or causal (0/-1e9) mask is supported")
+    elif np.any(m):
+        raise ValueError("flash attention: the mask must be [.., S, S]")
+    else:
+        causal = False
+    div = float(np.asarray(divisor.host).reshape(-1)[0])
+    return L.FlashParams(B, S, H, D, 1.0 / div, int(causal))
+
+
+@builder("b200flashattention_f32")
+def _b_b200_flash(ins, outs, p):
+    """The fused node of hackathon_b200.c33_passes.fuse_flash_attention in fp32:
+    softmax(Q K^T / divisor + mask) V with heads merged, read from the packed
+    QKV projection, no score tensor."""
+    qkv = ins[0]
+    fp = flash_params_from_node(qkv, ins[1], ins[2], ins[3], p)
+    shape = (fp.batch, fp.seq, fp.heads * fp.head_dim)
+    return Prepared([Launch(L.K_FLASH_ATTN, [qkv.t()], [_out(outs, 0, shape, qkv.dtype)], fp)], [shape])
+
 
 def resolve_reshape(in_shape, target, allowzero=0) -> Tuple[int, ...]:
     out, infer, known = [], None, 1

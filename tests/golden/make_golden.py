@@ -12,6 +12,10 @@ nothing at test time needs the reference.  What it produces:
    bias, c32/kernel_registry.py:318-453).
    The large decoder (configs[4] shapes) gets an engine golden at one
    sequence: ``--models tx_large --no-kat``.
+3. ``plan_<model>_b<N>_b200_bf16.json`` -- the same graphs through the
+   reference pipeline, the executor's fold rewrite, the backend's extra C3.3
+   passes (``hackathon_b200.c33_passes``) and the reference scheduler with the
+   bf16 precision profile (``hackathon_b200.c34_precision``): ``--b200-plans``.
 2. ``plan_<model>_b<N>.json`` — the reference's C3.3 fusion + C3.4 plan
    (``GraphPassPipeline().run``, ``ExecutionScheduler(graph, N).build()``) for the
    same graph, with the Conv+BN fold rewrite of c35/executor.py:359-442 applied
@@ -42,6 +46,11 @@ from hackathon_b200.workloads import BUILDERS, make_inputs  # noqa: E402
 # Small batches keep the fixtures a few hundred KB.
 GOLDEN_BATCH = {"mlp": 16, "resnet18": 4, "tx_small": 4, "tx_large": 1}
 PLAN_BATCH = {"mlp": 16, "resnet18": 4, "tx_small": 4}
+# Plans through the B200 C3.3 passes and the bf16 C3.2/C3.4 profile
+# (hackathon_b200.c33_passes, hackathon_b200.c34_precision): the test batches,
+# plus the headline ResNet batch and its 2/4/8-GPU shards that bench.py replays.
+B200_PLANS = [("mlp", 16), ("resnet18", 4), ("tx_small", 4), ("resnet18", 4096), ("resnet18", 2048),
+              ("resnet18", 1024), ("resnet18", 512)]
 
 
 def numpy_cupy_shim() -> types.ModuleType:
@@ -193,7 +202,8 @@ def plan_to_json(plan, g, folds, graph):
                               logical_inputs=list(k.logical_inputs), logical_outputs=list(k.logical_outputs),
                               inputs=dict(k.inputs), outputs=dict(k.outputs), stream_id=k.stream_id,
                               tuning_params=_jsonable(k.tuning_params),
-                              operator_params=_jsonable(k.operator_params)) for k in plan.kernel_steps],
+                              operator_params=_jsonable(k.operator_params),
+                              precision_profile=_jsonable(k.precision_profile or {})) for k in plan.kernel_steps],
         "events": [e.event_id for e in plan.events],
         "timeline": [dict(kind=s.kind, stream_id=s.stream_id, ref_index=s.ref_index,
                           event_id=s.event_id, tensor_name=s.tensor_name) for s in plan.timeline],
@@ -205,14 +215,42 @@ def plan_to_json(plan, g, folds, graph):
     }
 
 
+def b200_plans(ref: str) -> None:
+    load_reference(ref)
+    sys.path.insert(0, ref)
+    import c3common.ir.graph as ref_ir
+    from c33.pipeline import GraphPassPipeline
+    from hackathon_b200.c33_passes import run_b200_passes
+    from hackathon_b200.c34_precision import build_plan
+    for model, batch in B200_PLANS:
+        graph = BUILDERS[model]()
+        g = to_reference_ir(ref_ir, graph, infer_shapes(graph))
+        res = GraphPassPipeline().run(g)
+        assert res["Fusion"]["stats"]["validation_passed"]
+        folds = fold_bn_rewrite(g)
+        counts = run_b200_passes(g)["counts"]
+        plan = build_plan(g, batch, "bf16")
+        js = plan_to_json(plan, g, folds, graph)
+        js["b200_passes"] = counts
+        with open(HERE / f"plan_{model}_b{batch}_b200_bf16.json", "w") as f:
+            json.dump(js, f, separators=(",", ":"))
+        names = [k["kernel_name"] for k in js["kernel_steps"]]
+        print(model, batch, "b200 plan kernels", len(names), sorted(set(names)), counts)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
     ap.add_argument("--models", default=",".join(GOLDEN_BATCH),
                     help="comma-separated subset of the workloads to (re)generate")
     ap.add_argument("--no-kat", action="store_true", help="skip the registry known answers")
+    ap.add_argument("--b200-plans", action="store_true",
+                    help="only (re)generate the plans with the backend's passes and bf16 profile")
     args = ap.parse_args()
     wanted = [m for m in args.models.split(",") if m]
+    if args.b200_plans:
+        b200_plans(args.reference)
+        return
     engine, registry = load_reference(args.reference)
     sys.path.insert(0, args.reference)
     import c3common.ir.graph as ref_ir

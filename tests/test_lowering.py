@@ -103,23 +103,13 @@ class _Recorder(_DryPlan):
         self.actions.append(("W", s, e))
 
 
-def _dry_runner(model, batch):
-    plan = json.load(open(os.path.join(HERE, "golden", f"plan_{model}_b{batch}.json")))
+def _dry_runner(model, batch, suffix="", profile=None):
+    plan = json.load(open(os.path.join(HERE, "golden", f"plan_{model}_b{batch}{suffix}.json")))
     g = BUILDERS[model]()
     gold = np.load(os.path.join(HERE, "golden", f"engine_{model}.npz"))
     specs = {vi.name: (gold[vi.name][:batch].shape, gold[vi.name].dtype) for vi in g.inputs}
-    r = C34PlanRunner.__new__(C34PlanRunner)
-    r.plan = plan
-    w = dict(g.initializers)
-    w.update(fold_weights(plan.get("folds", {}), g.initializers))
-    r._weights, r._specs = w, specs
-    sids = sorted({s["stream_id"] for s in plan["timeline"] if s["kind"] not in ("ALLOC", "FREE")})
-    r.stream_index = {sid: i for i, sid in enumerate(sids)}
-    r.event_index = {e: i for i, e in enumerate(plan["events"])}
-    r.spills = {}
-    r._walk(_DryPlan(), plan["arena_bytes"])  # sizes spills
     rec = _Recorder()
-    r._walk(rec, plan["arena_bytes"])
+    r = C34PlanRunner(plan, g.initializers, specs, profile=profile, target=rec)
     return r, rec, plan
 
 
@@ -136,7 +126,7 @@ def test_reference_plan_adapter_walks_fixture(model, batch):
             recorded.add(a[2])
         if a[0] == "W":
             assert a[2] in recorded
-    limit = plan["arena_bytes"] + sum(sz for _, sz in r.spills.values())
+    limit = r._extra_top
     for _, _, _, ln in kernels:
         for t in list(ln.ins) + list(ln.outs):
             n = int(np.prod([t.shape[i] for i in range(t.ndim)])) if t.ndim else 1
