@@ -80,20 +80,21 @@ def test_b200_plan_bf16_replay(model, batch):
 
 @pytest.mark.parametrize("model,batch", [("resnet18", 4), ("tx_small", 4)])
 def test_b200_plan_equals_backend_lowering(model, batch):
-    """The plan path and the backend's own lowering launch the same kernels on
-    the same operands: identical logits for ResNet-18, and agreement to fp32
-    rounding for the Transformer (its last residual add runs inside the
-    LayerNorm on the plan path and inside the GEMM epilogue in the lowering)."""
+    """The plan path and the backend's own lowering launch the same kernels.
+    They differ only in where a residual add is fused (the plan adds a
+    downsampling block's main branch inside the shortcut conv, the lowering
+    the other way round; the plan's last Transformer residual add runs inside
+    the LayerNorm), so the logits agree to bf16 rounding of one tensor."""
     from hackathon_b200.lowering import lower
     from hackathon_b200.program import Executor
     r, feeds, _, g = _runner(model, batch)
     out = r.run(feeds)["logits"]
     ex = Executor(lower(g, batch, "bf16"))
     want = ex.run(feeds)["logits"]
-    if model == "resnet18":
-        assert np.array_equal(out, want)
-    else:
-        assert np.abs(out - want).max() <= 1e-5 * np.abs(want).max() + 1e-6
+    d = float(np.abs(out - want).max())
+    print(f"{model}: plan vs lowering max abs diff {d:.3e}")
+    assert d <= 1e-2 * np.abs(want).max()
+    assert (out.argmax(-1) == want.argmax(-1)).all()
     r.native.close()
     ex.native.close()
 
