@@ -110,7 +110,10 @@ int launch_flash_attn(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_fl
   C3B_REQUIRE(numel(qkv) == tokens * 3 * p.heads * fa::D, "flash attention: qkv extents");
   C3B_REQUIRE(numel(out) >= tokens * p.heads * fa::D, "flash attention: output too small");
   if (tokens == 0) return C3B_OK;
-  if (qkv.dtype == C3B_BF16) return launch_flash_mma(qkv, out, p, s);
+  if (qkv.dtype == C3B_BF16) {
+    if (flash_tc_supported(p)) return launch_flash_tc(qkv, out, p, s);
+    return launch_flash_mma(qkv, out, p, s);
+  }
   const int64_t blocks = (int64_t)p.batch * p.heads * ((p.seq + fa::QT - 1) / fa::QT);
   C3B_REQUIRE(blocks < ((int64_t)1 << 31), "flash attention: grid too large");
   flash_simt_kernel<float><<<(unsigned)blocks, fa::NT, 0, s>>>((const float*)qkv.ptr, (float*)out.ptr, p);
