@@ -104,12 +104,16 @@ int launch_flash_mma(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_fla
 
 int launch_flash_attn(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_flash_params& p, cudaStream_t s) {
   C3B_REQUIRE(p.head_dim == fa::D, "flash attention: head_dim must be 64");
-  C3B_REQUIRE(qkv.dtype == out.dtype && (qkv.dtype == C3B_F32 || qkv.dtype == C3B_BF16),
-              "flash attention: f32 or bf16, same dtype in and out");
+  C3B_REQUIRE(qkv.dtype == out.dtype && (qkv.dtype == C3B_F32 || qkv.dtype == C3B_BF16 || qkv.dtype == C3B_F16),
+              "flash attention: f32, bf16 or fp16, same dtype in and out");
   const int64_t tokens = (int64_t)p.batch * p.seq;
   C3B_REQUIRE(numel(qkv) == tokens * 3 * p.heads * fa::D, "flash attention: qkv extents");
   C3B_REQUIRE(numel(out) >= tokens * p.heads * fa::D, "flash attention: output too small");
   if (tokens == 0) return C3B_OK;
+  if (qkv.dtype == C3B_F16) {
+    C3B_REQUIRE(flash_tc_supported(p), "flash attention: fp16 needs head_dim 64 and a multiple of 128 keys");
+    return launch_flash_tc(qkv, out, p, s);
+  }
   if (qkv.dtype == C3B_BF16) {
     if (flash_tc_supported(p)) return launch_flash_tc(qkv, out, p, s);
     return launch_flash_mma(qkv, out, p, s);

@@ -4,7 +4,8 @@
 // attention: fused_attention_scores_f32 (softmax(Q K^T / divisor + mask) into a
 // [B, H, S, S] tensor, c35/engine.py:1250-1380) followed by the P.V matmul_f32
 // (c32/kernel_registry.py:318-358) and the head merge.  Same contract as the
-// other flash kernels: qkv [B, S, 3, H, 64] bf16 -> out [B, S, H*64] bf16.
+// other flash kernels: qkv [B, S, 3, H, 64] bf16 -> out [B, S, H*64] bf16 (or
+// fp16 in and out for the fp16 profile).
 //
 // Design (persistent, two CTAs per SM, 10 warps and about 100 KB of shared
 // memory each).  A work item is one (batch, head, 128-row query tile); items
@@ -76,7 +77,8 @@ constexpr uint32_t COL_S = 0, COL_O = 128, COL_P = 192;
 struct Args {
   int batch, seq, heads, qtiles, n_items, causal;
   float scale_log2;  // softmax scale x log2(e)
-  __nv_bfloat16* out;
+  uint16_t* out;
+  int h16;           // 16-bit format of qkv, P and out: 0 bf16, 1 fp16
   unsigned long long* prof;  // optional wait counters (C3B200_FLASH_PROF=1), else null
 };
 
@@ -145,10 +147,7 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accum));
 }
 
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
+
 
 __global__ void __launch_bounds__(THREADS, CTAS_PER_SM) flash_tc_kernel(const __grid_constant__ CUtensorMap qkv_map,
                                                                        const Args a) {
@@ -247,8 +246,8 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM) flash_tc_kernel(const __
     // Sub-tile u of an item = keys 64u .. 64u+63 = half u&1 of K/V tile u>>1.
     // S of global sub-tile t goes to S buffer t&1, P to P buffer t&1.
     if (lane == 0) {
-      const uint32_t id_s = instr_desc(BQ, SUB);
-      const uint32_t id_pv = instr_desc(BQ, D) | (1u << 16);  // B (V) is MN-major
+      const uint32_t id_s = instr_desc_h(BQ, SUB, a.h16);
+      const uint32_t id_pv = instr_desc_h(BQ, D, a.h16) | (1u << 16);  // B (V) is MN-major
       const uint64_t q_desc0 = smem_desc(smem_u32(sm + OFF_Q));
       const uint64_t k_desc0 = smem_desc(smem_u32(sm + OFF_K));
       const uint64_t v_desc0 = smem_desc(smem_u32(sm + OFF_V));
@@ -431,7 +430,7 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM) flash_tc_kernel(const __
             } else {
               e[q] = make_float2(exp2_sfu(z.x), exp2_sfu(z.y));
             }
-            pk[4 * ch + q] = pack2(e[q].x, e[q].y);
+            pk[4 * ch + q] = pack2h(e[q], a.h16);
           }
           sum2[ch & 1] = __fadd2_rn(sum2[ch & 1], __fadd2_rn(__fadd2_rn(e[0], e[1]), __fadd2_rn(e[2], e[3])));
         }
@@ -462,10 +461,10 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM) flash_tc_kernel(const __
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint4 v;
-        v.x = pack2(o[8 * c] * inv, o[8 * c + 1] * inv);
-        v.y = pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-        v.z = pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-        v.w = pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+        v.x = pack2h(make_float2(o[8 * c] * inv, o[8 * c + 1] * inv), a.h16);
+        v.y = pack2h(make_float2(o[8 * c + 2] * inv, o[8 * c + 3] * inv), a.h16);
+        v.z = pack2h(make_float2(o[8 * c + 4] * inv, o[8 * c + 5] * inv), a.h16);
+        v.w = pack2h(make_float2(o[8 * c + 6] * inv, o[8 * c + 7] * inv), a.h16);
         dst[c] = v;
       }
     }
@@ -499,7 +498,8 @@ bool flash_tc_supported(const c3b_flash_params& p) {
 }
 
 int launch_flash_tc(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_flash_params& p, cudaStream_t s) {
-  C3B_REQUIRE(qkv.dtype == C3B_BF16 && out.dtype == C3B_BF16, "flash tc: bf16 in and out");
+  C3B_REQUIRE((qkv.dtype == C3B_BF16 || qkv.dtype == C3B_F16) && out.dtype == qkv.dtype,
+              "flash tc: bf16 or fp16, the same in and out");
   C3B_REQUIRE(((uintptr_t)qkv.ptr & 15) == 0 && ((uintptr_t)out.ptr & 15) == 0, "flash tc: 16-byte alignment");
   fat::Args a;
   a.batch = p.batch;
@@ -509,7 +509,8 @@ int launch_flash_tc(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_flas
   a.n_items = p.batch * p.heads * a.qtiles;
   a.causal = p.causal;
   a.scale_log2 = p.scale * 1.4426950408889634f;
-  a.out = (__nv_bfloat16*)out.ptr;
+  a.out = (uint16_t*)out.ptr;
+  a.h16 = qkv.dtype == C3B_F16;
   a.prof = nullptr;
   if (a.n_items == 0) return C3B_OK;
   // Wait profiler (C3B200_FLASH_PROF=1, measurement runs only): cycles summed

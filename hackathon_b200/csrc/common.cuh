@@ -133,6 +133,42 @@ __device__ __forceinline__ float2 gelu2_as_fast(float2 x) {
 // branch): a per-element select lets the compiler evaluate every variant,
 // erff included, for every element — which cost the tcgen05 GEMM epilogues a
 // third of their throughput.  bf16 outputs take the fast GELU.
+// 16-bit storage formats of the tensor-core paths: bf16 (bf16 profile) or
+// fp16 (fp16 profile), selected per launch by `h16` (1 = fp16).
+__device__ __forceinline__ float2 unpack2h(uint32_t w, bool h16) {
+  if (h16) return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+__device__ __forceinline__ uint32_t pack2h(float2 v, bool h16) {
+  uint32_t r;
+  if (h16) {
+    __half2 t = __float22half2_rn(v);
+    r = *reinterpret_cast<uint32_t*>(&t);
+  } else {
+    __nv_bfloat162 t = __float22bfloat162_rn(v);
+    r = *reinterpret_cast<uint32_t*>(&t);
+  }
+  return r;
+}
+// 8 consecutive 16-bit elements (one 16-byte word) <-> floats
+__device__ __forceinline__ void unpack8h(const uint4& w, float* v, bool h16) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack2h(u[i], h16);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8h(const float* v, bool h16) {
+  uint4 w;
+  w.x = pack2h(make_float2(v[0], v[1]), h16);
+  w.y = pack2h(make_float2(v[2], v[3]), h16);
+  w.z = pack2h(make_float2(v[4], v[5]), h16);
+  w.w = pack2h(make_float2(v[6], v[7]), h16);
+  return w;
+}
+
 template <int N>
 __device__ __forceinline__ void act_inplace(float* v, int act, bool bf16_out) {
   if (act == C3B_ACT_RELU) {

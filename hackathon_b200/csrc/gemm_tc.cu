@@ -75,6 +75,8 @@ struct TcArgs {
   // tc_gemm_kernel: bf16 output through per-warp shared-memory tiles and TMA
   // stores (maps.out: 16 columns x 32 rows, 32-byte swizzle)
   int tma_out;
+  // 16-bit format of A, B and every 16-bit output / residual: 0 bf16, 1 fp16
+  int h16;
 };
 
 // Epilogue for 32 columns of one bf16 output row whose residual (bf16) was
@@ -91,26 +93,22 @@ __device__ __forceinline__ void store32_bf16(const TcArgs& a, int64_t off, int64
   if (rv) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv[i]);
+      float rr[8];
+      unpack8h(rv[i], rr, a.h16);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[8 * i + j] += __bfloat162float(rb[j]);
+      for (int j = 0; j < 8; ++j) v[8 * i + j] += rr[j];
     }
   }
   act_inplace<32>(v, a.act, true);
-  uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
+  uint4* op = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + off);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __align__(16) __nv_bfloat16 o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(v[8 * i + j]);
-    op[i] = *reinterpret_cast<const uint4*>(o);
-  }
+  for (int i = 0; i < 4; ++i) op[i] = pack8h(v + 8 * i, a.h16);
 }
 
 // Residual of 32 consecutive columns (bf16: 64 bytes, f32: 128 bytes) as raw words.
 __device__ __forceinline__ void load_res32(const TcArgs& a, int64_t off, uint4* r) {
-  if (a.dt_res == C3B_BF16) {
-    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off);
+  if (a.dt_res != C3B_F32) {
+    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.res) + off);
 #pragma unroll
     for (int i = 0; i < 4; ++i) r[i] = rp[i];
   } else {
@@ -142,12 +140,13 @@ __device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t c
     }
   }
   if (r) {
-    if (a.dt_res == C3B_BF16) {
+    if (a.dt_res != C3B_F32) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&r[i]);
+        float rr[8];
+        unpack8h(r[i], rr, a.h16);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[8 * i + j] += __bfloat162float(rb[j]);
+        for (int j = 0; j < 8; ++j) v[8 * i + j] += rr[j];
       }
     } else {
 #pragma unroll
@@ -158,16 +157,11 @@ __device__ __forceinline__ void finish32(const TcArgs& a, int64_t off, int64_t c
       }
     }
   }
-  act_inplace<32>(v, a.act, a.dt_out == C3B_BF16);
-  if (a.dt_out == C3B_BF16) {
-    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
+  act_inplace<32>(v, a.act, a.dt_out != C3B_F32);
+  if (a.dt_out != C3B_F32) {
+    uint4* op = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + off);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      __align__(16) __nv_bfloat16 o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(v[8 * i + j]);
-      op[i] = *reinterpret_cast<const uint4*>(o);
-    }
+    for (int i = 0; i < 4; ++i) op[i] = pack8h(v + 8 * i, a.h16);
   } else {
     float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
 #pragma unroll
@@ -186,8 +180,8 @@ __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.
 
 // Residual of 16 consecutive columns (bf16: 32 bytes, f32: 64 bytes) as raw words.
 __device__ __forceinline__ void load_res16(const TcArgs& a, int64_t off, uint4* r) {
-  if (a.dt_res == C3B_BF16) {
-    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off);
+  if (a.dt_res != C3B_F32) {
+    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.res) + off);
     r[0] = rp[0]; r[1] = rp[1];
   } else {
     const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const float*>(a.res) + off);
@@ -222,32 +216,29 @@ __device__ __forceinline__ void epi16(const TcArgs& a, int64_t col0, float* v, c
     }
   }
   if (r) {
-    if (a.dt_res == C3B_BF16) {
-      const __nv_bfloat162* rb = reinterpret_cast<const __nv_bfloat162*>(r);
+    if (a.dt_res != C3B_F32) {
+      const uint32_t* rb = reinterpret_cast<const uint32_t*>(r);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v2[i] = __fadd2_rn(v2[i], __bfloat1622float2(rb[i]));
+      for (int i = 0; i < 8; ++i) v2[i] = __fadd2_rn(v2[i], unpack2h(rb[i], a.h16));
     } else {
       const float2* rf = reinterpret_cast<const float2*>(r);
 #pragma unroll
       for (int i = 0; i < 8; ++i) v2[i] = __fadd2_rn(v2[i], rf[i]);
     }
   }
-  act_inplace<16>(v, a.act, a.dt_out == C3B_BF16);
+  act_inplace<16>(v, a.act, a.dt_out != C3B_F32);
 }
 
 __device__ __forceinline__ void finish16(const TcArgs& a, int64_t off, int64_t col0, float* v, const uint4* r,
                                          float rs) {
   epi16(a, col0, v, r, rs);
   float2* v2 = reinterpret_cast<float2*>(v);
-  if (a.dt_out == C3B_BF16) {
-    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
+  if (a.dt_out != C3B_F32) {
+    uint4* op = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + off);
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      __align__(16) __nv_bfloat162 o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[j] = __float22bfloat162_rn(v2[4 * i + j]);
-      op[i] = *reinterpret_cast<const uint4*>(o);
-    }
+    for (int i = 0; i < 2; ++i)
+      op[i] = make_uint4(pack2h(v2[4 * i], a.h16), pack2h(v2[4 * i + 1], a.h16), pack2h(v2[4 * i + 2], a.h16),
+                         pack2h(v2[4 * i + 3], a.h16));
   } else {
     float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
 #pragma unroll
@@ -384,7 +375,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = F8 ? instr_desc_e4m3(BM, a.block_n) : instr_desc(BM, a.block_n);
+      const uint32_t idesc = F8 ? instr_desc_e4m3(BM, a.block_n) : instr_desc_h(BM, a.block_n, a.h16);
       // stage descriptors = base descriptor + offset in 16-byte units
       const uint64_t ad0 = smem_desc(smem_u32(sa)), bd0 = smem_desc(smem_u32(sb));
       int stage = 0;
@@ -451,15 +442,15 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
           if (u < units) {
             const int r = u >> 3, c = u & 7;
             const float2 s2 = make_float2(sc[i], sc[i]);
-            __align__(16) __nv_bfloat162 o[4];
+            uint32_t o[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const __half2_raw h =
                   __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((pk[i] >> (8 * j)) & 0xFF), __NV_E2M1);
               const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
-              o[j] = __float22bfloat162_rn(__fmul2_rn(f, s2));
+              o[j] = pack2h(__fmul2_rn(f, s2), a.h16);
             }
-            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
+            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
         fence_proxy_async();
@@ -511,13 +502,9 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
             uint8_t* tile = my_stg + (n_st & 1) * 1024;
             if (lane == 0) bulk_wait_read1();  // the store that last used this tile has read it
             __syncwarp();
-            __align__(16) __nv_bfloat162 o[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = __float22bfloat162_rn(make_float2(v[2 * j], v[2 * j + 1]));
 #pragma unroll
             for (int h = 0; h < 2; ++h)
-              *reinterpret_cast<uint4*>(tile + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4)) =
-                  reinterpret_cast<const uint4*>(o)[h];
+              *reinterpret_cast<uint4*>(tile + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4)) = pack8h(v + 8 * h, a.h16);
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) {
@@ -561,16 +548,13 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, int64_t off, int64_
     for (int i = 0; i < 16; ++i) v[i] += a.bias[col0 + i];
   }
   if (a.res) {
-    if (a.dt_res == C3B_BF16) {
-      const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off);
-      uint4 r0 = rp[0], r1 = rp[1];
-      const __nv_bfloat16* rb0 = reinterpret_cast<const __nv_bfloat16*>(&r0);
-      const __nv_bfloat16* rb1 = reinterpret_cast<const __nv_bfloat16*>(&r1);
+    if (a.dt_res != C3B_F32) {
+      const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.res) + off);
+      float rr[16];
+      unpack8h(rp[0], rr, a.h16);
+      unpack8h(rp[1], rr + 8, a.h16);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[i] += __bfloat162float(rb0[i]);
-        v[i + 8] += __bfloat162float(rb1[i]);
-      }
+      for (int i = 0; i < 16; ++i) v[i] += rr[i];
     } else {
       const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + off);
 #pragma unroll
@@ -580,14 +564,11 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, int64_t off, int64_
       }
     }
   }
-  act_inplace<16>(v, a.act, a.dt_out == C3B_BF16);
-  if (a.dt_out == C3B_BF16) {
-    __align__(16) __nv_bfloat16 o[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) o[i] = __float2bfloat16_rn(v[i]);
-    uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off);
-    op[0] = reinterpret_cast<const uint4*>(o)[0];
-    op[1] = reinterpret_cast<const uint4*>(o)[1];
+  act_inplace<16>(v, a.act, a.dt_out != C3B_F32);
+  if (a.dt_out != C3B_F32) {
+    uint4* op = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + off);
+    op[0] = pack8h(v, a.h16);
+    op[1] = pack8h(v + 8, a.h16);
   } else {
     float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
 #pragma unroll
@@ -706,7 +687,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(BM, a.block_n);
+      const uint32_t idesc = instr_desc_h(BM, a.block_n, a.h16);
       const uint64_t bd0 = smem_desc(smem_u32(sb));
       int hs = 0, bs = 0, acc = 0;
       uint32_t hph = 0, bph = 0, acc_phase = 0;
@@ -799,7 +780,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
 #pragma unroll
         for (int u = 0; u < 2; ++u)
           if (own[u]) {
-            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + off[u]);
+            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.res) + off[u]);
 #pragma unroll
             for (int i = 0; i < 4; ++i) rv[u][i] = rp[i];
           }
@@ -828,9 +809,10 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
           if (a.res) {
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
-              const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv[u][2 * h + i]);
+              float rr[8];
+              unpack8h(rv[u][2 * h + i], rr, a.h16);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[8 * i + e] += __bfloat162float(rb[e]);
+              for (int e = 0; e < 8; ++e) v[8 * i + e] += rr[e];
             }
           }
           act_inplace<16>(v, a.act, true);
@@ -840,13 +822,10 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
             uint8_t* tile = stg + (size_t)(warp - 2) * 1024;
             if (lane == 0) bulk_wait_read0();  // the previous store has read the tile
             __syncwarp();
-            __align__(16) __nv_bfloat162 o2[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o2[e] = __float22bfloat162_rn(make_float2(v[2 * e], v[2 * e + 1]));
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh)
               *reinterpret_cast<uint4*>(tile + lane * 32 + ((hh ^ ((lane >> 2) & 1)) << 4)) =
-                  reinterpret_cast<const uint4*>(o2)[hh];
+                  pack8h(v + 8 * hh, a.h16);
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) {
@@ -856,14 +835,9 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
             }
             continue;
           }
-          uint4* op = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off[u] + h * 16);
+          uint4* op = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + off[u] + h * 16);
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            __align__(16) __nv_bfloat16 o8[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o8[e] = __float2bfloat16_rn(v[8 * i + e]);
-            op[i] = *reinterpret_cast<const uint4*>(o8);
-          }
+          for (int i = 0; i < 2; ++i) op[i] = pack8h(v + 8 * i, a.h16);
         }
       }
       tc_fence_before();
@@ -977,7 +951,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc64 = instr_desc(BM, 64), idesc128 = instr_desc(BM, 128);
+      const uint32_t idesc64 = instr_desc_h(BM, 64, a.h16), idesc128 = instr_desc_h(BM, 128, a.h16);
       int acc = 0;
       uint32_t acc_phase = 0;
       uint32_t cbase = 0;
@@ -1136,16 +1110,13 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
 #pragma unroll
             for (int e = 0; e < 8; ++e) x[e] = v[j][c * 8 + e] + bias[c * 8 + e];
             if (a.res) {
-              const uint4 rw = *cp;
-              const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rw);
+              float rr[8];
+              unpack8h(*cp, rr, a.h16);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) x[e] += __bfloat162float(rb[e]);
+              for (int e = 0; e < 8; ++e) x[e] += rr[e];
             }
             act_inplace<8>(x, a.act, true);
-            __align__(16) __nv_bfloat16 o[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = __float2bfloat16_rn(x[e]);
-            *cp = *reinterpret_cast<const uint4*>(o);
+            *cp = pack8h(x, a.h16);
           }
         }
         fence_proxy_async();
@@ -1188,7 +1159,7 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
                                                                   const float* __restrict__ x,
                                                                   const float* __restrict__ wt,
                                                                   const float* __restrict__ bias, c3b_stem_params g,
-                                                                  int act, int64_t M, int n_tiles) {
+                                                                  int act, int64_t M, int n_tiles, int h16) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;                                   // STEM_STAGES x 16 KB patch tiles
@@ -1208,13 +1179,13 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
   // weights -> B operand: row n (output channel), K-major, zero beyond K
   for (int i = threadIdx.x; i < 64 * 8; i += STEM_THREADS) {
     const int n = i >> 3, c = i & 7;  // 16-byte chunk c = K elements 8c..8c+7
-    __align__(16) __nv_bfloat162 o[4];
+    uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int k0 = c * 8 + 2 * j;
-      o[j] = __floats2bfloat162_rn(k0 < K ? wt[k0 * 64 + n] : 0.f, k0 + 1 < K ? wt[(k0 + 1) * 64 + n] : 0.f);
+      o[j] = pack2h(make_float2(k0 < K ? wt[k0 * 64 + n] : 0.f, k0 + 1 < K ? wt[(k0 + 1) * 64 + n] : 0.f), h16);
     }
-    *reinterpret_cast<uint4*>(sbw + n * 128 + ((c ^ (n & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
+    *reinterpret_cast<uint4*>(sbw + n * 128 + ((c ^ (n & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
   if (threadIdx.x < 32) {
     const int k = threadIdx.x;
@@ -1302,12 +1273,7 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
       }
       uint8_t* row = sa + (size_t)stage * 16384 + r * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        __align__(16) __nv_bfloat162 o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(v[c * 8 + 2 * j], v[c * 8 + 2 * j + 1]);
-        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
-      }
+      for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = pack8h(v + c * 8, h16);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[stage]);
@@ -1338,12 +1304,8 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
       if (lane == 0) bulk_wait_read0();  // the previous store has read the tile
       __syncwarp();
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        __align__(16) __nv_bfloat162 o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(v[c * 8 + 2 * j], v[c * 8 + 2 * j + 1]);
-        *reinterpret_cast<uint4*>(tile + lane * 128 + ((c ^ (lane & 7)) << 4)) = *reinterpret_cast<const uint4*>(o);
-      }
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(tile + lane * 128 + ((c ^ (lane & 7)) << 4)) = pack8h(v + c * 8, h16);
       fence_proxy_async();
       __syncwarp();
       const int64_t row0 = (int64_t)t * 128 + q * 32;
@@ -1355,7 +1317,7 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
     if (lane == 0) bulk_wait0();
   } else if (lane == 0) {
     // ---------------- MMA issue
-    const uint32_t idesc = instr_desc(BM, 64);
+    const uint32_t idesc = instr_desc_h(BM, 64, h16);
     const uint64_t ad0 = smem_desc(smem_u32(sa)), bd = smem_desc(smem_u32(sbw));
     int stage = 0, acc = 0;
     uint32_t phase = 0, acc_phase = 0;
@@ -1408,7 +1370,7 @@ static int enable_tma_out(tc::TmaMaps& maps, tc::TcArgs& a) {
     return !(e && e[0] == '0');
   }();
   a.tma_out = 0;
-  if (!on || a.dt_out != C3B_BF16 || a.N % 16) return C3B_OK;
+  if (!on || a.dt_out == C3B_F32 || a.N % 16) return C3B_OK;
   uint64_t dims[2] = {(uint64_t)a.N, (uint64_t)a.M};
   uint64_t str[1] = {(uint64_t)a.N * 2};
   uint32_t box[2] = {16, 32};
@@ -1463,7 +1425,8 @@ static int fill_epilogue(tc::TcArgs& a, const c3b_tensor* in, int n_in, int firs
   }
   if (has_residual) {
     C3B_REQUIRE(idx < n_in, "tc: missing residual");
-    C3B_REQUIRE(in[idx].dtype == C3B_BF16 || in[idx].dtype == C3B_F32, "tc: residual bf16/f32");
+    C3B_REQUIRE(in[idx].dtype == (a.h16 ? C3B_F16 : C3B_BF16) || in[idx].dtype == C3B_F32,
+                a.h16 ? "tc: residual fp16/f32" : "tc: residual bf16/f32");
     C3B_REQUIRE(numel(in[idx]) >= M * N, "tc: residual too small");
     C3B_REQUIRE(((uintptr_t)in[idx].ptr & 15) == 0, "tc: residual must be 16-byte aligned");
     a.res = in[idx].ptr;
@@ -1471,7 +1434,8 @@ static int fill_epilogue(tc::TcArgs& a, const c3b_tensor* in, int n_in, int firs
     idx++;
   }
   C3B_REQUIRE(idx == n_in, "tc: input count does not match bias/residual flags");
-  C3B_REQUIRE(out.dtype == C3B_BF16 || out.dtype == C3B_F32, "tc: output bf16/f32");
+  C3B_REQUIRE(out.dtype == (a.h16 ? C3B_F16 : C3B_BF16) || out.dtype == C3B_F32,
+              a.h16 ? "tc: output fp16/f32" : "tc: output bf16/f32");
   C3B_REQUIRE(numel(out) >= M * N, "tc: output too small");
   C3B_REQUIRE(((uintptr_t)out.ptr & 15) == 0, "tc: output must be 16-byte aligned");
   a.out = out.ptr;
@@ -1505,7 +1469,8 @@ int launch_wait_probe(const c3b_wait_probe_params& p, cudaStream_t s) {
 int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p,
                    cudaStream_t s) {
   C3B_REQUIRE(n_in >= 2, "tc gemm: needs A and B");
-  C3B_REQUIRE(in[0].dtype == C3B_BF16 && in[1].dtype == C3B_BF16, "tc gemm: A and B must be bf16");
+  C3B_REQUIRE((in[0].dtype == C3B_BF16 || in[0].dtype == C3B_F16) && in[1].dtype == in[0].dtype,
+              "tc gemm: A and B must be both bf16 or both fp16");
   C3B_REQUIRE(p.K > 0 && p.K % 8 == 0, "tc gemm: K must be a positive multiple of 8");
   C3B_REQUIRE(p.N > 0 && p.N % 32 == 0, "tc gemm: N must be a positive multiple of 32");
   C3B_REQUIRE(p.M >= 0 && p.M < (int64_t)1 << 31, "tc gemm: M range");
@@ -1513,6 +1478,7 @@ int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0, "tc gemm: 16-byte alignment");
   tc::TcArgs a;
   memset(&a, 0, sizeof(a));
+  a.h16 = in[0].dtype == C3B_F16;
   int rc = fill_epilogue(a, in, n_in, 2, p.bias_mode, p.has_residual, p.M, p.N, out);
   if (rc) return rc;
   if (p.M == 0) return C3B_OK;
@@ -1553,6 +1519,7 @@ int launch_gemm_fp8(const c3b_tensor* in, int n_in, const c3b_tensor& out, const
               "fp8 gemm: 16-byte alignment");
   tc::TcArgs a;
   memset(&a, 0, sizeof(a));
+  a.h16 = out.dtype == C3B_F16;
   int rc = fill_epilogue(a, in, n_in, 4, p.bias_mode, p.has_residual, p.M, p.N, out);
   if (rc) return rc;
   if (p.M == 0) return C3B_OK;
@@ -1588,8 +1555,9 @@ int launch_gemm_fp8(const c3b_tensor* in, int n_in, const c3b_tensor& out, const
 int launch_gemm_w4a16(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p,
                       cudaStream_t s) {
   C3B_REQUIRE(n_in >= 3, "w4a16 gemm: needs A, packed B, B scales");
-  C3B_REQUIRE(in[0].dtype == C3B_BF16 && in[1].dtype == C3B_U8 && in[2].dtype == C3B_F32,
-              "w4a16 gemm: A bf16, B packed FP4 (u8), scales f32");
+  C3B_REQUIRE((in[0].dtype == C3B_BF16 || in[0].dtype == C3B_F16) && in[1].dtype == C3B_U8 &&
+                  in[2].dtype == C3B_F32,
+              "w4a16 gemm: A bf16 or fp16, B packed FP4 (u8), scales f32");
   C3B_REQUIRE(p.K > 0 && p.K % 64 == 0, "w4a16 gemm: K must be a positive multiple of 64");
   C3B_REQUIRE(p.N > 0 && p.N % 32 == 0, "w4a16 gemm: N must be a positive multiple of 32");
   C3B_REQUIRE(p.M >= 0 && p.M < (int64_t)1 << 31, "w4a16 gemm: M range");
@@ -1599,6 +1567,7 @@ int launch_gemm_w4a16(const c3b_tensor* in, int n_in, const c3b_tensor& out, con
               "w4a16 gemm: 16-byte alignment");
   tc::TcArgs a;
   memset(&a, 0, sizeof(a));
+  a.h16 = in[0].dtype == C3B_F16;  // the FP4 weights expand to the activations' format
   int rc = fill_epilogue(a, in, n_in, 3, p.bias_mode, p.has_residual, p.M, p.N, out);
   if (rc) return rc;
   if (p.M == 0) return C3B_OK;
@@ -1638,7 +1607,8 @@ int launch_gemm_w4a16(const c3b_tensor* in, int n_in, const c3b_tensor& out, con
 int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_tc_params& p,
                    cudaStream_t s) {
   C3B_REQUIRE(n_in == 3 + (p.has_residual ? 1 : 0), "tc conv: inputs x, w, bias [, residual]");
-  C3B_REQUIRE(in[0].dtype == C3B_BF16 && in[1].dtype == C3B_BF16, "tc conv: bf16 activations and weights");
+  C3B_REQUIRE((in[0].dtype == C3B_BF16 || in[0].dtype == C3B_F16) && in[1].dtype == in[0].dtype,
+              "tc conv: activations and weights both bf16 or both fp16");
   C3B_REQUIRE(p.cin % 64 == 0, "tc conv: Cin must be a multiple of 64");
   C3B_REQUIRE(p.cout % 32 == 0, "tc conv: Cout must be a multiple of 32");
   C3B_REQUIRE(p.stride == 1 || p.stride == 2, "tc conv: stride 1 or 2");
@@ -1657,6 +1627,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   const int64_t M = (int64_t)p.n * pix;
   tc::TcArgs a;
   memset(&a, 0, sizeof(a));
+  a.h16 = in[0].dtype == C3B_F16;
   int rc = fill_epilogue(a, in, n_in, 2, C3B_BIAS_COL, p.has_residual, M, p.cout, out);
   if (rc) return rc;
   if (M == 0) return C3B_OK;
@@ -1685,8 +1656,8 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   // Halo mode: 3x3, stride 1, pad 1, Cout <= 128 (one weight tile), two output
   // rows per super-tile.
   const int wt = p.wo < 16 ? p.wo : 16;
-  // (bf16 output and residual only: their epilogues store bf16 rows)
-  const bool bf16_epi = a.dt_out == C3B_BF16 && (!a.res || a.dt_res == C3B_BF16);
+  // (16-bit output and residual only: their epilogues store 16-bit rows)
+  const bool bf16_epi = a.dt_out != C3B_F32 && (!a.res || a.dt_res != C3B_F32);
   if (p.mode != 1 && bf16_epi && p.k == 3 && p.stride == 1 && p.pad == 1 && p.cout <= 128 && a.n_tiles_n == 1 &&
       p.wo % wt == 0 && 128 % wt == 0 && (128 / wt) >= 8 && p.ho % 2 == 0) {
     a.img = 128 / wt;
@@ -1834,7 +1805,8 @@ bool launch_stem_tc(const c3b_tensor* in, const c3b_tensor& out, const c3b_stem_
   const int n_tiles = (int)((M + 127) / 128);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
   *rc = launch_pdl(tc::tc_stem_kernel, grid, tc::STEM_THREADS, smem, s, maps, (const float*)in[0].ptr,
-                   (const float*)in[1].ptr, (const float*)in[2].ptr, g, p.act, M, n_tiles);
+                   (const float*)in[1].ptr, (const float*)in[2].ptr, g, p.act, M, n_tiles,
+                   (int)(out.dtype == C3B_F16));
   return true;
 }
 

@@ -411,6 +411,14 @@ __device__ __forceinline__ void st4(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint2*>(p) = t;
 }
 
+__device__ __forceinline__ void st4(__half* p, const float* v) {
+  __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+  uint2 t;
+  t.x = *reinterpret_cast<uint32_t*>(&a);
+  t.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = t;
+}
+
 template <typename TI, typename TO, int V>
 __global__ void __launch_bounds__(256) layernorm_vec_kernel(const TI* __restrict__ x, const TI* __restrict__ res,
                                                             const float* __restrict__ scale,
@@ -609,6 +617,17 @@ int launch_layernorm(const c3b_tensor* in, int n_in, const c3b_tensor* out, int 
   int sdt = p.write_sum ? out[1].dtype : 0;
   int g = grid_for(p.rows * 32, 256);
   const float* bp = bi ? (const float*)bi->ptr : nullptr;
+  const bool vec_f16 = !p.write_sum && x.dtype == C3B_F32 && !res && out[0].dtype == C3B_F16 &&
+                       ((uintptr_t)x.ptr % 16 == 0) && ((uintptr_t)out[0].ptr % 16 == 0) &&
+                       ((uintptr_t)sc.ptr % 16 == 0) && (!bp || (uintptr_t)bp % 16 == 0);
+  if (vec_f16) {  // fp16 profile: fp32 residual stream -> fp16 rows for the next GEMM
+    const int gv = (int)std::min<int64_t>((p.rows * 32 + 255) / 256, (int64_t)sm_count() * 16);
+    if (launch_ln_vec<float, __half>(x.ptr, rp, (const float*)sc.ptr, bp, out[0].ptr, p.rows, p.cols, p.epsilon, s,
+                                     gv)) {
+      C3B_CHECK_CUDA(cudaGetLastError());
+      return C3B_OK;
+    }
+  }
   const bool vec_ok = !p.write_sum && (x.dtype == C3B_F32 || x.dtype == C3B_BF16) &&
                       (!res || res->dtype == x.dtype) && (out[0].dtype == C3B_F32 || out[0].dtype == C3B_BF16) &&
                       ((uintptr_t)x.ptr % 16 == 0) && (!res || (uintptr_t)res->ptr % 16 == 0) &&
@@ -984,7 +1003,7 @@ int launch_stem_conv(const c3b_tensor* in, int n_in, const c3b_tensor& out, cons
   const c3b_stem_params& g = p.geom;
   const int K = g.g.kh * g.g.kw * g.c;
   C3B_REQUIRE(in[0].dtype == C3B_F32 && in[1].dtype == C3B_F32 && in[2].dtype == C3B_F32, "stem conv: f32 inputs");
-  C3B_REQUIRE(out.dtype == C3B_BF16, "stem conv: bf16 NHWC output");
+  C3B_REQUIRE(out.dtype == C3B_BF16 || out.dtype == C3B_F16, "stem conv: bf16 or fp16 NHWC output");
   C3B_REQUIRE(p.cout == 64 || p.cout == 32 || p.cout == 16, "stem conv: Cout 16, 32 or 64");
   C3B_REQUIRE(K <= 64, "stem conv: at most 64 taps x channels");
   C3B_REQUIRE(numel(in[0]) == (int64_t)g.n * g.c * g.h * g.w, "stem conv: input extents");
@@ -996,6 +1015,7 @@ int launch_stem_conv(const c3b_tensor* in, int n_in, const c3b_tensor& out, cons
   C3B_REQUIRE((uintptr_t)in[1].ptr % 16 == 0, "stem conv: weight alignment");
   int trc = C3B_OK;
   if (launch_stem_tc(in, out, p, s, &trc)) return trc;  // tcgen05 path (Cout 64, K <= 32)
+  C3B_REQUIRE(out.dtype == C3B_BF16, "stem conv: an fp16 output needs the tcgen05 stem (Cout 64, K <= 32)");
   if (launch_stem_mma(in, out, p, s)) {  // mma.sync path (Cout 64, K <= 32)
     C3B_CHECK_CUDA(cudaGetLastError());
     return C3B_OK;

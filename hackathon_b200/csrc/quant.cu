@@ -34,6 +34,12 @@ __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, flo
   for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(h[i]);
 }
 
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float* v) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  unpack8h(u, v, true);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(QWARPS * 32) quant_e4m3_kernel(const T* __restrict__ x, uint8_t* __restrict__ q,
                                                                  float* __restrict__ scale, int64_t M, int64_t K) {
@@ -96,7 +102,7 @@ __global__ void quant_fp4_kernel(const T* __restrict__ x, uint8_t* __restrict__ 
 // times the group scale, one bf16 rounding), so both paths see identical
 // weights.  One thread per (row, 16-element group).
 __global__ void dequant_fp4_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scale,
-                                   __nv_bfloat16* __restrict__ w, int64_t N, int64_t K) {
+                                   uint16_t* __restrict__ w, int64_t N, int64_t K, int h16) {
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t groups = K / 16;
   if (gid >= N * groups) return;
@@ -104,24 +110,24 @@ __global__ void dequant_fp4_kernel(const uint8_t* __restrict__ q, const float* _
   const uint2 pk = __ldg(reinterpret_cast<const uint2*>(q + n * (K / 2) + g * 8));
   const float sc = __ldg(scale + ((g >> 2) * N + n) * 4 + (g & 3));
   const float2 s2 = make_float2(sc, sc);
-  __align__(16) __nv_bfloat162 o[8];
+  uint32_t o[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const uint32_t word = j < 4 ? pk.x : pk.y;
     const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((word >> (8 * (j & 3))) & 0xFF), __NV_E2M1);
-    o[j] = __float22bfloat162_rn(__fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), s2));
+    o[j] = pack2h(__fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), s2), h16);
   }
   uint4* dst = reinterpret_cast<uint4*>(w + n * K + g * 16);
-  dst[0] = reinterpret_cast<const uint4*>(o)[0];
-  dst[1] = reinterpret_cast<const uint4*>(o)[1];
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 }  // namespace
 
 int launch_dequant_fp4(const c3b_tensor& q, const c3b_tensor& scale, const c3b_tensor& w, const c3b_quant_params& p,
                        cudaStream_t s) {
-  C3B_REQUIRE(q.dtype == C3B_U8 && scale.dtype == C3B_F32 && w.dtype == C3B_BF16,
-              "dequantize fp4: inputs u8 codes and f32 scales, output bf16");
+  C3B_REQUIRE(q.dtype == C3B_U8 && scale.dtype == C3B_F32 && (w.dtype == C3B_BF16 || w.dtype == C3B_F16),
+              "dequantize fp4: inputs u8 codes and f32 scales, output bf16 or fp16");
   C3B_REQUIRE(p.M >= 0 && p.K > 0 && p.K % 64 == 0, "dequantize fp4: K must be a positive multiple of 64");
   C3B_REQUIRE(numel(q) >= p.M * p.K / 2 && numel(scale) >= p.M * p.K / 16 && numel(w) >= p.M * p.K,
               "dequantize fp4: extents");
@@ -129,7 +135,8 @@ int launch_dequant_fp4(const c3b_tensor& q, const c3b_tensor& scale, const c3b_t
   const int64_t work = p.M * (p.K / 16);
   if (work == 0) return C3B_OK;
   dequant_fp4_kernel<<<(unsigned)((work + 255) / 256), 256, 0, s>>>((const uint8_t*)q.ptr, (const float*)scale.ptr,
-                                                                   (__nv_bfloat16*)w.ptr, p.M, p.K);
+                                                                   (uint16_t*)w.ptr, p.M, p.K,
+                                                                   (int)(w.dtype == C3B_F16));
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
@@ -156,7 +163,8 @@ int launch_quant_fp4(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor&
 
 int launch_quant_e4m3(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor& scale, const c3b_quant_params& p,
                       cudaStream_t s) {
-  C3B_REQUIRE(x.dtype == C3B_F32 || x.dtype == C3B_BF16, "quantize e4m3: input f32 or bf16");
+  C3B_REQUIRE(x.dtype == C3B_F32 || x.dtype == C3B_BF16 || x.dtype == C3B_F16,
+              "quantize e4m3: input f32, bf16 or fp16");
   C3B_REQUIRE(q.dtype == C3B_U8 && scale.dtype == C3B_F32, "quantize e4m3: outputs u8 and f32");
   C3B_REQUIRE(p.M >= 0 && p.K > 0 && p.K % 16 == 0, "quantize e4m3: K must be a positive multiple of 16");
   C3B_REQUIRE(numel(x) >= p.M * p.K && numel(q) >= p.M * p.K && numel(scale) >= p.M, "quantize e4m3: extents");
@@ -166,6 +174,9 @@ int launch_quant_e4m3(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor
   if (x.dtype == C3B_F32)
     quant_e4m3_kernel<float><<<blocks, QWARPS * 32, 0, s>>>((const float*)x.ptr, (uint8_t*)q.ptr, (float*)scale.ptr,
                                                             p.M, p.K);
+  else if (x.dtype == C3B_F16)
+    quant_e4m3_kernel<__half><<<blocks, QWARPS * 32, 0, s>>>((const __half*)x.ptr, (uint8_t*)q.ptr,
+                                                             (float*)scale.ptr, p.M, p.K);
   else
     quant_e4m3_kernel<__nv_bfloat16><<<blocks, QWARPS * 32, 0, s>>>((const __nv_bfloat16*)x.ptr, (uint8_t*)q.ptr,
                                                                     (float*)scale.ptr, p.M, p.K);

@@ -142,6 +142,10 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 __host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
+// The same with A=B=fp16 (format code 0) when h16 is set, else bf16.
+__host__ __device__ constexpr uint32_t instr_desc_h(int m, int n, int h16) {
+  return h16 ? ((1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24)) : instr_desc(m, n);
+}
 
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accum) {

@@ -21,7 +21,9 @@ Patterns recognised on the unfused ONNX graph:
   moves in front of the (row-wise) LayerNorm.
 
 Precision profiles: ``fp32`` keeps IEEE FP32 math everywhere (SIMT FFMA
-contractions); ``bf16`` runs contractions on tcgen05 with bf16 operands and
+contractions); ``fp16`` is ``bf16`` with fp16 in place of bf16 (tcgen05
+``kind::f16`` with fp16 operands, fp16 activations, the same fp32
+accumulation, residual stream and logits); ``bf16`` runs contractions on tcgen05 with bf16 operands and
 fp32 accumulation, NHWC bf16 activations for convolutions, an fp32 residual
 stream and fp32 LayerNorm statistics for transformers, fp32 logits; ``fp8``
 is ``bf16`` with the linear layers the reference's precision policy marks fp8
@@ -33,7 +35,8 @@ two scales applied in the epilogue; ``mixed`` applies the whole GEMM policy
 GEMMs with K, N >= 128, K and N multiples of 32 and K*N >= 32768 run W4A16
 (FP4 E2M1 weights in groups of 16 with fp32 scales, expanded to bf16 in
 shared memory next to the MMA), other aligned GEMMs with K, N >= 64 run fp8,
-the rest bf16.
+the rest fp16 (its 16-bit activations are fp16 throughout, the policy's
+activation format, c32/strategy.py:102-108).
 """
 
 from __future__ import annotations
@@ -72,8 +75,12 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 class _State:
     def __init__(self, graph: ModelGraph, batch: int, profile: str):
-        if profile not in ("fp32", "bf16", "fp8", "mixed"):
+        if profile not in ("fp32", "bf16", "fp16", "fp8", "mixed"):
             raise ValueError(f"unknown precision profile {profile!r}")
+        # 16-bit format of tensor-core operands and 16-bit activations: fp16 for
+        # the fp16 profile and for `mixed` (the reference policy's activation
+        # format, c32/strategy.py:102-108), bf16 otherwise
+        self.t16 = L.F16 if profile in ("fp16", "mixed") else L.BF16
         self.g = graph
         self.batch = batch
         self.profile = profile
@@ -100,6 +107,12 @@ class _State:
 
     def t(self, logical: str) -> str:
         return self.alias.get(logical, logical)
+
+    def bits16(self, x: np.ndarray) -> np.ndarray:
+        """float32 -> this profile's 16-bit weight bits (uint16)."""
+        if self.t16 == L.F16:
+            return np.ascontiguousarray(x, np.float32).astype(np.float16).view(np.uint16)
+        return bf16_bits(x)
 
     def weight(self, stem: str, host: np.ndarray, dtype: int) -> str:
         self.wcount += 1
@@ -434,7 +447,8 @@ def _ln_feeds_f8_linear(st: _State, op: dict, cols: int) -> bool:
 
 
 def _emit(st: _State, op: dict) -> None:
-    P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp8", "mixed")
+    P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp16", "fp8", "mixed")
+    T16 = st.t16
     k = op["kind"]
     if k == "conv":
         x = st.t(op["x"])
@@ -466,7 +480,7 @@ def _emit(st: _State, op: dict) -> None:
             # stem: direct conv from the NCHW f32 input to NHWC bf16 (K = C*kh*kw is tiny)
             wk = np.ascontiguousarray(w.reshape(O, -1).T, np.float32)  # [K (c,r,s)][Cout]
             wname = st.weight("stem", wk, L.F32)
-            P.add_tensor(out, (N * Ho * Wo, O), L.BF16)
+            P.add_tensor(out, (N * Ho * Wo, O), T16)
             sp = L.StemParams()
             sp.n, sp.c, sp.h, sp.w, sp.ho, sp.wo, sp.kpad = N, C, H, W, Ho, Wo, 0
             sp.g = geo
@@ -483,9 +497,9 @@ def _emit(st: _State, op: dict) -> None:
             kpad = (C * kh * kw + 63) // 64 * 64
             wk = np.zeros((O, kpad), np.float32)
             wk[:, :C * kh * kw] = w.transpose(0, 2, 3, 1).reshape(O, -1)
-            wname = st.weight("stem", bf16_bits(wk), L.BF16)
-            cols = P.add_tensor(f"{out}:cols", (N * Ho * Wo, kpad), L.BF16)
-            P.add_tensor(out, (N * Ho * Wo, O), L.BF16)
+            wname = st.weight("stem", st.bits16(wk), T16)
+            cols = P.add_tensor(f"{out}:cols", (N * Ho * Wo, kpad), T16)
+            P.add_tensor(out, (N * Ho * Wo, O), T16)
             sp = L.StemParams()
             sp.n, sp.c, sp.h, sp.w, sp.ho, sp.wo, sp.kpad = N, C, H, W, Ho, Wo, kpad
             sp.g = geo
@@ -502,8 +516,8 @@ def _emit(st: _State, op: dict) -> None:
         else:
             if lay != "nhwc":
                 raise RuntimeError("bf16 conv expects NHWC bf16 activations")
-            wname = st.weight("conv", bf16_bits(np.ascontiguousarray(w.transpose(0, 2, 3, 1))), L.BF16)
-            P.add_tensor(out, (N * Ho * Wo, O), L.BF16)
+            wname = st.weight("conv", st.bits16(np.ascontiguousarray(w.transpose(0, 2, 3, 1))), T16)
+            P.add_tensor(out, (N * Ho * Wo, O), T16)
             cp = L.ConvTcParams()
             if kh != kw or geo.ph0 != geo.ph1 or geo.pw0 != geo.ph0 or geo.sh != geo.sw or geo.dh != 1:
                 raise NotImplementedError("tc conv: square kernels, symmetric padding, equal strides")
@@ -577,7 +591,7 @@ def _emit(st: _State, op: dict) -> None:
             st.layout[out] = "rows"
             st.lshape[out] = shp
             return
-        P.add_tensor(out, (rows, cols), L.BF16 if bf else L.F32)
+        P.add_tensor(out, (rows, cols), T16 if bf else L.F32)
 
         def build(d, x=x, sname=sname, bname=bname, out=out, lp=lp, rows=rows, cols=cols):
             ins = [d[x].t((rows, cols)), d[sname].t()] + ([d[bname].t()] if bname else [])
@@ -609,7 +623,7 @@ def _emit(st: _State, op: dict) -> None:
         res = st.t(op["res"]) if op["res"] else None
         out = op["out"]
         flops = 2.0 * M * N * K
-        use_tc = bf and N % 32 == 0 and K % 64 == 0 and (x in st.fused_q or P.tensors[x].dtype == L.BF16)
+        use_tc = bf and N % 32 == 0 and K % 64 == 0 and (x in st.fused_q or P.tensors[x].dtype == T16)
         bname = st.weight("bias", (op["b"] * op.get("beta", 1.0)).astype(np.float32), L.F32) \
             if op["b"] is not None else None
         # the reference policy for GEMMs (c32/strategy.py:146-157): fp4 (W4A16)
@@ -624,7 +638,7 @@ def _emit(st: _State, op: dict) -> None:
             wq, ws = quant_groups_fp4(w)
             wqn = st.weight("linear_fp4", wq, L.U8)
             wsn = st.weight("linear_fp4_scale", ws, L.F32)
-            odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else L.BF16
+            odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else T16
             P.add_tensor(out, (M, N), odt)
 
             if M >= W4A16_EXPAND_ROWS:
@@ -632,7 +646,7 @@ def _emit(st: _State, op: dict) -> None:
                 # arena tensor) and run the bf16 GEMM, instead of re-expanding
                 # them next to the MMA for every 128-row tile
                 wdq = f"{out}:w_bf16"
-                P.add_tensor(wdq, (N, K), L.BF16)
+                P.add_tensor(wdq, (N, K), T16)
 
                 def build_dq(d, wqn=wqn, wsn=wsn, wdq=wdq, N=N, K=K):
                     return [Launch(L.K_DEQUANT_FP4, [d[wqn].t(), d[wsn].t()], [d[wdq].t()], L.QuantParams(N, K))]
@@ -658,7 +672,7 @@ def _emit(st: _State, op: dict) -> None:
             wq, ws = quant_rows_e4m3(w)
             wqn = st.weight("linear_e4m3", wq, L.U8)
             wsn = st.weight("linear_e4m3_scale", ws, L.F32)
-            odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else L.BF16
+            odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else T16
             P.add_tensor(out, (M, N), odt)
             if x in st.fused_q:  # quantised by the producing LayerNorm
                 xq, xs = st.fused_q[x]
@@ -685,9 +699,9 @@ def _emit(st: _State, op: dict) -> None:
         elif use_tc:
             if op.get("alpha", 1.0) != 1.0:
                 raise NotImplementedError("tc linear: alpha != 1")
-            wname = st.weight("linear", bf16_bits(w), L.BF16)
+            wname = st.weight("linear", st.bits16(w), T16)
             # outputs feeding a residual stream or the logits stay fp32
-            odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else L.BF16
+            odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else T16
             P.add_tensor(out, (M, N), odt)
 
             def build(d, x=x, wname=wname, bname=bname, out=out, M=M, N=N, K=K, act=op["act"], res=res):

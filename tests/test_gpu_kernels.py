@@ -684,3 +684,118 @@ def test_flash_attention_growing_scores(torch_cuda, dt, growth, qscale):
     smax = float(np.abs(np.matmul(q, k.transpose(0, 1, 3, 2))).max()) / 8.0
     tol = max(RTOL, 4.0 * float(np.finfo(np.float32).eps) * smax)
     assert rel(got, ref) < (tol if dt == "f32" else 2e-2)
+
+
+# ------------------------------------------------------------------ fp16 profile
+
+def _f16(t, a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda().to(torch.float16)
+
+
+def _round_f16(a):
+    return np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+
+
+@pytest.mark.parametrize("M,N,K,act,res,odt", [(128, 64, 64, 0, 0, "f32"), (300, 128, 192, 1, 1, "f16"),
+                                               (1000, 256, 512, 2, 1, "f32"), (257, 96, 72, 0, 1, "f16")])
+def test_gemm_tc_fp16(torch_cuda, M, N, K, act, res, odt):
+    """tcgen05 kind::f16 with fp16 operands (format code 0): fp16 A and B, fp32
+    accumulation, fp32 or fp16 output, fp16 residual with an fp16 output."""
+    import torch
+    from hackathon_b200 import _lib as L
+    a, w, b = _round_f16(randn(M, K)), _round_f16(randn(N, K) * 0.1), randn(N)
+    r = _round_f16(randn(M, N))
+    code = L.F32 if odt == "f32" else L.F16
+    out = torch.empty((M, N), dtype=torch.float32 if odt == "f32" else torch.float16, device="cuda")
+    g = L.GemmTcParams()
+    g.M, g.N, g.K, g.bias_mode, g.act, g.has_residual, g.block_n = M, N, K, L.BIAS_COL, act, res, 0
+    ta, tw, tb = _f16(torch, a), _f16(torch, w), dev(torch, b)
+    tr = _f16(torch, r) if odt == "f16" else dev(torch, r)
+    ins = [L.make_tensor(ta.data_ptr(), L.F16, (M, K)), L.make_tensor(tw.data_ptr(), L.F16, (N, K)),
+           L.make_tensor(tb.data_ptr(), L.F32, (N,))]
+    if res:
+        ins.append(L.make_tensor(tr.data_ptr(), L.F16 if odt == "f16" else L.F32, (M, N)))
+    L.launch(L.K_GEMM_TC, ins, [L.make_tensor(out.data_ptr(), code, (M, N))], g,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + b
+    if res:
+        ref = ref + r
+    if act == 1:
+        ref = np.maximum(ref, 0)
+    elif act == 2:
+        ref = O.gelu_erf(ref.astype(np.float32))
+    # fp32 output: accumulation order only; fp16 output: half an fp16 ulp
+    assert rel(host(out), ref) < (2e-5 if odt == "f32" else 1e-3)
+
+
+def test_gemm_tc_rejects_mixed_16bit_operands(torch_cuda):
+    import torch
+    from hackathon_b200 import _lib as L
+    a = torch.zeros((128, 64), dtype=torch.float16, device="cuda")
+    w = torch.zeros((64, 64), dtype=torch.bfloat16, device="cuda")
+    out = torch.empty((128, 64), dtype=torch.float32, device="cuda")
+    g = L.GemmTcParams()
+    g.M, g.N, g.K = 128, 64, 64
+    with pytest.raises(RuntimeError, match="both bf16 or both fp16"):
+        L.launch(L.K_GEMM_TC, [L.make_tensor(a.data_ptr(), L.F16, (128, 64)), L.make_tensor(w.data_ptr(), L.BF16, (64, 64))],
+                 [L.make_tensor(out.data_ptr(), L.F32, (128, 64))], g, torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("n,h,cin,cout,k,stride,res", [(2, 32, 64, 64, 3, 1, 0), (3, 16, 64, 128, 3, 2, 0),
+                                                       (4, 16, 128, 128, 3, 1, 1), (8, 8, 128, 256, 1, 2, 0),
+                                                       (9, 32, 64, 64, 3, 1, 1)])
+def test_conv_tc_fp16(torch_cuda, n, h, cin, cout, k, stride, res, mode):
+    """The convolution variants (row ring, halo, per-tap windows) with fp16
+    activations, weights, residual and output."""
+    import torch
+    from hackathon_b200 import _lib as L
+    pad = k // 2
+    x = _round_f16(randn(n, cin, h, h))
+    w = _round_f16(randn(cout, cin, k, k) * 0.05)
+    b = randn(cout)
+    ref = O.conv2d(x, w, b, strides=[stride, stride], pads=[pad] * 4)
+    ho = ref.shape[2]
+    r = _round_f16(randn(n, cout, ho, ho)) if res else None
+    if res:
+        ref = np.maximum(ref + r, 0)
+    xn = _f16(torch, x.transpose(0, 2, 3, 1))
+    wn = _f16(torch, w.transpose(0, 2, 3, 1))
+    tb = dev(torch, b)
+    out = torch.empty((n, ho, ho, cout), dtype=torch.float16, device="cuda")
+    cp = L.ConvTcParams()
+    cp.n, cp.h, cp.w, cp.cin, cp.cout, cp.ho, cp.wo, cp.k, cp.stride, cp.pad = n, h, h, cin, cout, ho, ho, k, stride, pad
+    cp.has_residual, cp.act, cp.block_n, cp.mode = res, 1 if res else 0, 0, mode
+    ins = [L.make_tensor(xn.data_ptr(), L.F16, (n, h, h, cin)), L.make_tensor(wn.data_ptr(), L.F16, (cout, k, k, cin)),
+           L.make_tensor(tb.data_ptr(), L.F32, (cout,))]
+    if res:
+        rn = _f16(torch, r.transpose(0, 2, 3, 1))
+        ins.append(L.make_tensor(rn.data_ptr(), L.F16, (n, ho, ho, cout)))
+    L.launch(L.K_CONV_TC, ins, [L.make_tensor(out.data_ptr(), L.F16, (n, ho, ho, cout))], cp,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    got = out.float().cpu().numpy().transpose(0, 3, 1, 2)
+    assert rel(got, ref) < 1e-3  # fp16 output rounding: half an ulp is 2^-11
+
+
+@pytest.mark.parametrize("B,S,H", [(2, 128, 4), (2, 512, 3)])
+def test_flash_attention_fp16(torch_cuda, B, S, H):
+    import torch
+    from hackathon_b200 import _lib as L
+    D = 64
+    qkv = _round_f16(randn(B, S, 3, H, D))
+    q, k, v = (qkv[:, :, i].transpose(0, 2, 1, 3) for i in range(3))
+    ref = O.causal_attention(q, k, v, 1.0 / 8.0).transpose(0, 2, 1, 3).reshape(B, S, H * D)
+    tq = _f16(torch, qkv)
+    out = torch.empty((B, S, H * D), dtype=torch.float16, device="cuda")
+    L.launch(L.K_FLASH_ATTN, [L.make_tensor(tq.data_ptr(), L.F16, (B, S, 3, H, D))],
+             [L.make_tensor(out.data_ptr(), L.F16, (B, S, H * D))], L.FlashParams(B, S, H, D, 1.0 / 8.0, 1),
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    # P is rounded to fp16 (2^-11) before P.V; the output to fp16
+    assert rel(out.float().cpu().numpy(), ref) < 4e-3
