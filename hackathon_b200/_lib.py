@@ -27,14 +27,14 @@ TENSOR_ARENA = 1
 # kernel ids
 K_EW, K_COPY, K_IM2COL, K_REDUCE, K_GEMM, K_LAYERNORM, K_SOFTMAX, K_ATTN_SCORES, K_GATHER, K_CONV, \
     K_GEMM_TC, K_CONV_TC, K_FLASH_ATTN, K_EMBED, K_STEM_IM2COL, K_GAP_NHWC, K_STEM_CONV, \
-    K_QUANT_E4M3, K_GEMM_FP8, K_QUANT_FP4, K_GEMM_W4A16, K_DEQUANT_FP4, K_WAIT_PROBE = range(1, 24)
+    K_QUANT_E4M3, K_GEMM_FP8, K_QUANT_FP4, K_GEMM_W4A16, K_DEQUANT_FP4, K_WAIT_PROBE, K_GEMM_TF32 = range(1, 25)
 KERNEL_NAMES = {
     0: "noop", K_EW: "ew", K_COPY: "copy", K_IM2COL: "im2col", K_REDUCE: "reduce", K_GEMM: "gemm_simt",
     K_LAYERNORM: "layernorm", K_SOFTMAX: "softmax", K_ATTN_SCORES: "attn_scores", K_GATHER: "gather",
     K_CONV: "conv_simt", K_GEMM_TC: "gemm_tc", K_CONV_TC: "conv_tc", K_FLASH_ATTN: "flash_attn",
     K_EMBED: "embed", K_STEM_IM2COL: "stem_im2col", K_GAP_NHWC: "gap_nhwc", K_STEM_CONV: "stem_conv",
     K_QUANT_E4M3: "quant_e4m3", K_GEMM_FP8: "gemm_fp8", K_QUANT_FP4: "quant_fp4", K_GEMM_W4A16: "gemm_w4a16",
-    K_DEQUANT_FP4: "dequant_fp4", K_WAIT_PROBE: "wait_probe",
+    K_DEQUANT_FP4: "dequant_fp4", K_WAIT_PROBE: "wait_probe", K_GEMM_TF32: "gemm_tf32",
 }
 
 # ew ops

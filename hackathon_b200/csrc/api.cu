@@ -79,6 +79,13 @@ static const NameEntry kNames[] = {
     // W4A16 path (the policy's fp4 for constant-weight GEMMs)
     {"quantize_fp4_groups", C3B_K_QUANT_FP4}, {"matmul_f4", C3B_K_GEMM_W4A16},
     {"gemm_bias_act_w4a16", C3B_K_GEMM_W4A16}, {"dequantize_fp4_groups", C3B_K_DEQUANT_FP4},
+    // tf32 profile and the fused nodes of the backend's extra C3.3 passes
+    {"gemm_bias_act_tf32", C3B_K_GEMM_TF32},
+    {"b200convbiasact_f32", C3B_K_CONV}, {"b200convbiasact_bf16", C3B_K_CONV_TC},
+    {"b200convbiasact_fp16", C3B_K_CONV_TC}, {"b200linearepilogue_f32", C3B_K_GEMM},
+    {"b200linearepilogue_bf16", C3B_K_GEMM_TC}, {"b200linearepilogue_fp16", C3B_K_GEMM_TC},
+    {"b200flashattention_f32", C3B_K_FLASH_ATTN}, {"b200flashattention_bf16", C3B_K_FLASH_ATTN},
+    {"b200flashattention_fp16", C3B_K_FLASH_ATTN},
 };
 
 static int find_name(const std::string& n) {
@@ -257,6 +264,12 @@ int dispatch(int kid, const c3b_tensor* in, int n_in, const c3b_tensor* out, int
       if ((rc = get_params(params, len, p))) return rc;
       C3B_REQUIRE(n_out == 1, "w4a16 gemm: one output");
       return launch_gemm_w4a16(in, n_in, out[0], p, s);
+    }
+    case C3B_K_GEMM_TF32: {
+      c3b_gemm_tc_params p;
+      if ((rc = get_params(params, len, p))) return rc;
+      C3B_REQUIRE(n_out == 1, "tf32 gemm: one output");
+      return launch_gemm_tf32(in, n_in, out[0], p, s);
     }
     case C3B_K_WAIT_PROBE: {
       c3b_wait_probe_params p;

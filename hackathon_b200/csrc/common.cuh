@@ -207,6 +207,7 @@ int launch_stem_conv(const c3b_tensor* in, int n_in, const c3b_tensor& out, cons
                      cudaStream_t s);
 int launch_gap_nhwc(const c3b_tensor& in, const c3b_tensor& out, const c3b_gap_params& p, cudaStream_t s);
 int launch_wait_probe(const c3b_wait_probe_params& p, cudaStream_t s);
+int launch_gemm_tf32(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p, cudaStream_t s);
 bool flash_tc_supported(const c3b_flash_params& p);
 int launch_flash_tc(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_flash_params& p, cudaStream_t s);
 int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_params& p, cudaStream_t s);

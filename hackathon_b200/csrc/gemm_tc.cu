@@ -260,8 +260,8 @@ constexpr int W4_GROUP = 16;  // K elements per FP4 scale
 
 template <int MODE>
 __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
-  constexpr bool F8 = MODE == 1, W4 = MODE == 2;
-  constexpr int KEL = F8 ? 128 : BK;  // elements per K block (one 128-byte row)
+  constexpr bool F8 = MODE == 1, W4 = MODE == 2, TF = MODE == 3;
+  constexpr int KEL = F8 ? 128 : TF ? 32 : BK;  // elements per K block (one 128-byte row)
   constexpr int EPIW = W4 ? 8 : 16;   // epilogue warps
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled stages.
@@ -375,7 +375,8 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = F8 ? instr_desc_e4m3(BM, a.block_n) : instr_desc_h(BM, a.block_n, a.h16);
+      const uint32_t idesc =
+          F8 ? instr_desc_e4m3(BM, a.block_n) : TF ? instr_desc_tf32(BM, a.block_n) : instr_desc_h(BM, a.block_n, a.h16);
       // stage descriptors = base descriptor + offset in 16-byte units
       const uint64_t ad0 = smem_desc(smem_u32(sa)), bd0 = smem_desc(smem_u32(sb));
       int stage = 0;
@@ -396,6 +397,8 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
           for (int k = 0; k < 4; ++k) {  // four 32-byte K steps per 128-byte row
             if (F8)
               mma_e4m3(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else if (TF)
+              mma_tf32(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
             else
               mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
@@ -1408,6 +1411,7 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
 }
 
 static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s, int mode = 0) {
+  if (mode == 3) return launch_tc_mode<3>(maps, a, s);
   if (mode == 1) return launch_tc_mode<1>(maps, a, s);
   if (mode == 2) return launch_tc_mode<2>(maps, a, s);
   return launch_tc_mode<0>(maps, a, s);
@@ -1503,6 +1507,51 @@ int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   }
   if ((rc = enable_tma_out(maps, a))) return rc;
   return launch_tc(maps, a, s);
+}
+
+// fp32 operands on the tensor cores as tf32 (the tf32 precision profile):
+// kind::tf32 reads fp32 words and uses their 10 leading mantissa bits, fp32
+// accumulation in TMEM, the same epilogue as the bf16 GEMM.
+int launch_gemm_tf32(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p,
+                     cudaStream_t s) {
+  C3B_REQUIRE(n_in >= 2, "tf32 gemm: needs A and B");
+  C3B_REQUIRE(in[0].dtype == C3B_F32 && in[1].dtype == C3B_F32, "tf32 gemm: A and B must be f32");
+  C3B_REQUIRE(p.K > 0 && p.K % 4 == 0, "tf32 gemm: K must be a positive multiple of 4");
+  C3B_REQUIRE(p.N > 0 && p.N % 32 == 0, "tf32 gemm: N must be a positive multiple of 32");
+  C3B_REQUIRE(p.M >= 0 && p.M < (int64_t)1 << 31, "tf32 gemm: M range");
+  C3B_REQUIRE(numel(in[0]) >= p.M * p.K && numel(in[1]) >= p.N * p.K, "tf32 gemm: operand extents");
+  C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0, "tf32 gemm: 16-byte alignment");
+  C3B_REQUIRE(out.dtype == C3B_F32, "tf32 gemm: f32 output");
+  tc::TcArgs a;
+  memset(&a, 0, sizeof(a));
+  int rc = fill_epilogue(a, in, n_in, 2, p.bias_mode, p.has_residual, p.M, p.N, out);
+  if (rc) return rc;
+  C3B_REQUIRE(!a.res || a.dt_res == C3B_F32, "tf32 gemm: f32 residual");
+  if (p.M == 0) return C3B_OK;
+  a.M = p.M; a.N = p.N; a.K = p.K; a.act = p.act;
+  a.block_n = pick_block_n(p.N, p.block_n);
+  a.n_tiles_n = (int)((p.N + a.block_n - 1) / a.block_n);
+  a.n_tiles = (int)((p.M + tc::BM - 1) / tc::BM) * a.n_tiles_n;
+  a.k_blocks = (int)((p.K + 31) / 32);
+  tc::TmaMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    uint64_t str[1] = {(uint64_t)p.K * 4};
+    uint32_t box[2] = {32, tc::BM};
+    if ((rc = encode(&maps.a[0], in[0].ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return rc;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
+    uint64_t str[1] = {(uint64_t)p.K * 4};
+    uint32_t box[2] = {32, (uint32_t)a.block_n};
+    if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return rc;
+  }
+  return launch_tc(maps, a, s, 3);
 }
 
 int launch_gemm_fp8(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p,

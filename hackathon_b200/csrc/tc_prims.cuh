@@ -142,6 +142,21 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 __host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
+// Instruction descriptor for kind::tf32: D=f32, A=B=tf32 (format code 2), K-major.
+__host__ __device__ constexpr uint32_t instr_desc_tf32(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// tf32 x tf32 -> f32 (kind::tf32, K = 8 per instruction: 32 bytes of fp32, the
+// same byte step as a bf16 K = 16 instruction).
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accum) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+
 // The same with A=B=fp16 (format code 0) when h16 is set, else bf16.
 __host__ __device__ constexpr uint32_t instr_desc_h(int m, int n, int h16) {
   return h16 ? ((1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24)) : instr_desc(m, n);

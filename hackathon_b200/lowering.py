@@ -21,7 +21,10 @@ Patterns recognised on the unfused ONNX graph:
   moves in front of the (row-wise) LayerNorm.
 
 Precision profiles: ``fp32`` keeps IEEE FP32 math everywhere (SIMT FFMA
-contractions); ``fp16`` is ``bf16`` with fp16 in place of bf16 (tcgen05
+contractions); ``tf32`` is ``fp32`` with the linear layers (N % 32 == 0,
+K % 4 == 0) on tcgen05 ``kind::tf32`` (fp32 operands read with a 10-bit
+mantissa, fp32 accumulation), convolutions and attention still fp32 SIMT;
+``fp16`` is ``bf16`` with fp16 in place of bf16 (tcgen05
 ``kind::f16`` with fp16 operands, fp16 activations, the same fp32
 accumulation, residual stream and logits); ``bf16`` runs contractions on tcgen05 with bf16 operands and
 fp32 accumulation, NHWC bf16 activations for convolutions, an fp32 residual
@@ -33,7 +36,7 @@ per-output-row scales, tcgen05 ``kind::f8f6f4`` with fp32 accumulation and the
 two scales applied in the epilogue; ``mixed`` applies the whole GEMM policy
 (c32/strategy.py:146-157) for a device that supports fp8 and fp4: constant-weight
 GEMMs with K, N >= 128, K and N multiples of 32 and K*N >= 32768 run W4A16
-(FP4 E2M1 weights in groups of 16 with fp32 scales, expanded to bf16 in
+(FP4 E2M1 weights in groups of 16 with fp32 scales, expanded to fp16 in
 shared memory next to the MMA), other aligned GEMMs with K, N >= 64 run fp8,
 the rest fp16 (its 16-bit activations are fp16 throughout, the policy's
 activation format, c32/strategy.py:102-108).
@@ -75,7 +78,7 @@ def bf16_to_f32(b: np.ndarray) -> np.ndarray:
 
 class _State:
     def __init__(self, graph: ModelGraph, batch: int, profile: str):
-        if profile not in ("fp32", "bf16", "fp16", "fp8", "mixed"):
+        if profile not in ("fp32", "tf32", "bf16", "fp16", "fp8", "mixed"):
             raise ValueError(f"unknown precision profile {profile!r}")
         # 16-bit format of tensor-core operands and 16-bit activations: fp16 for
         # the fp16 profile and for `mixed` (the reference policy's activation
@@ -707,6 +710,17 @@ def _emit(st: _State, op: dict) -> None:
             def build(d, x=x, wname=wname, bname=bname, out=out, M=M, N=N, K=K, act=op["act"], res=res):
                 return [_gemm_tc_launch(d, x, wname, bname, out, M, N, K, act, res)]
             P.add_step("gemm_tc", [x, wname] + ([bname] if bname else []) + ([res] if res else []), [out], build,
+                       flops)
+        elif st.profile == "tf32" and N % 32 == 0 and K % 4 == 0 and op.get("alpha", 1.0) == 1.0 \
+                and P.tensors[x].dtype == L.F32:
+            wname = st.weight("linear", np.ascontiguousarray(w, np.float32), L.F32)
+            P.add_tensor(out, (M, N), L.F32)
+
+            def build(d, x=x, wname=wname, bname=bname, out=out, M=M, N=N, K=K, act=op["act"], res=res):
+                ln = _gemm_tc_launch(d, x, wname, bname, out, M, N, K, act, res)
+                ln.kid = L.K_GEMM_TF32
+                return [ln]
+            P.add_step("gemm_tf32", [x, wname] + ([bname] if bname else []) + ([res] if res else []), [out], build,
                        flops)
         else:
             if P.tensors[x].dtype != L.F32:

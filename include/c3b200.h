@@ -91,7 +91,8 @@ enum {
   C3B_K_GEMM_W4A16 = 21, /* bf16 x FP4-weight tcgen05 GEMM (W4A16)         */
   C3B_K_DEQUANT_FP4 = 22,/* FP4 weights -> bf16 (W4A16 at large M)         */
   C3B_K_WAIT_PROBE = 23, /* failure-path probe: a bounded wait that expires */
-  C3B_K_COUNT = 24
+  C3B_K_GEMM_TF32 = 24,  /* fp32 x fp32 tcgen05 GEMM as tf32 (kind::tf32) */
+  C3B_K_COUNT = 25
 };
 
 /* --- C3B_K_EW: out = program(in0..in5) with NumPy broadcasting.
@@ -280,6 +281,12 @@ typedef struct {
  * rows per call (M in the thousands) expanding once and running C3B_K_GEMM_TC
  * costs less than re-expanding the weights for every 128-row tile.
  * Parameters: c3b_quant_params, with M = N rows.  No reference counterpart. */
+
+/* --- C3B_K_GEMM_TF32: C = act(A B^T + bias [+ residual]) with A [M,K] and
+ * B [N,K] f32 read by the tensor cores as tf32 (10-bit mantissa), fp32
+ * accumulation in TMEM, f32 output; c3b_gemm_tc_params, K % 4 == 0,
+ * N % 32 == 0.  The tf32 precision profile's contraction (the fp32 C3.5
+ * contractions, c35/engine.py:722-849, at tensor-core rate). */
 
 /* --- C3B_K_WAIT_PROBE: no tensors.  One thread waits on an mbarrier that is
  * never armed, through the bounded wait every tcgen05 kernel uses; when the

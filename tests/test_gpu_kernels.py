@@ -799,3 +799,33 @@ def test_flash_attention_fp16(torch_cuda, B, S, H):
     assert L.device_status() == 0
     # P is rounded to fp16 (2^-11) before P.V; the output to fp16
     assert rel(out.float().cpu().numpy(), ref) < 4e-3
+
+
+@pytest.mark.parametrize("M,N,K,act,res", [(128, 64, 64, 0, 0), (300, 128, 200, 1, 1), (1000, 256, 1024, 2, 1)])
+def test_gemm_tf32(torch_cuda, M, N, K, act, res):
+    """kind::tf32 on fp32 operands: the inputs lose their low 13 mantissa bits,
+    so the error is bounded by ~2^-10 of the dot products' magnitude."""
+    import torch
+    from hackathon_b200 import _lib as L
+    a, w, b, r = randn(M, K), randn(N, K) * 0.1, randn(N), randn(M, N)
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    g = L.GemmTcParams()
+    g.M, g.N, g.K, g.bias_mode, g.act, g.has_residual, g.block_n = M, N, K, L.BIAS_COL, act, res, 0
+    ta, tw, tb, tr = dev(torch, a), dev(torch, w), dev(torch, b), dev(torch, r)
+    ins = [L.make_tensor(ta.data_ptr(), L.F32, (M, K)), L.make_tensor(tw.data_ptr(), L.F32, (N, K)),
+           L.make_tensor(tb.data_ptr(), L.F32, (N,))]
+    if res:
+        ins.append(L.make_tensor(tr.data_ptr(), L.F32, (M, N)))
+    L.launch(L.K_GEMM_TF32, ins, [L.make_tensor(out.data_ptr(), L.F32, (M, N))], g,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + b
+    if res:
+        ref = ref + r
+    if act == 1:
+        ref = np.maximum(ref, 0)
+    elif act == 2:
+        ref = O.gelu_erf(ref.astype(np.float32))
+    err = rel(host(out), ref)
+    assert 0 < err < 2e-3  # tf32, not fp32: some error must show

@@ -301,3 +301,19 @@ def test_fp16_profile(wl, model, batch):
         assert abs_err < BF16_GATE_ABS
         assert n_real_flip == 0
     ex.native.close()
+
+
+@pytest.mark.parametrize("model,batch", [("mlp", 256), ("tx_small", 8)])
+def test_tf32_profile(wl, model, batch):
+    """tf32 profile: linear layers on tcgen05 kind::tf32 against the fp32
+    oracle; tf32 keeps 10 mantissa bits, so logits agree to ~1e-3 of their
+    scale, with no argmax flip beyond near-ties."""
+    g = wl.BUILDERS[model]()
+    feeds = wl.make_inputs(g, batch)
+    ref = run_graph(g, feeds)["logits"]
+    ex, out = _run_program(g, batch, "tf32", feeds)
+    assert "gemm_tf32" in {s.label for s in ex.prog.steps}
+    abs_err, n_flip, n_real_flip = _bf16_gate(f"{model} tf32 b{batch}", out, ref)
+    assert abs_err / np.abs(ref).max() < 5e-3
+    assert n_real_flip == 0
+    ex.native.close()
