@@ -33,6 +33,14 @@ sys.path.insert(0, ROOT)
 WORKLOADS = {
     "resnet18_bf16": ("resnet18", 4096, "bf16", "img/s", "strong", None,
                       "BASELINE configs[3]: ResNet-18 CIFAR, explicit BN folded, bf16 profile, batch 4096 sharded"),
+    "resnet18_fp16": ("resnet18", 4096, "fp16", "img/s", "strong", None,
+                      "configs[3] shapes with the fp16 profile (the reference policy's MIXED default for "
+                      "convolutions, c32/strategy.py:127-145), batch 4096 sharded"),
+    "resnet18_fp16_plan": ("resnet18", 4096, "fp16", "img/s", "strong", None,
+                           "configs[3] shapes, fp16 profile, through the reference C3.3/C3.4 path "
+                           "(tests/golden/plan_resnet18_b<N>_b200_fp16.json) replayed by C34PlanRunner"),
+    "tx_large_fp16": ("tx_large", 256, "fp16", "tok/s", "weak", 512,
+                      "configs[4] shapes with the fp16 profile, 256 seq per GPU"),
     "resnet18_fp32": ("resnet18", 256, "fp32", "img/s", "strong", None,
                       "BASELINE configs[1]: ResNet-18 CIFAR, fp32 profile, batch 256"),
     "tx_large_bf16": ("tx_large", 256, "bf16", "tok/s", "weak", 512,
@@ -225,7 +233,7 @@ def measure_plan(args, workload, ws, rank, local, with_cpu_baseline):
     key, gbatch, profile, unit, scaling, ups, note = WORKLOADS[workload]
     g = BUILDERS[key]()
     total, start, per = rows_for(scaling, gbatch, ws, rank)
-    path = os.path.join(ROOT, "tests", "golden", f"plan_{key}_b{per}_b200_bf16.json")
+    path = os.path.join(ROOT, "tests", "golden", f"plan_{key}_b{per}_b200_{profile}.json")
     if not os.path.exists(path):
         raise SystemExit(f"no committed plan for per-GPU batch {per}: {path}")
     plan = json.load(open(path))

@@ -21,7 +21,7 @@ dict ``plan_to_dict`` produces (the committed fixtures use that form).
 
 Precision.  Each ``KernelStep`` carries the ``precision_profile`` C3.2 chose
 for its node (c34/scheduler.py:173-192, c34/execution_plan.py:65).  Steps
-whose profile computes in bf16 and whose kernel is one of the fused nodes of
+whose profile computes in bf16 or fp16 (one of them per plan) and whose kernel is one of the fused nodes of
 ``c33_passes`` (or ``fused_gemm_epilogue``, when aligned) run on the tcgen05
 kernels: convolutions read and write channels-last 16-bit activations,
 linear layers 16-bit rows with an fp32 output where a residual stream or a
@@ -193,12 +193,13 @@ class C34PlanRunner:
                     cons.setdefault(nm, []).append(i)
         self._tc: Dict[int, bool] = {}
         self._wfmt: Dict[str, str] = {}
+        dts = set()
         for i, ks in enumerate(steps):
             base = _base(ks["kernel_name"])
             dt = self._dtype_of(ks)
             tc = base in _TC_BASES and dt in ("bf16", "fp16")
-            if tc and dt == "fp16":
-                raise NotImplementedError("plan replay: the fp16 profile is not built for plan steps")
+            if tc:
+                dts.add(dt)
             ins = ks["logical_inputs"]
             if tc and base == "fused_gemm_epilogue":
                 p = ks.get("operator_params") or {}
@@ -227,6 +228,10 @@ class C34PlanRunner:
                 if not stem and C % 64 != 0:
                     raise ValueError(f"conv step {ks['node_id']}: Cin {C} is not a multiple of 64")
             self._tc[i] = tc
+        if len(dts) > 1:
+            raise ValueError("plan replay: bf16 and fp16 steps in one plan")
+        # 16-bit format of the plan's tensor-core steps (bf16 or fp16 profile)
+        self.t16 = L.F16 if dts == {"fp16"} else L.BF16
         # output dtypes of the 16-bit steps and of LayerNorms feeding them
         self._out16: Dict[str, bool] = {}
 
@@ -281,9 +286,9 @@ class C34PlanRunner:
         return Desc(off, L.F32, d.shape, True)
 
     def _to_16(self, np_, s, name: str, d: Desc, nhwc: bool, label: str) -> Desc:
-        """The bf16 copy of a tensor, channels-last when ``nhwc``."""
+        """The 16-bit copy of a tensor (the plan's format), channels-last when ``nhwc``."""
         want = "nhwc" if nhwc else "plain"
-        if d.dtype == L.BF16 and d.layout == want:
+        if d.dtype == self.t16 and d.layout == want:
             return d
         src = self._to_f32(np_, s, name, d, label) if d.layout != "plain" else d
         off = self._extra_alloc(f"bf16{want}:{name}", d.numel * 2)
@@ -298,8 +303,8 @@ class C34PlanRunner:
         for k, v in enumerate(strides):
             cp.in_stride[k] = int(v)
         self._k(np_, s, Launch(L.K_COPY, [L.make_tensor(src.ptr, src.dtype, (d.numel,), True)],
-                             [L.make_tensor(off, L.BF16, oshape, True)], cp), f"{label}:to_bf16")
-        return Desc(off, L.BF16, d.shape, True, layout=want)
+                             [L.make_tensor(off, self.t16, oshape, True)], cp), f"{label}:to_16")
+        return Desc(off, self.t16, d.shape, True, layout=want)
 
     def _out_slot(self, allocs, ks, name: str, nbytes: int) -> int:
         a = allocs[ks["outputs"][name]]
@@ -308,19 +313,24 @@ class C34PlanRunner:
             raise ValueError(f"output '{name}' needs {nbytes} bytes, planned capacity is {cap}")
         return a["offset_bytes"]
 
+    def _bits16(self, x: np.ndarray) -> np.ndarray:
+        if self.t16 == L.F16:
+            return np.ascontiguousarray(x, np.float32).astype(np.float16).view(np.uint16)
+        return _bf16_bits(x)
+
     def _weight_host(self, name: str, host: np.ndarray) -> np.ndarray:
         fmt = self._wfmt.get(name)
         if fmt is None:
             return host
         w = np.asarray(host, np.float32)
         if fmt == "ohwc16":
-            return _bf16_bits(np.ascontiguousarray(w.transpose(0, 2, 3, 1)))
+            return self._bits16(np.ascontiguousarray(w.transpose(0, 2, 3, 1)))
         if fmt == "stem":
             return np.ascontiguousarray(w.reshape(w.shape[0], -1).T, np.float32)
         if fmt == "nk16":      # [K, N] (MatMul / Gemm transB=0) -> [N, K]
-            return _bf16_bits(np.ascontiguousarray(w.T))
+            return self._bits16(np.ascontiguousarray(w.T))
         if fmt == "nk16_t":    # already [N, K] (Gemm transB=1)
-            return _bf16_bits(np.ascontiguousarray(w))
+            return self._bits16(np.ascontiguousarray(w))
         raise ValueError(fmt)
 
     # ---------------------------------------------------------- tensor-core steps
@@ -347,7 +357,7 @@ class C34PlanRunner:
                 sp.n, sp.c, sp.h, sp.w, sp.ho, sp.wo, sp.kpad = N, C, H, W, Ho, Wo, 0
                 sp.g = geo
                 self._k(np_, s, Launch(L.K_STEM_CONV, [x.t(), w.t(), b.t((O,))],
-                                       [L.make_tensor(off, L.BF16, (M, O), True)], L.StemConvParams(sp, O, act)),
+                                       [L.make_tensor(off, self.t16, (M, O), True)], L.StemConvParams(sp, O, act)),
                         label + ":stem", 2.0 * M * O * C * kh * kw)
             else:
                 if kh != kw or geo.ph0 != geo.ph1 or geo.pw0 != geo.ph0 or geo.sh != geo.sw or geo.dh != 1:
@@ -361,9 +371,9 @@ class C34PlanRunner:
                 cp.n, cp.h, cp.w, cp.cin, cp.cout, cp.ho, cp.wo = N, H, W, C, O, Ho, Wo
                 cp.k, cp.stride, cp.pad = kh, geo.sh, geo.ph0
                 cp.has_residual, cp.act, cp.block_n, cp.mode = int(res is not None), act, 0, 0
-                self._k(np_, s, Launch(L.K_CONV_TC, tin, [L.make_tensor(off, L.BF16, (M, O), True)], cp), label,
+                self._k(np_, s, Launch(L.K_CONV_TC, tin, [L.make_tensor(off, self.t16, (M, O), True)], cp), label,
                         2.0 * M * O * C * kh * kw)
-            values[out] = Desc(off, L.BF16, (N, O, Ho, Wo), True, layout="nhwc")
+            values[out] = Desc(off, self.t16, (N, O, Ho, Wo), True, layout="nhwc")
             return
         if base in _LINEAR_BASES:
             x, w = ins[0], ins[1]
@@ -389,7 +399,7 @@ class C34PlanRunner:
                                      f"(sqrt 2, 1, 0.5): {vals}")
             x = self._to_16(np_, s, ks["logical_inputs"][0], Desc(x.ptr, x.dtype, (M, K), True, layout=x.layout)
                             if x.layout == "plain" else x, False, label)
-            odt = L.BF16 if self._out16.get(out) else L.F32
+            odt = self.t16 if self._out16.get(out) else L.F32
             off = self._out_slot(allocs, ks, out, M * N * L.DTYPE_SIZE[odt])
             g = L.GemmTcParams()
             g.M, g.N, g.K = M, N, K
@@ -409,9 +419,9 @@ class C34PlanRunner:
             fp = flash_params_from_node(qkv, ins[1], ins[2], ins[3], p)
             shape = (fp.batch, fp.seq, fp.heads * fp.head_dim)
             off = self._out_slot(allocs, ks, out, int(np.prod(shape)) * 2)
-            self._k(np_, s, Launch(L.K_FLASH_ATTN, [qkv.t()], [L.make_tensor(off, L.BF16, shape, True)], fp), label,
+            self._k(np_, s, Launch(L.K_FLASH_ATTN, [qkv.t()], [L.make_tensor(off, self.t16, shape, True)], fp), label,
                     4.0 * fp.batch * fp.heads * fp.seq * fp.seq * fp.head_dim * (0.5 if fp.causal else 1.0))
-            values[out] = Desc(off, L.BF16, shape, True)
+            values[out] = Desc(off, self.t16, shape, True)
             return
         raise NotImplementedError(base)
 
@@ -457,8 +467,8 @@ class C34PlanRunner:
                         raise ValueError(f"'{name}' requires {host.nbytes} bytes, planned capacity is {cap}")
                     # Model tensors are uploaded once and stay resident (executor.py:805-839).
                     np_.upload(a["offset_bytes"], host)
-                    values[name] = Desc(a["offset_bytes"], _NP_DTYPE[host.dtype], tuple(host.shape), True,
-                                        host=orig)
+                    dt = self.t16 if host.dtype == np.uint16 else _NP_DTYPE[host.dtype]
+                    values[name] = Desc(a["offset_bytes"], dt, tuple(host.shape), True, host=orig)
             elif kind == "KERNEL":
                 idx = step["ref_index"]
                 ks = plan["kernel_steps"][idx]
@@ -539,7 +549,7 @@ class C34PlanRunner:
         o16 = len(onames) == 1 and self._out16.get(onames[0]) and len(prep.launches) == 1 and \
             prep.launches[0].kid == L.K_LAYERNORM
         if o16:  # the LayerNorm feeds only tensor-core linears: write bf16 rows
-            prep.launches[0].outs[0].dtype = L.BF16
+            prep.launches[0].outs[0].dtype = self.t16
         for ln in prep.launches:
             self._k(np_, s, ln, name)
         k = 0

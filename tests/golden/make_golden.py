@@ -12,10 +12,11 @@ nothing at test time needs the reference.  What it produces:
    bias, c32/kernel_registry.py:318-453).
    The large decoder (configs[4] shapes) gets an engine golden at one
    sequence: ``--models tx_large --no-kat``.
-3. ``plan_<model>_b<N>_b200_bf16.json`` -- the same graphs through the
+3. ``plan_<model>_b<N>_b200_<bf16|fp16>.json`` -- the same graphs through the
    reference pipeline, the executor's fold rewrite, the backend's extra C3.3
    passes (``hackathon_b200.c33_passes``) and the reference scheduler with the
-   bf16 precision profile (``hackathon_b200.c34_precision``): ``--b200-plans``.
+   bf16 or fp16 precision profile (``hackathon_b200.c34_precision``):
+   ``--b200-plans``.
 2. ``plan_<model>_b<N>.json`` — the reference's C3.3 fusion + C3.4 plan
    (``GraphPassPipeline().run``, ``ExecutionScheduler(graph, N).build()``) for the
    same graph, with the Conv+BN fold rewrite of c35/executor.py:359-442 applied
@@ -49,8 +50,9 @@ PLAN_BATCH = {"mlp": 16, "resnet18": 4, "tx_small": 4}
 # Plans through the B200 C3.3 passes and the bf16 C3.2/C3.4 profile
 # (hackathon_b200.c33_passes, hackathon_b200.c34_precision): the test batches,
 # plus the headline ResNet batch and its 2/4/8-GPU shards that bench.py replays.
-B200_PLANS = [("mlp", 16), ("resnet18", 4), ("tx_small", 4), ("resnet18", 4096), ("resnet18", 2048),
-              ("resnet18", 1024), ("resnet18", 512)]
+B200_PLANS = [("mlp", 16, "bf16"), ("resnet18", 4, "bf16"), ("tx_small", 4, "bf16"), ("resnet18", 4096, "bf16"),
+              ("resnet18", 2048, "bf16"), ("resnet18", 1024, "bf16"), ("resnet18", 512, "bf16"),
+              ("resnet18", 4, "fp16"), ("tx_small", 4, "fp16"), ("resnet18", 4096, "fp16")]
 
 
 def numpy_cupy_shim() -> types.ModuleType:
@@ -222,20 +224,20 @@ def b200_plans(ref: str) -> None:
     from c33.pipeline import GraphPassPipeline
     from hackathon_b200.c33_passes import run_b200_passes
     from hackathon_b200.c34_precision import build_plan
-    for model, batch in B200_PLANS:
+    for model, batch, profile in B200_PLANS:
         graph = BUILDERS[model]()
         g = to_reference_ir(ref_ir, graph, infer_shapes(graph))
         res = GraphPassPipeline().run(g)
         assert res["Fusion"]["stats"]["validation_passed"]
         folds = fold_bn_rewrite(g)
         counts = run_b200_passes(g)["counts"]
-        plan = build_plan(g, batch, "bf16")
+        plan = build_plan(g, batch, profile)
         js = plan_to_json(plan, g, folds, graph)
         js["b200_passes"] = counts
-        with open(HERE / f"plan_{model}_b{batch}_b200_bf16.json", "w") as f:
+        with open(HERE / f"plan_{model}_b{batch}_b200_{profile}.json", "w") as f:
             json.dump(js, f, separators=(",", ":"))
         names = [k["kernel_name"] for k in js["kernel_steps"]]
-        print(model, batch, "b200 plan kernels", len(names), sorted(set(names)), counts)
+        print(model, batch, profile, "b200 plan kernels", len(names), sorted(set(names)), counts)
 
 
 def main() -> None:

@@ -195,17 +195,19 @@ class _Recorder:
         self.actions.append((label, ln))
 
 
-@pytest.mark.parametrize("model,batch,want", [
-    ("resnet18", 4, {L.K_CONV_TC: 19, L.K_STEM_CONV: 1, L.K_GAP_NHWC: 1, L.K_GEMM: 1}),
-    ("resnet18", 4096, {L.K_CONV_TC: 19, L.K_STEM_CONV: 1, L.K_GAP_NHWC: 1, L.K_GEMM: 1}),
-    ("tx_small", 4, {L.K_GEMM_TC: 17, L.K_FLASH_ATTN: 4, L.K_LAYERNORM: 9}),
+@pytest.mark.parametrize("model,batch,profile,want", [
+    ("resnet18", 4, "bf16", {L.K_CONV_TC: 19, L.K_STEM_CONV: 1, L.K_GAP_NHWC: 1, L.K_GEMM: 1}),
+    ("resnet18", 4096, "bf16", {L.K_CONV_TC: 19, L.K_STEM_CONV: 1, L.K_GAP_NHWC: 1, L.K_GEMM: 1}),
+    ("tx_small", 4, "bf16", {L.K_GEMM_TC: 17, L.K_FLASH_ATTN: 4, L.K_LAYERNORM: 9}),
+    ("resnet18", 4, "fp16", {L.K_CONV_TC: 19, L.K_STEM_CONV: 1, L.K_GAP_NHWC: 1, L.K_GEMM: 1}),
+    ("tx_small", 4, "fp16", {L.K_GEMM_TC: 17, L.K_FLASH_ATTN: 4, L.K_LAYERNORM: 9}),
 ])
-def test_b200_plans_walk_onto_tensor_core_kernels(model, batch, want):
+def test_b200_plans_walk_onto_tensor_core_kernels(model, batch, profile, want):
     from hackathon_b200.c34_plan import C34PlanRunner
     from hackathon_b200.workloads import BUILDERS, make_inputs
-    plan = json.load(open(os.path.join(HERE, "golden", f"plan_{model}_b{batch}_b200_bf16.json")))
+    plan = json.load(open(os.path.join(HERE, "golden", f"plan_{model}_b{batch}_b200_{profile}.json")))
     steps = plan["kernel_steps"]
-    assert all(k["precision_profile"]["compute_dtype"] == "bf16" for k in steps if k["kernel_name"].startswith("b200"))
+    assert all(k["precision_profile"]["compute_dtype"] == profile for k in steps if k["kernel_name"].startswith("b200"))
     g = BUILDERS[model]()
     feeds = make_inputs(g, batch)
     rec = _Recorder()
@@ -215,6 +217,9 @@ def test_b200_plans_walk_onto_tensor_core_kernels(model, batch, want):
         got[ln.kid] = got.get(ln.kid, 0) + 1
     for kid, n in want.items():
         assert got.get(kid, 0) == n, (L.KERNEL_NAMES[kid], got)
+    t16 = L.F16 if profile == "fp16" else L.BF16
+    tc_outs = [int(ln.outs[0].dtype) for _, ln in rec.actions if ln.kid in (L.K_CONV_TC, L.K_FLASH_ATTN)]
+    assert tc_outs and all(d == t16 for d in tc_outs)
     # every tensor a launch touches lies inside the arena (plan arena + conversion slots)
     for _, ln in rec.actions:
         for t in list(ln.ins) + list(ln.outs):

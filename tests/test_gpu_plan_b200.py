@@ -26,10 +26,10 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def _runner(model, batch, profile=None, use_graph=True):
+def _runner(model, batch, profile=None, use_graph=True, plan_profile="bf16"):
     from hackathon_b200.c34_plan import C34PlanRunner
     from hackathon_b200.workloads import BUILDERS
-    plan = json.load(open(os.path.join(HERE, "golden", f"plan_{model}_b{batch}_b200_bf16.json")))
+    plan = json.load(open(os.path.join(HERE, "golden", f"plan_{model}_b{batch}_b200_{plan_profile}.json")))
     gold = np.load(os.path.join(HERE, "golden", f"engine_{model}.npz"))
     g = BUILDERS[model]()
     feeds = {vi.name: gold[vi.name][:batch] for vi in g.inputs}
@@ -119,3 +119,19 @@ def test_b200_plan_headline_batch():
     ref = gold["logits"]
     assert np.abs(out[:n] - ref).max() < 0.35
     assert (out[:n].argmax(-1) == ref.argmax(-1)).all()
+
+
+@pytest.mark.parametrize("model,batch", [("resnet18", 4), ("tx_small", 4)])
+def test_b200_plan_fp16_replay(model, batch):
+    """The same passes and scheduler with the fp16 profile (the reference
+    policy's MIXED default for convolutions and GEMMs, c32/strategy.py:127-158):
+    fp16 steps on the tcgen05 kernels with fp16 operands."""
+    from hackathon_b200 import _lib as L
+    r, feeds, ref, g = _runner(model, batch, plan_profile="fp16")
+    assert r.t16 == L.F16
+    out = r.run(feeds)["logits"]
+    d = float(np.abs(out.astype(np.float64) - ref).max())
+    print(f"{model} b200 plan fp16: max abs err {d:.4e}, max |logit| {np.abs(ref).max():.3f}")
+    assert d < (0.04 if model == "resnet18" else 2e-2)
+    assert (out.argmax(-1) == ref.argmax(-1)).all()
+    r.native.close()
