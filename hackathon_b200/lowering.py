@@ -117,10 +117,10 @@ class _State:
             return np.ascontiguousarray(x, np.float32).astype(np.float16).view(np.uint16)
         return bf16_bits(x)
 
-    def weight(self, stem: str, host: np.ndarray, dtype: int) -> str:
+    def weight(self, stem: str, host: Optional[np.ndarray], dtype: int, shape=None) -> str:
         self.wcount += 1
         name = f"w{self.wcount}:{stem}"
-        self.prog.add_tensor(name, host.shape, dtype, "weight", host)
+        self.prog.add_tensor(name, host.shape if host is not None else shape, dtype, "weight", host)
         return name
 
 
@@ -671,10 +671,12 @@ def _emit(st: _State, op: dict) -> None:
                 P.add_step("gemm_w4a16", [x, wqn, wsn] + ([bname] if bname else []) + ([res] if res else []), [out],
                            build, flops)
         elif use_f8:
-            from .fp8 import quant_rows_e4m3
-            wq, ws = quant_rows_e4m3(w)
-            wqn = st.weight("linear_e4m3", wq, L.U8)
-            wsn = st.weight("linear_e4m3_scale", ws, L.F32)
+            # E4M3 bytes and row scales are computed on the GPU when the
+            # program is bound (program._quantize_weights_on_device)
+            wqn = st.weight("linear_e4m3", None, L.U8, shape=(N, K))
+            wsn = st.weight("linear_e4m3_scale", None, L.F32, shape=(N,))
+            P.tensors[wqn].quant_src = np.ascontiguousarray(w, np.float32)
+            P.tensors[wqn].quant_scale = wsn
             odt = L.F32 if (res is not None or op["out"] in [o.name for o in st.g.outputs]) else T16
             P.add_tensor(out, (M, N), odt)
             if x in st.fused_q:  # quantised by the producing LayerNorm

@@ -38,6 +38,10 @@ class TensorInfo:
     kind: str  # "input" | "weight" | "act"
     host: Optional[np.ndarray] = None  # weights: the (already converted) host values
     offset: int = -1
+    # weights quantised on the device at set-up (fp8 profile): fp32 source and
+    # the name of the row-scale tensor the quantiser also writes
+    quant_src: Optional[np.ndarray] = None
+    quant_scale: Optional[str] = None
 
     @property
     def nbytes(self) -> int:
@@ -144,6 +148,40 @@ class Program:
         return Desc(t.offset, t.dtype, t.shape, True)
 
 
+def _quantize_weights_on_device(prog: Program) -> None:
+    """Rowwise E4M3 weights (the fp8 profile) computed once on the GPU by the
+    same kernel that quantises activations (C3B_K_QUANT_E4M3: per row
+    scale = max|w| / 448, bytes = E4M3(w / scale), nearest even, saturating),
+    through a one-off native plan; the bytes and scales become the weights'
+    host values, uploaded like every other weight."""
+    todo = [t for t in prog.tensors.values() if t.quant_src is not None and t.host is None]
+    if not todo:
+        return
+    offs, top = [], 0
+    for t in todo:
+        n, k = t.shape
+        src, q, sc = top, top + _align(n * k * 4), 0
+        sc = q + _align(n * k)
+        top = sc + _align(n * 4)
+        offs.append((src, q, sc))
+    plan = NativePlan(top, n_streams=1)
+    try:
+        for t, (src, q, sc) in zip(todo, offs):
+            n, k = t.shape
+            plan.upload(src, np.ascontiguousarray(t.quant_src, np.float32))
+            plan.kernel(0, Launch(L.K_QUANT_E4M3, [L.make_tensor(src, L.F32, (n, k), True)],
+                                  [L.make_tensor(q, L.U8, (n, k), True), L.make_tensor(sc, L.F32, (n,), True)],
+                                  L.QuantParams(n, k)), "quant_weights_e4m3")
+        plan.finalize(use_graph=False)  # finalize runs the pass once
+        plan.sync()
+        for t, (src, q, sc) in zip(todo, offs):
+            n, k = t.shape
+            t.host = plan.download(q, np.empty((n, k), np.uint8))
+            prog.tensors[t.quant_scale].host = plan.download(sc, np.empty((n,), np.float32))
+    finally:
+        plan.close()
+
+
 class Executor:
     """A planned program bound to a native plan with pinned input/output slots."""
 
@@ -156,6 +194,7 @@ class Executor:
             prog.plan()
         self.prog = prog
         self.copies = copies
+        _quantize_weights_on_device(prog)
         p = NativePlan(prog.arena_bytes, n_streams=2, n_events=2)
         self.native = p
         for t in prog.tensors.values():
