@@ -69,6 +69,7 @@ struct TcArgs {
   int bres;  // 1: all weight taps resident in shared memory for the whole kernel
   // row-ring mode (tc_conv_rowring_kernel)
   int segs, seg_rows, ring, row_bytes, n_items;
+  int rring;  // sliding-window kernel: residual rows staged by TMA in this many slots (0: none)
   // fp8 GEMM (tc_gemm_kernel<1>): per-row scale of A, per-column scale of B
   const float* a_scale;
   const float* b_scale;
@@ -77,7 +78,13 @@ struct TcArgs {
   int tma_out;
   // 16-bit format of A, B and every 16-bit output / residual: 0 bf16, 1 fp16
   int h16;
+  // optional wait counters of the row-ring kernel (C3B200_CONV_PROF=1), else null
+  unsigned long long* prof;
 };
+
+// Row-ring wait-profiler slots (cycles summed over CTAs; epilogue slots over warps).
+enum { RP_PROD_TOTAL, RP_PROD_EMPTY, RP_MMA_TOTAL, RP_MMA_RFULL, RP_MMA_TEMPTY, RP_EPI_TOTAL, RP_EPI_TFULL,
+       RP_EPI_RES, RP_PAIRS, RP_COUNT };
 
 // Epilogue for 32 columns of one bf16 output row whose residual (bf16) was
 // prefetched into `rv` (4 x 16 bytes): +bias -> +residual -> act -> 64-byte store.
@@ -937,6 +944,8 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
       for (int tap = 0; tap < 9; ++tap)
         tma_load_2d(sb + (size_t)((tap % 3) * 3 + 2 - tap / 3) * b_bytes, &maps.b, &wfull[0], tap * a.cin, 0);
       uint32_t c = 0;  // rows loaded so far
+      const long long pt0 = a.prof ? clock64() : 0;
+      long long pw = 0;
       for (int u = blockIdx.x; u < a.n_items; u += gridDim.x) {
         const int seg = u % a.segs;
         const int strip = u / a.segs;
@@ -944,17 +953,25 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
         const int h0 = seg * SR;
         for (int ir = 0; ir < SR + 2; ++ir, ++c) {
           const int slot = (int)(c % NS);
+          const long long w0 = a.prof ? clock64() : 0;
           if (!mbar_wait(&rempty[slot], ((c / NS) & 1) ^ 1, abort_flag, 31)) goto producer_done;
+          if (a.prof) pw += clock64() - w0;
           mbar_arrive_tx(&rfull[slot], (uint32_t)a.row_bytes);
           tma_load_4d(sr + (size_t)slot * rb_al, &maps.a[0], &rfull[slot], 0, ib * a.img, wb * a.wt - 1,
                       h0 - 1 + ir);
         }
       }
-    producer_done:;
+    producer_done:
+      if (a.prof) {
+        atomicAdd(&a.prof[RP_PROD_TOTAL], (unsigned long long)(clock64() - pt0));
+        atomicAdd(&a.prof[RP_PROD_EMPTY], (unsigned long long)pw);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc64 = instr_desc_h(BM, 64, a.h16), idesc128 = instr_desc_h(BM, 128, a.h16);
+      const long long mt0 = a.prof ? clock64() : 0;
+      long long m_rf = 0, m_te = 0, pairs = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       uint32_t cbase = 0;
@@ -964,14 +981,17 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
         for (int pr = 0; pr < SR / 2 && ok; ++pr) {
           // input rows 2pr .. 2pr+3 of this segment; the first pair waits for
           // all four, later pairs for the two new ones
+          long long w0 = a.prof ? clock64() : 0;
           for (int ir = (pr == 0 ? 0 : 2 * pr + 2); ir <= 2 * pr + 3; ++ir) {
             const uint32_t c = cbase + ir;
             if (!mbar_wait(&rfull[c % NS], (c / NS) & 1, abort_flag, 33)) { ok = false; break; }
           }
           if (!ok) break;
           tc_fence_after();
+          if (a.prof) { const long long t = clock64(); m_rf += t - w0; w0 = t; ++pairs; }
           if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 34)) { ok = false; break; }
           tc_fence_after();
+          if (a.prof) m_te += clock64() - w0;
           const uint32_t d0 = tmem_base + (uint32_t)(acc * 2 * a.block_n);
           // One thread issues all MMAs of the pair, so their operands are
           // precomputed descriptors plus compile-time offsets (the descriptor
@@ -1010,6 +1030,12 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
         }
         cbase += SR + 2;
       }
+      if (a.prof) {
+        atomicAdd(&a.prof[RP_MMA_TOTAL], (unsigned long long)(clock64() - mt0));
+        atomicAdd(&a.prof[RP_MMA_RFULL], (unsigned long long)m_rf);
+        atomicAdd(&a.prof[RP_MMA_TEMPTY], (unsigned long long)m_te);
+        atomicAdd(&a.prof[RP_PAIRS], (unsigned long long)pairs);
+      }
     }
   } else if (!a.res) {
     // Epilogue without a residual: direct 16-byte stores from registers.
@@ -1022,6 +1048,8 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
     int acc = 0;
     uint32_t acc_phase = 0;
     bool run = true;
+    const long long et0 = a.prof ? clock64() : 0;
+    long long e_tf = 0;
     for (int u = blockIdx.x; u < a.n_items && run; u += gridDim.x) {
       const int seg = u % a.segs;
       const int strip = u / a.segs;
@@ -1033,9 +1061,11 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
       const int64_t col_base = half * cols;
       for (int pr = 0; pr < SR / 2; ++pr) {
         const int hrow = seg * SR + 2 * pr;
+        const long long w0 = a.prof ? clock64() : 0;
         const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 35);
         if (!__all_sync(0xffffffffu, ok)) { run = false; break; }
         tc_fence_after();
+        if (a.prof) e_tf += clock64() - w0;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int64_t pix = ((int64_t)img * a.ho + hrow + j) * a.wo + w;
@@ -1050,6 +1080,10 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
         if (lane == 0) mbar_arrive(&tempty[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
+    }
+    if (a.prof && lane == 0) {
+      atomicAdd(&a.prof[RP_EPI_TOTAL], (unsigned long long)(clock64() - et0));
+      atomicAdd(&a.prof[RP_EPI_TFULL], (unsigned long long)e_tf);
     }
 
   } else {
@@ -1071,6 +1105,8 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
     float bias[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) bias[i] = a.bias ? __ldg(a.bias + half * 32 + i) : 0.f;
+    const long long et0 = a.prof ? clock64() : 0;
+    long long e_tf = 0, e_rs = 0;
     for (int u = blockIdx.x; u < a.n_items && run; u += gridDim.x) {
       const int seg = u % a.segs;
       const int strip = u / a.segs;
@@ -1087,9 +1123,11 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
             tma_load_4d(tile + 2048, &maps.res, rbar, half * 32, img0, w0, hrow + 1);
           }
         }
+        long long tw = a.prof ? clock64() : 0;
         const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 35);
         if (!__all_sync(0xffffffffu, ok)) { run = false; break; }
         tc_fence_after();
+        if (a.prof) { const long long t = clock64(); e_tf += t - tw; tw = t; }
         float v[2][32];
 #pragma unroll
         for (int j = 0; j < 2; ++j)
@@ -1102,6 +1140,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
           const bool rok = mbar_wait(rbar, rphase, abort_flag, 36);
           rphase ^= 1;
           if (!__all_sync(0xffffffffu, rok)) { run = false; break; }
+          if (a.prof) e_rs += clock64() - tw;
         }
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
@@ -1132,6 +1171,305 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
       }
     }
     if (lane == 0) bulk_wait0();
+    if (a.prof && lane == 0) {
+      atomicAdd(&a.prof[RP_EPI_TOTAL], (unsigned long long)(clock64() - et0));
+      atomicAdd(&a.prof[RP_EPI_TFULL], (unsigned long long)e_tf);
+      atomicAdd(&a.prof[RP_EPI_RES], (unsigned long long)e_rs);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+  }
+}
+
+// 3x3 stride-1 convolution, Cin = Cout = 64, weights resident: sliding-window
+// variant of the row-ring kernel.  The input-row ring and work items are the
+// row ring's, but the accumulators are a ring of NB output rows in TMEM
+// (64 columns each).  Input row i of a segment feeds output rows i-2, i-1, i
+// through taps r = 2, 1, 0; with the weights stored [W(2,s), W(1,s), W(0,s)]
+// per column shift s, those three are one N=192 MMA per (s, K step) whose
+// accumulator columns are three consecutive ring blocks: 12 MMAs per output
+// row (two where the three blocks wrap around the ring, and fewer at segment
+// ends).  Every MMA accumulates; the epilogue zeroes a block after draining it
+// (and all blocks at start), which is what lets one instruction start one
+// output row while it continues two others.
+constexpr int SLIDE_NB = 8;
+constexpr int SLIDE_THREADS = 352;  // producer, MMA, 8 epilogue warps, residual producer
+
+__global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(const __grid_constant__ TmaMaps maps,
+                                                                          const TcArgs a) {
+  constexpr int NB = SLIDE_NB;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int NS = a.ring;
+  const uint32_t rb_al = (uint32_t)((a.row_bytes + 1023) & ~1023);
+  constexpr uint32_t b_bytes = 64u * BK * 2;
+  uint8_t* sr = smem;
+  uint8_t* sb = smem + (size_t)NS * rb_al;
+  const int NR = a.rring;
+  const uint32_t res_bytes = (uint32_t)(a.img * a.wt * 64 * 2);  // one output row of the strip
+  uint8_t* rs = sb + (size_t)9 * b_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rs + (size_t)NR * res_bytes);
+  uint64_t* rfull = bars;
+  uint64_t* rempty = rfull + NS;
+  uint64_t* wfull = rempty + NS;
+  uint64_t* tfull = wfull + 1;
+  uint64_t* tempty = tfull + NB;
+  uint64_t* resfull = tempty + NB;
+  uint64_t* resempty = resfull + NR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(resempty + NR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr uint32_t tmem_cols = 64u * NB;
+  const int SR = a.seg_rows;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&rfull[i], 1);
+      mbar_init(&rempty[i], 1);
+    }
+    mbar_init(&wfull[0], 1);
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);
+    }
+    for (int i = 0; i < NR; ++i) {
+      mbar_init(&resfull[i], 1);
+      mbar_init(&resempty[i], 8);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a[0])));
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)));
+    if (NR) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.res)));
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_tx(&wfull[0], 9u * b_bytes);
+      for (int tap = 0; tap < 9; ++tap)
+        tma_load_2d(sb + (size_t)((tap % 3) * 3 + 2 - tap / 3) * b_bytes, &maps.b, &wfull[0], tap * a.cin, 0);
+      uint32_t c = 0;
+      const long long pt0 = a.prof ? clock64() : 0;
+      long long pw = 0;
+      for (int u = blockIdx.x; u < a.n_items; u += gridDim.x) {
+        const int seg = u % a.segs;
+        const int strip = u / a.segs;
+        const int wb = strip % a.wblocks, ib = strip / a.wblocks;
+        const int h0 = seg * SR;
+        for (int ir = 0; ir < SR + 2; ++ir, ++c) {
+          const int slot = (int)(c % NS);
+          const long long t0 = a.prof ? clock64() : 0;
+          if (!mbar_wait(&rempty[slot], ((c / NS) & 1) ^ 1, abort_flag, 41)) goto producer_done;
+          if (a.prof) pw += clock64() - t0;
+          mbar_arrive_tx(&rfull[slot], (uint32_t)a.row_bytes);
+          tma_load_4d(sr + (size_t)slot * rb_al, &maps.a[0], &rfull[slot], 0, ib * a.img, wb * a.wt - 1,
+                      h0 - 1 + ir);
+        }
+      }
+    producer_done:
+      if (a.prof) {
+        atomicAdd(&a.prof[RP_PROD_TOTAL], (unsigned long long)(clock64() - pt0));
+        atomicAdd(&a.prof[RP_PROD_EMPTY], (unsigned long long)pw);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc64 = instr_desc_h(BM, 64, a.h16), idesc128 = instr_desc_h(BM, 128, a.h16),
+                     idesc192 = instr_desc_h(BM, 192, a.h16);
+      const long long mt0 = a.prof ? clock64() : 0;
+      long long m_rf = 0, m_te = 0, rows = 0;
+      bool ok = mbar_wait(&wfull[0], 0, abort_flag, 42);
+      tc_fence_after();
+      const uint64_t bd0 = smem_desc(smem_u32(sb));
+      const uint64_t sstep = (uint64_t)(a.img * 128) >> 4;
+      constexpr uint64_t WB = (64 * BK * 2) >> 4;  // one weight block, 16-byte units
+      uint32_t G = 0;  // output rows started so far (ring position)
+      uint32_t c = 0;  // input rows consumed so far
+      for (int u = blockIdx.x; u < a.n_items && ok; u += gridDim.x) {
+        for (int i = 0; i < SR + 2; ++i, ++c) {
+          const int slot = (int)(c % NS);
+          long long t0 = a.prof ? clock64() : 0;
+          if (!mbar_wait(&rfull[slot], (c / NS) & 1, abort_flag, 43)) { ok = false; break; }
+          if (a.prof) { const long long t = clock64(); m_rf += t - t0; t0 = t; }
+          if (i < SR) {
+            // output row i starts here: its block must have been drained and zeroed
+            const uint32_t gi = G + (uint32_t)i;
+            if (!mbar_wait(&tempty[gi % NB], (gi / NB) & 1, abort_flag, 44)) { ok = false; break; }
+            if (a.prof) { m_te += clock64() - t0; ++rows; }
+          }
+          tc_fence_after();
+          const int j0 = i >= 2 ? i - 2 : 0;
+          const int j1 = i < SR ? i : SR - 1;
+          const int cnt = j1 - j0 + 1;
+          const int b0 = (int)((G + (uint32_t)j0) % NB);
+          const int n1 = cnt < NB - b0 ? cnt : NB - b0;
+          const int n2 = cnt - n1;
+          const int r0 = i - j0;  // tap row of block j0; the next blocks take r0-1, r0-2
+          const uint64_t ad = smem_desc(smem_u32(sr + (size_t)slot * rb_al));
+          const uint64_t bd = bd0 + (uint64_t)(2 - r0) * WB;
+          const uint32_t d1 = tmem_base + (uint32_t)(b0 * 64);
+          const uint32_t id1 = n1 == 3 ? idesc192 : n1 == 2 ? idesc128 : idesc64;
+          if (n2 == 0) {
+#pragma unroll
+            for (int s = 0; s < 3; ++s)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                mma_bf16(d1, ad + (uint64_t)s * sstep + (uint64_t)(2 * k), bd + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k),
+                         id1, 1u);
+          } else {
+            const uint32_t id2 = n2 == 2 ? idesc128 : idesc64;
+            const uint64_t bd2 = bd + (uint64_t)n1 * WB;
+#pragma unroll
+            for (int s = 0; s < 3; ++s)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k) {
+                const uint64_t aa = ad + (uint64_t)s * sstep + (uint64_t)(2 * k);
+                mma_bf16(d1, aa, bd + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k), id1, 1u);
+                mma_bf16(tmem_base, aa, bd2 + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k), id2, 1u);
+              }
+          }
+          mma_commit(&rempty[slot]);
+          if (i >= 2) mma_commit(&tfull[(G + (uint32_t)(i - 2)) % NB]);
+        }
+        G += (uint32_t)SR;
+      }
+      if (a.prof) {
+        atomicAdd(&a.prof[RP_MMA_TOTAL], (unsigned long long)(clock64() - mt0));
+        atomicAdd(&a.prof[RP_MMA_RFULL], (unsigned long long)m_rf);
+        atomicAdd(&a.prof[RP_MMA_TEMPTY], (unsigned long long)m_te);
+        atomicAdd(&a.prof[RP_PAIRS], (unsigned long long)rows);
+      }
+    }
+  } else if (warp == SLIDE_THREADS / 32 - 1) {
+    // residual producer: output rows of the residual, in epilogue order, into
+    // a ring of NR slots (128-byte swizzled pixel rows of 64 channels)
+    if (lane == 0 && NR) {
+      uint32_t G = 0;
+      for (int u = blockIdx.x; u < a.n_items; u += gridDim.x) {
+        const int seg = u % a.segs;
+        const int strip = u / a.segs;
+        const int wb = strip % a.wblocks, ib = strip / a.wblocks;
+        for (int j = 0; j < SR; ++j) {
+          const uint32_t gj = G + (uint32_t)j;
+          const int slot = (int)(gj % NR);
+          if (!mbar_wait(&resempty[slot], ((gj / NR) & 1) ^ 1, abort_flag, 46)) goto res_done;
+          mbar_arrive_tx(&resfull[slot], res_bytes);
+          tma_load_4d(rs + (size_t)slot * res_bytes, &maps.res, &resfull[slot], 0, ib * a.img, wb * a.wt,
+                      seg * SR + j);
+        }
+        G += (uint32_t)SR;
+      }
+    res_done:;
+    }
+  } else {
+    // Epilogue: warp (q, half) owns TMEM lanes 32q..32q+31 (pixels) and
+    // channels 32*half..+31 of every output row.  It drains a block, zeroes
+    // it, finishes the row from registers (+bias, +residual from the staged
+    // ring, activation, 64-byte stores) and then hands the block back.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int col0 = half * 32;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)col0;
+#pragma unroll 1
+    for (int b = 0; b < NB; ++b) tmem_st32_zero(lane_base + (uint32_t)(b * 64));
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0)
+      for (int b = 0; b < NB; ++b) mbar_arrive(&tempty[b]);
+    float bias[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) bias[i] = a.bias ? __ldg(a.bias + col0 + i) : 0.f;
+    uint16_t* out = static_cast<uint16_t*>(a.out);
+    const long long et0 = a.prof ? clock64() : 0;
+    long long e_tf = 0;
+    uint32_t G = 0;
+    bool run = true;
+    for (int u = blockIdx.x; u < a.n_items && run; u += gridDim.x) {
+      const int seg = u % a.segs;
+      const int strip = u / a.segs;
+      const int wb = strip % a.wblocks, ib = strip / a.wblocks;
+      const int m = q * 32 + lane;
+      const int img = ib * a.img + (m % a.img);
+      const int w = wb * a.wt + m / a.img;
+      const bool img_ok = img < a.n_img;
+      const int64_t pix0 = ((int64_t)img * a.ho + seg * SR) * a.wo + w;  // output row 0 of the segment
+      for (int j = 0; j < SR; ++j) {
+        const uint32_t gj = G + (uint32_t)j;
+        const uint32_t blk = gj % NB;
+        const long long t0 = a.prof ? clock64() : 0;
+        const bool ok = mbar_wait(&tfull[blk], (gj / NB) & 1, abort_flag, 45);
+        if (!__all_sync(0xffffffffu, ok)) { run = false; break; }
+        tc_fence_after();
+        if (a.prof) e_tf += clock64() - t0;
+        float v[32];
+        tmem_ld32(lane_base + blk * 64, v);
+        tmem_st32_zero(lane_base + blk * 64);
+        const int64_t off = (pix0 + (int64_t)j * a.wo) * 64 + col0;
+        uint4 rv[4];
+        if (NR) {
+          const int slot = (int)(gj % NR);
+          const bool rok = mbar_wait(&resfull[slot], (gj / NR) & 1, abort_flag, 47);
+          if (!__all_sync(0xffffffffu, rok)) { run = false; break; }
+          const uint8_t* rrow = rs + (size_t)slot * res_bytes + (size_t)m * 128;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            rv[i] = *reinterpret_cast<const uint4*>(rrow + ((((half * 4 + i) ^ (m & 7))) << 4));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&resempty[slot]);
+        }
+        if (img_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] += bias[i];
+          if (NR) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float rr[8];
+              unpack8h(rv[i], rr, a.h16);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[8 * i + e] += rr[e];
+            }
+          }
+          act_inplace<32>(v, a.act, true);
+          uint4* op = reinterpret_cast<uint4*>(out + off);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) op[i] = pack8h(v + 8 * i, a.h16);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[blk]);
+      }
+      G += (uint32_t)SR;
+    }
+    tmem_st_wait();  // (an aborted row may leave its zeroing store unwaited)
+    if (a.prof && lane == 0) {
+      atomicAdd(&a.prof[RP_EPI_TOTAL], (unsigned long long)(clock64() - et0));
+      atomicAdd(&a.prof[RP_EPI_TFULL], (unsigned long long)e_tf);
+    }
   }
 
   tc_fence_before();
@@ -1714,6 +2052,79 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
     a.wblocks = p.wo / wt;
     a.ho = p.ho;
     a.n_img = p.n;
+    // sliding-window accumulators (tc_conv_rowslide_kernel) unless
+    // C3B200_CONV_RING=1 selects the paired row-ring kernel (A/B timing)
+    static const bool use_ring = [] {
+      const char* e = getenv("C3B200_CONV_RING");
+      return e && e[0] == '1';
+    }();
+    if (p.mode == 0 && !use_ring && p.cin == 64 && p.cout == 64 && a.block_n == 64 && 32 % a.img == 0) {
+      const int strips = ((p.n + a.img - 1) / a.img) * a.wblocks;
+      int segs = 1;
+      while (strips * segs < 4 * sm_count() && p.ho % (segs * 2) == 0 && segs * 2 <= p.ho / 2) segs *= 2;
+      a.segs = segs;
+      a.seg_rows = p.ho / segs;
+      a.n_items = strips * segs;
+      a.row_bytes = 64 * a.img * (wt + 2) * 2;
+      const size_t rb = ((size_t)a.row_bytes + 1023) & ~(size_t)1023;
+      const size_t wbytes = (size_t)9 * 64 * tc::BK * 2;
+      // residual rows (one strip row = IMG x WT pixels x 64 channels) in 3 slots
+      a.rring = p.has_residual ? 3 : 0;
+      const size_t res_bytes = (size_t)a.img * wt * 64 * 2;
+      const size_t fixed = 1024 + wbytes + a.rring * (res_bytes + 16) + (1 + 2 * tc::SLIDE_NB) * 8 + 16;
+      int ring = (int)((227 * 1024 - fixed) / (rb + 16));
+      if (ring > 8) ring = 8;
+      if (ring >= 4) {
+        a.ring = ring;
+        uint64_t dims[4] = {C, (uint64_t)p.n, (uint64_t)p.w, (uint64_t)p.h};
+        uint64_t str[3] = {(uint64_t)p.h * p.w * C * 2, C * 2, (uint64_t)p.w * C * 2};
+        uint32_t box[4] = {64, (uint32_t)a.img, (uint32_t)(wt + 2), 1};
+        if ((rc = encode(&maps.a[0], x, 4, dims, str, box))) return rc;
+        if (a.rring) {
+          uint64_t rdims[4] = {64, (uint64_t)p.n, (uint64_t)p.wo, (uint64_t)p.ho};
+          uint64_t rstr[3] = {(uint64_t)p.ho * p.wo * 64 * 2, 64 * 2, (uint64_t)p.wo * 64 * 2};
+          uint32_t rbox[4] = {64, (uint32_t)a.img, (uint32_t)wt, 1};
+          if ((rc = encode(&maps.res, const_cast<void*>(a.res), 4, rdims, rstr, rbox))) return rc;
+        }
+        const size_t smem = fixed + ring * (rb + 16);
+        static bool attr_slide = false;
+        if (!attr_slide) {
+          C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_conv_rowslide_kernel,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+          attr_slide = true;
+        }
+        static unsigned long long* prof_buf = [] {
+          const char* e = getenv("C3B200_CONV_PROF");
+          unsigned long long* b = nullptr;
+          if (e && e[0] == '1' && cudaMalloc(&b, tc::RP_COUNT * sizeof(unsigned long long)) != cudaSuccess) b = nullptr;
+          return b;
+        }();
+        if (prof_buf) {
+          C3B_CHECK_CUDA(cudaMemsetAsync(prof_buf, 0, tc::RP_COUNT * sizeof(unsigned long long), s));
+          a.prof = prof_buf;
+        }
+        int grid = a.n_items < sm_count() ? a.n_items : sm_count();
+        if ((rc = launch_pdl(tc::tc_conv_rowslide_kernel, grid, tc::SLIDE_THREADS, smem, s, maps, a))) return rc;
+        C3B_CHECK_CUDA(cudaGetLastError());
+        if (prof_buf) {
+          unsigned long long h[tc::RP_COUNT];
+          C3B_CHECK_CUDA(cudaStreamSynchronize(s));
+          C3B_CHECK_CUDA(cudaMemcpy(h, prof_buf, sizeof(h), cudaMemcpyDeviceToHost));
+          const double rows = h[tc::RP_PAIRS] ? (double)h[tc::RP_PAIRS] : 1.0;
+          fprintf(stderr,
+                  "[rowslide prof] res=%d per CTA: prod %.0f (empty-wait %.0f) | mma %.0f (rfull %.0f tempty %.0f) | "
+                  "per epilogue warp: %.0f (tfull %.0f) | per output row: mma %.0f rfull %.0f tempty %.0f "
+                  "epi-tfull %.0f | rows/CTA %.1f ring %d\n",
+                  a.res != nullptr, (double)h[tc::RP_PROD_TOTAL] / grid, (double)h[tc::RP_PROD_EMPTY] / grid,
+                  (double)h[tc::RP_MMA_TOTAL] / grid, (double)h[tc::RP_MMA_RFULL] / grid,
+                  (double)h[tc::RP_MMA_TEMPTY] / grid, (double)h[tc::RP_EPI_TOTAL] / (8.0 * grid),
+                  (double)h[tc::RP_EPI_TFULL] / (8.0 * grid), (double)h[tc::RP_MMA_TOTAL] / rows,
+                  (double)h[tc::RP_MMA_RFULL] / rows, (double)h[tc::RP_MMA_TEMPTY] / rows,
+                  (double)h[tc::RP_EPI_TFULL] / (8.0 * rows), rows / grid, ring);
+        }
+        return C3B_OK;
+      }
+    }
     if ((p.mode == 0) && p.cin == 64 && p.cout == 64 && a.block_n == 64) {
       // row ring: strips of IMG images x WT columns, segments of seg_rows rows
       const int strips = ((p.n + a.img - 1) / a.img) * a.wblocks;
@@ -1751,9 +2162,39 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
             attr_ring = true;
           }
+          // Wait profiler (C3B200_CONV_PROF=1, measurement runs only): cycles
+          // summed over CTAs, printed after a synchronous launch.
+          static unsigned long long* prof_buf = [] {
+            const char* e = getenv("C3B200_CONV_PROF");
+            unsigned long long* b = nullptr;
+            if (e && e[0] == '1' && cudaMalloc(&b, tc::RP_COUNT * sizeof(unsigned long long)) != cudaSuccess)
+              b = nullptr;
+            return b;
+          }();
+          if (prof_buf) {
+            C3B_CHECK_CUDA(cudaMemsetAsync(prof_buf, 0, tc::RP_COUNT * sizeof(unsigned long long), s));
+            a.prof = prof_buf;
+          }
           int grid = a.n_items < sm_count() ? a.n_items : sm_count();
           if ((rc = launch_pdl(tc::tc_conv_rowring_kernel, grid, tc::HALO_THREADS, smem, s, maps, a))) return rc;
           C3B_CHECK_CUDA(cudaGetLastError());
+          if (prof_buf) {
+            unsigned long long h[tc::RP_COUNT];
+            C3B_CHECK_CUDA(cudaStreamSynchronize(s));
+            C3B_CHECK_CUDA(cudaMemcpy(h, prof_buf, sizeof(h), cudaMemcpyDeviceToHost));
+            const double pairs = h[tc::RP_PAIRS] ? (double)h[tc::RP_PAIRS] : 1.0;
+            fprintf(stderr,
+                    "[rowring prof] res=%d per CTA: prod %.0f (empty-wait %.0f) | mma %.0f (rfull %.0f tempty %.0f) | "
+                    "per epilogue warp: %.0f (tfull %.0f res %.0f) | per pair: mma %.0f rfull %.0f tempty %.0f "
+                    "epi-tfull %.0f | pairs/CTA %.1f\n",
+                    a.res != nullptr, (double)h[tc::RP_PROD_TOTAL] / grid, (double)h[tc::RP_PROD_EMPTY] / grid,
+                    (double)h[tc::RP_MMA_TOTAL] / grid, (double)h[tc::RP_MMA_RFULL] / grid,
+                    (double)h[tc::RP_MMA_TEMPTY] / grid, (double)h[tc::RP_EPI_TOTAL] / (8.0 * grid),
+                    (double)h[tc::RP_EPI_TFULL] / (8.0 * grid), (double)h[tc::RP_EPI_RES] / (8.0 * grid),
+                    (double)h[tc::RP_MMA_TOTAL] / pairs, (double)h[tc::RP_MMA_RFULL] / pairs,
+                    (double)h[tc::RP_MMA_TEMPTY] / pairs, (double)h[tc::RP_EPI_TFULL] / (8.0 * pairs),
+                    pairs / grid);
+          }
           return C3B_OK;
         }
       }
