@@ -70,6 +70,7 @@ struct TcArgs {
   // row-ring mode (tc_conv_rowring_kernel)
   int segs, seg_rows, ring, row_bytes, n_items;
   int rring;  // sliding-window kernel: residual rows staged by TMA in this many slots (0: none)
+  int cg;     // tc_gemm_kernel: 1 single CTAs, 2 CTA pairs (M = 256 tiles)
   // fp8 GEMM (tc_gemm_kernel<1>): per-row scale of A, per-column scale of B
   const float* a_scale;
   const float* b_scale;
@@ -265,9 +266,16 @@ __device__ __forceinline__ void finish16(const TcArgs& a, int64_t off, int64_t c
 // in every mode.
 constexpr int W4_GROUP = 16;  // K elements per FP4 scale
 
-template <int MODE>
+// CG = 2: CTA pairs (clusters of two) share each M=256 tile: every CTA loads
+// its own 128 A rows and half of the tile's B columns, CTA 0 issues
+// tcgen05.mma.cta_group::2 for both, and each CTA drains its own 128 rows.
+// Per SM that halves the B bytes staged and read per MMA.  bf16/fp16 only.
+template <int MODE, int CG = 1>
 __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
   constexpr bool F8 = MODE == 1, W4 = MODE == 2, TF = MODE == 3;
+  static_assert(CG == 1 || MODE == 0, "CTA pairs: bf16/fp16 operands only");
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int cid = (int)blockIdx.x / CG, ncl = (int)gridDim.x / CG;
   constexpr int KEL = F8 ? 128 : TF ? 32 : BK;  // elements per K block (one 128-byte row)
   constexpr int EPIW = W4 ? 8 : 16;   // epilogue warps
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -275,7 +283,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stages = a.stages;
   const uint32_t a_bytes = BM * BK * 2;
-  const uint32_t b_bytes = (uint32_t)a.block_n * BK * 2;
+  const uint32_t b_bytes = (uint32_t)(a.block_n / CG) * BK * 2;  // this CTA's share of B
   const uint32_t raw_bytes = W4 ? (uint32_t)a.block_n * (BK / 2) : 0u;                 // packed FP4
   const uint32_t scl_bytes = W4 ? (uint32_t)a.block_n * (BK / W4_GROUP) * 4u : 0u;     // fp32 scales
   uint8_t* sa = smem;
@@ -306,7 +314,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], EPIW);
+      mbar_init(&tempty[i], EPIW * CG);  // CTA pairs: both CTAs' epilogues release CTA 0's accumulator
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -317,12 +325,20 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)));
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(tmem_cols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (CG == 2) {
+      // one warp of each CTA of the pair allocates collectively
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(tmem_cols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(tmem_cols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (CG == 2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Programmatic dependent launch: the prologue above (barriers, TMEM, tensor
@@ -335,9 +351,9 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+      for (int t = cid; t < a.n_tiles; t += ncl) {
         const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
-        const int m0 = mb * BM, n0 = nb * a.block_n;
+        const int m0 = (mb * CG + (int)rank) * BM, n0 = nb * a.block_n + (int)rank * (a.block_n / CG);
         int img0 = 0, oh0 = 0;
         if (a.conv) {
           img0 = m0 / a.pix;
@@ -352,6 +368,29 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
             tma_load_2d(dA, &maps.a[0], &full[stage], kb * BK, m0);
             tma_load_2d(sraw + (size_t)stage * raw_bytes, &maps.a[1], &full[stage], kb * (BK / 2), n0);
             tma_load_3d(sscl + (size_t)stage * scl_bytes, &maps.a[2], &full[stage], 0, n0, kb);
+          } else if (CG == 2) {
+            // both CTAs' bytes are counted on CTA 0's barrier; only CTA 0 arrives
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            if (rank == 0) mbar_arrive_tx(&full[stage], 2 * (a_bytes + b_bytes));
+            if (!a.conv) {
+              tma_load_2d_pair(dA, &maps.a[0], fb, kb * KEL, m0);
+            } else {
+              const int tap = kb / a.cblocks, cb = kb % a.cblocks;
+              const int r = tap / a.ksz, s = tap % a.ksz;
+              int map = 0, ro, so;
+              if (a.stride == 1) {
+                ro = r - a.pad;
+                so = s - a.pad;
+              } else {
+                const int dr = r - a.pad, ds = s - a.pad;
+                const int pr = dr & 1, ps = ds & 1;
+                ro = (dr - pr) / 2;
+                so = (ds - ps) / 2;
+                map = pr * 2 + ps;
+              }
+              tma_load_4d_pair(dA, &maps.a[map], fb, cb * BK, so, oh0 + ro, img0);
+            }
+            tma_load_2d_pair(dB, &maps.b, fb, kb * KEL, n0);
           } else if (!a.conv) {
             mbar_arrive_tx(&full[stage], a_bytes + b_bytes);
             tma_load_2d(dA, &maps.a[0], &full[stage], kb * KEL, m0);
@@ -380,18 +419,21 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     producer_done:;
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc =
-          F8 ? instr_desc_e4m3(BM, a.block_n) : TF ? instr_desc_tf32(BM, a.block_n) : instr_desc_h(BM, a.block_n, a.h16);
+    // ---------------- MMA issuer (CTA pairs: CTA 0 only)
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = F8   ? instr_desc_e4m3(BM, a.block_n)
+                             : TF ? instr_desc_tf32(BM, a.block_n)
+                                  : instr_desc_h(BM * CG, a.block_n, a.h16);
       // stage descriptors = base descriptor + offset in 16-byte units
       const uint64_t ad0 = smem_desc(smem_u32(sa)), bd0 = smem_desc(smem_u32(sb));
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 12)) break;
+      for (int t = cid; t < a.n_tiles; t += ncl) {
+        if (!(CG == 2 ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, abort_flag, 12)
+                      : mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 12)))
+          break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * a.block_n);
         bool ok = true;
@@ -402,18 +444,26 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
           const uint64_t bd = bd0 + (uint64_t)stage * (b_bytes >> 4);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // four 32-byte K steps per 128-byte row
-            if (F8)
+            if (CG == 2)
+              mma_bf16_pair(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else if (F8)
               mma_e4m3(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
             else if (TF)
               mma_tf32(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
             else
               mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
-          mma_commit(&empty[stage]);
+          if (CG == 2)
+            mma_commit_pair(&empty[stage]);
+          else
+            mma_commit(&empty[stage]);
           if (++stage == stages) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        mma_commit(&tfull[acc]);
+        if (CG == 2)
+          mma_commit_pair(&tfull[acc]);
+        else
+          mma_commit(&tfull[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
@@ -483,10 +533,10 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     uint32_t acc_phase = 0;
     uint8_t* my_stg = stg + (size_t)(warp - 2) * 2048;
     uint32_t n_st = 0;  // TMA stores this warp has issued
-    for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+    for (int t = cid; t < a.n_tiles; t += ncl) {
       const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
-      const int64_t row = (int64_t)mb * BM + q * 32 + lane;
-      const int64_t row0 = (int64_t)mb * BM + q * 32;  // first row of this warp's lanes
+      const int64_t row0 = ((int64_t)mb * CG + rank) * BM + q * 32;  // first row of this warp's lanes
+      const int64_t row = row0 + lane;
       const int64_t col_base = (int64_t)nb * a.block_n + part * cols;
       const bool row_ok = row < a.M && col_base < a.N;
       const float rs = (F8 && row_ok) ? __ldg(a.a_scale + row) : 1.0f;
@@ -533,7 +583,12 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if (CG == 2)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        else
+          mbar_arrive(&tempty[acc]);
+      }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
     if (a.tma_out && lane == 0) bulk_wait0();
@@ -545,9 +600,15 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     // Give copies still in flight time to land before shared memory is released.
     for (int i = 0; i < 1000; ++i) __nanosleep(1000);
   }
+  // CTA pairs: neither CTA leaves (releasing its shared memory and TMEM) while
+  // the pair's MMAs or the peer's remote arrivals may still reach it
+  if (CG == 2) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+    if (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
   }
 }
 
@@ -1721,10 +1782,10 @@ static int enable_tma_out(tc::TmaMaps& maps, tc::TcArgs& a) {
   return C3B_OK;
 }
 
-template <int MODE>
+template <int MODE, int CG = 1>
 static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s) {
   // one 128-byte K row per operand row; MODE 2 adds the packed FP4 tile and its scales
-  size_t stage_bytes = (size_t)tc::BM * 128 + (size_t)a.block_n * 128;
+  size_t stage_bytes = (size_t)tc::BM * 128 + (size_t)(a.block_n / CG) * 128;
   if (MODE == 2) stage_bytes += (size_t)a.block_n * (tc::BK / 2) + (size_t)a.block_n * (tc::BK / tc::W4_GROUP) * 4;
   const size_t out_tiles = a.tma_out ? (size_t)(MODE == 2 ? 8 : 16) * 2048 + 1024 : 0;  // + alignment
   // with output tiles the stage ring takes what the opt-in maximum leaves, so
@@ -1737,18 +1798,69 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
   const size_t smem = 1024 + stages * stage_bytes + out_tiles + (3 * stages + 4) * 8 + 16;
   static bool attr_set = false;
   if (!attr_set) {
-    C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<MODE, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         227 * 1024));
     attr_set = true;
   }
+  if (CG == 2) {
+    // persistent pairs: as many clusters as can be resident at once
+    static int max_clusters = 0;
+    if (!max_clusters) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)sm_count());
+      cfg.blockDim = dim3((unsigned)tc::HALO16_THREADS);
+      cfg.dynamicSmemBytes = 227 * 1024;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, tc::tc_gemm_kernel<MODE, CG>, &cfg) != cudaSuccess || n < 1) {
+        (void)cudaGetLastError();
+        n = sm_count() / 2;
+      }
+      max_clusters = n;
+    }
+    const int clusters = a.n_tiles < max_clusters ? a.n_tiles : max_clusters;
+    if (clusters < 1) return C3B_OK;
+    if (int rc = launch_pdl_cluster(tc::tc_gemm_kernel<MODE, CG>, 2 * clusters, 2, tc::HALO16_THREADS, smem, s, maps,
+                                    a))
+      return rc;
+    C3B_CHECK_CUDA(cudaGetLastError());
+    return C3B_OK;
+  }
   int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
   if (grid < 1) return C3B_OK;
-  if (int rc = launch_pdl(tc::tc_gemm_kernel<MODE>, grid, tc::HALO16_THREADS, smem, s, maps, a)) return rc;
+  if (int rc = launch_pdl(tc::tc_gemm_kernel<MODE, CG>, grid, tc::HALO16_THREADS, smem, s, maps, a)) return rc;
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }
 
+// CTA pairs for bf16/fp16 GEMMs and convolutions through tc_gemm_kernel with
+// 256-column tiles: B is re-encoded with half-width boxes (each CTA of a pair
+// loads its half) and tiles are counted in 256 rows.  C3B200_GEMM_PAIR=0 keeps
+// single-CTA tiles (A/B timing).
+static int use_pairs(tc::TmaMaps& maps, tc::TcArgs& a, const void* b, uint64_t K, uint64_t N) {
+  static const bool on = [] {
+    const char* e = getenv("C3B200_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  a.cg = 1;
+  if (!on || a.block_n != 256 || a.M < 2 * tc::BM) return C3B_OK;
+  uint64_t dims[2] = {K, N};
+  uint64_t str[1] = {K * 2};
+  uint32_t box[2] = {tc::BK, (uint32_t)a.block_n / 2};
+  if (int rc = encode(&maps.b, const_cast<void*>(b), 2, dims, str, box)) return rc;
+  a.cg = 2;
+  a.n_tiles = (int)((a.M + 2 * tc::BM - 1) / (2 * tc::BM)) * a.n_tiles_n;
+  return C3B_OK;
+}
+
 static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s, int mode = 0) {
+  if (mode == 0 && a.cg == 2) return launch_tc_mode<0, 2>(maps, a, s);
   if (mode == 3) return launch_tc_mode<3>(maps, a, s);
   if (mode == 1) return launch_tc_mode<1>(maps, a, s);
   if (mode == 2) return launch_tc_mode<2>(maps, a, s);
@@ -1843,6 +1955,7 @@ int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
     uint32_t box[2] = {tc::BK, (uint32_t)a.block_n};
     if ((rc = encode(&maps.b, in[1].ptr, 2, dims, str, box))) return rc;
   }
+  if ((rc = use_pairs(maps, a, in[1].ptr, (uint64_t)p.K, (uint64_t)p.N))) return rc;
   if ((rc = enable_tma_out(maps, a))) return rc;
   return launch_tc(maps, a, s);
 }
@@ -2258,6 +2371,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
         if ((rc = encode(&maps.a[pr * 2 + ps], base, 4, dims, str, box))) return rc;
       }
   }
+  if ((rc = use_pairs(maps, a, in[1].ptr, (uint64_t)K, (uint64_t)p.cout))) return rc;
   if ((rc = enable_tma_out(maps, a))) return rc;
   return launch_tc(maps, a, s);
 }

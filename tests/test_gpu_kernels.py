@@ -731,6 +731,48 @@ def test_gemm_tc_fp16(torch_cuda, M, N, K, act, res, odt):
     assert rel(host(out), ref) < (2e-5 if odt == "f32" else 1e-3)
 
 
+@pytest.mark.parametrize("M,N,K,odt,res,act", [(384, 256, 64, "bf16", 0, 0), (2176, 768, 1024, "bf16", 1, 2),
+                                              (1000, 512, 256, "f32", 1, 1), (256, 256, 4096, "bf16", 0, 1),
+                                              (640, 256, 192, "f16", 1, 0)])
+def test_gemm_tc_pairs(torch_cuda, M, N, K, odt, res, act):
+    """256-column tiles run on CTA pairs (tcgen05.mma.cta_group::2, M = 256 per
+    pair): odd 128-row tile counts leave the second CTA of the last pair past
+    M, ragged M clips inside a CTA, every output / residual format."""
+    import torch
+    from hackathon_b200 import _lib as L
+    f16 = odt == "f16"
+    rnd = _round_f16 if f16 else round_bf16
+    conv = _f16 if f16 else _bf16
+    code = {"bf16": L.BF16, "f16": L.F16, "f32": L.F32}[odt]
+    ocode = L.F16 if f16 else L.BF16
+    a, w, b = rnd(randn(M, K)), rnd(randn(N, K) * 0.1), randn(N)
+    r = rnd(randn(M, N))
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[odt]
+    out = torch.empty((M, N), dtype=tdt, device="cuda")
+    g = L.GemmTcParams()
+    g.M, g.N, g.K, g.bias_mode, g.act, g.has_residual, g.block_n = M, N, K, L.BIAS_COL, act, res, 0
+    ta, tw, tb = conv(torch, a), conv(torch, w), dev(torch, b)
+    tr = dev(torch, r) if odt == "f32" else conv(torch, r)
+    ins = [L.make_tensor(ta.data_ptr(), ocode, (M, K)), L.make_tensor(tw.data_ptr(), ocode, (N, K)),
+           L.make_tensor(tb.data_ptr(), L.F32, (N,))]
+    if res:
+        ins.append(L.make_tensor(tr.data_ptr(), L.F32 if odt == "f32" else ocode, (M, N)))
+    L.launch(L.K_GEMM_TC, ins, [L.make_tensor(out.data_ptr(), code, (M, N))], g,
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + b
+    if res:
+        ref = ref + r
+    if act == 1:
+        ref = np.maximum(ref, 0)
+    elif act == 2:
+        ref = O.gelu_erf(ref.astype(np.float32))
+    got = out.float().cpu().numpy()
+    # fp32 output: accumulation order only; 16-bit output: half an ulp of the format
+    assert rel(got, ref) < {"f32": 2e-5, "f16": 1e-3, "bf16": 8e-3}[odt]
+
+
 def test_gemm_tc_rejects_mixed_16bit_operands(torch_cuda):
     import torch
     from hackathon_b200 import _lib as L
