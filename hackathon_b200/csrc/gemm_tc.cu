@@ -201,7 +201,11 @@ __device__ __forceinline__ void load_res16(const TcArgs& a, int64_t off, uint4* 
 // 16 columns of one output row: (x row scale x column scale) -> +bias ->
 // +residual -> act -> store (bf16 or f32).
 // finish16's arithmetic without the store: (x scales) -> +bias -> +residual -> act.
-__device__ __forceinline__ void epi16(const TcArgs& a, int64_t col0, float* v, const uint4* r, float rs) {
+// With `rtile`, the f32 residual is read as it is added from this lane's row of
+// a 64-byte-swizzled shared-memory tile (16 f32 per row), so it never needs
+// registers of its own.
+__device__ __forceinline__ void epi16(const TcArgs& a, int64_t col0, float* v, const uint4* r, float rs,
+                                      const uint8_t* rtile = nullptr, int lane = 0) {
   // pairwise (packed fp32) arithmetic: v2[i] holds columns 2i, 2i+1
   float2* v2 = reinterpret_cast<float2*>(v);
   if (a.b_scale) {
@@ -223,7 +227,14 @@ __device__ __forceinline__ void epi16(const TcArgs& a, int64_t col0, float* v, c
       v2[2 * i + 1] = __fadd2_rn(v2[2 * i + 1], make_float2(b.z, b.w));
     }
   }
-  if (r) {
+  if (rtile) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 q = *reinterpret_cast<const float4*>(rtile + swz64(lane, i));
+      v2[2 * i] = __fadd2_rn(v2[2 * i], make_float2(q.x, q.y));
+      v2[2 * i + 1] = __fadd2_rn(v2[2 * i + 1], make_float2(q.z, q.w));
+    }
+  } else if (r) {
     if (a.dt_res != C3B_F32) {
       const uint32_t* rb = reinterpret_cast<const uint32_t*>(r);
 #pragma unroll
@@ -290,16 +301,19 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   uint8_t* sb = smem + (size_t)stages * a_bytes;
   uint8_t* sraw = sb + (size_t)stages * b_bytes;
   uint8_t* sscl = sraw + (size_t)stages * raw_bytes;
-  // per-warp output tiles (2 x 1 KB per epilogue warp, 1024-byte aligned)
+  // per-warp output tiles (2 per epilogue warp: 1 KB for 16-bit output, 2 KB
+  // for f32 output; 1024-byte aligned)
+  const uint32_t tile_bytes = a.tma_out == 2 ? 2048u : 1024u;
   uint8_t* stg = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(sscl + (size_t)stages * scl_bytes) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stg + (a.tma_out ? (size_t)EPIW * 2048 : 0));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stg + (a.tma_out ? (size_t)EPIW * 2 * tile_bytes : 0));
   uint64_t* full = bars;
   uint64_t* empty = bars + stages;
   uint64_t* bready = bars + 2 * stages;  // MODE 2: B stage expanded
   uint64_t* tfull = bars + 3 * stages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rbar = tempty + 2;  // f32 TMA epilogue: residual tile landed (2 per epilogue warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * EPIW);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -316,6 +330,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], EPIW * CG);  // CTA pairs: both CTAs' epilogues release CTA 0's accumulator
     }
+    for (int i = 0; i < 2 * EPIW; ++i) mbar_init(&rbar[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -531,8 +546,22 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     const int cols = a.block_n / (EPIW / 4);  // columns per warp
     int acc = 0;
     uint32_t acc_phase = 0;
-    uint8_t* my_stg = stg + (size_t)(warp - 2) * 2048;
+    uint8_t* my_stg = stg + (size_t)(warp - 2) * 2 * tile_bytes;
     uint32_t n_st = 0;  // TMA stores this warp has issued
+    // f32 output through TMA (tma_out == 2): chunk g of this warp (16 columns
+    // x 32 rows, 2 KB, 64-byte swizzle) lives in tile g & 1.  Its residual
+    // arrives there by TMA, issued while chunk g-1 is finished (the first one
+    // before the accumulator wait), the result overwrites it in place and
+    // leaves by TMA store.
+    uint64_t* my_rbar = rbar + 2 * (warp - 2);
+    const bool f32_tma = a.tma_out == 2;
+    const bool res_tma = f32_tma && a.res != nullptr;
+    uint32_t g = 0;
+    if (res_tma && lane == 0 && cid < a.n_tiles) {
+      const int mb = cid / a.n_tiles_n, nb = cid % a.n_tiles_n;
+      mbar_arrive_tx(&my_rbar[0], 2048);
+      tma_load_2d(my_stg, &maps.res, &my_rbar[0], nb * a.block_n + part * cols, (mb * CG + (int)rank) * BM + q * 32);
+    }
     for (int t = cid; t < a.n_tiles; t += ncl) {
       const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
       const int64_t row0 = ((int64_t)mb * CG + rank) * BM + q * 32;  // first row of this warp's lanes
@@ -541,14 +570,60 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
       const bool row_ok = row < a.M && col_base < a.N;
       const float rs = (F8 && row_ok) ? __ldg(a.a_scale + row) : 1.0f;
       uint4 rc[4], rn[4];
-      if (a.res && row_ok) load_res16(a, row * a.N + col_base, rc);
+      if (a.res && row_ok && !f32_tma) load_res16(a, row * a.N + col_base, rc);
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 14);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.block_n + part * cols);
 #pragma unroll 1
-      for (int c0 = 0; c0 < cols; c0 += 16) {
-        const bool more = a.res && row_ok && c0 + 16 < cols && col_base + c0 + 16 < a.N;
+      for (int c0 = 0; f32_tma && c0 < cols; c0 += 16) {
+        float v[16];
+        tmem_ld16(tbase + c0, v);
+          const uint32_t slot = g & 1;
+          uint8_t* tile = my_stg + slot * 2048;
+          if (lane == 0) {
+            // the next chunk's residual into the other tile, once the store
+            // that last used it has read it
+            int nrow0 = (int)row0, ncol = (int)col_base + c0 + 16;
+            bool next = true;
+            if (c0 + 16 >= cols) {
+              const int t2 = t + ncl;
+              next = t2 < a.n_tiles;
+              if (next) {
+                const int mb2 = t2 / a.n_tiles_n, nb2 = t2 - mb2 * a.n_tiles_n;
+                nrow0 = (mb2 * CG + (int)rank) * BM + q * 32;
+                ncol = nb2 * a.block_n + part * cols;
+              }
+            }
+            bulk_wait_read0();
+            if (res_tma && next) {
+              mbar_arrive_tx(&my_rbar[slot ^ 1], 2048);
+              tma_load_2d(my_stg + (slot ^ 1) * 2048, &maps.res, &my_rbar[slot ^ 1], ncol, nrow0);
+            }
+          }
+          if (res_tma) {
+            const bool rok = mbar_wait(&my_rbar[slot], (g >> 1) & 1, abort_flag, 16);
+            if (!__all_sync(0xffffffffu, rok)) break;
+          }
+          __syncwarp();
+          // (chunks past N hold padding: no bias or scale reads there; each
+          // lane reads and then overwrites only its own row of the tile)
+          if (col_base + c0 < a.N) epi16(a, col_base + c0, v, nullptr, rs, res_tma ? tile : nullptr, lane);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<float4*>(tile + swz64(lane, i)) =
+                make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0 && row0 < a.M && col_base + c0 < a.N) {
+            tma_store_2d(&maps.out, tile, (int)(col_base + c0), (int)row0);
+            bulk_commit();
+          }
+          ++g;
+      }
+#pragma unroll 1
+      for (int c0 = 0; !f32_tma && c0 < cols; c0 += 16) {
+        const bool more = a.res && !f32_tma && row_ok && c0 + 16 < cols && col_base + c0 + 16 < a.N;
         if (more) load_res16(a, row * a.N + col_base + c0 + 16, rn);
         float v[16];
         tmem_ld16(tbase + c0, v);
@@ -1772,7 +1847,25 @@ static int enable_tma_out(tc::TmaMaps& maps, tc::TcArgs& a) {
     return !(e && e[0] == '0');
   }();
   a.tma_out = 0;
-  if (!on || a.dt_out == C3B_F32 || a.N % 16) return C3B_OK;
+  if (!on || a.N % 16) return C3B_OK;
+  if (a.dt_out == C3B_F32) {
+    // f32 output (and f32 residual) through 2 KB tiles: 16 columns x 32 rows, 64-byte swizzle
+    static const bool f32_on = [] {
+      const char* e = getenv("C3B200_GEMM_TMA_OUT32");
+      return !(e && e[0] == '0');
+    }();
+    if (!f32_on || (a.res && a.dt_res != C3B_F32)) return C3B_OK;
+    uint64_t dims[2] = {(uint64_t)a.N, (uint64_t)a.M};
+    uint64_t str[1] = {(uint64_t)a.N * 4};
+    uint32_t box[2] = {16, 32};
+    int rc = encode(&maps.out, a.out, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+    if (rc) return rc;
+    if (a.res && (rc = encode(&maps.res, const_cast<void*>(a.res), 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B,
+                              CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return rc;
+    a.tma_out = 2;
+    return C3B_OK;
+  }
   uint64_t dims[2] = {(uint64_t)a.N, (uint64_t)a.M};
   uint64_t str[1] = {(uint64_t)a.N * 2};
   uint32_t box[2] = {16, 32};
@@ -1787,7 +1880,8 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
   // one 128-byte K row per operand row; MODE 2 adds the packed FP4 tile and its scales
   size_t stage_bytes = (size_t)tc::BM * 128 + (size_t)(a.block_n / CG) * 128;
   if (MODE == 2) stage_bytes += (size_t)a.block_n * (tc::BK / 2) + (size_t)a.block_n * (tc::BK / tc::W4_GROUP) * 4;
-  const size_t out_tiles = a.tma_out ? (size_t)(MODE == 2 ? 8 : 16) * 2048 + 1024 : 0;  // + alignment
+  const size_t out_tiles =
+      a.tma_out ? (size_t)(MODE == 2 ? 8 : 16) * (a.tma_out == 2 ? 4096 : 2048) + 1024 : 0;  // + alignment
   // with output tiles the stage ring takes what the opt-in maximum leaves, so
   // long-K convolutions keep their pipeline depth
   const size_t budget = a.tma_out ? 227 * 1024 - 2048 - out_tiles : 200 * 1024;
@@ -1795,7 +1889,7 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(C3B_E_INVALID, "tc gemm: tile does not fit in shared memory");
   a.stages = stages;
-  const size_t smem = 1024 + stages * stage_bytes + out_tiles + (3 * stages + 4) * 8 + 16;
+  const size_t smem = 1024 + stages * stage_bytes + out_tiles + (3 * stages + 4 + 32) * 8 + 16;
   static bool attr_set = false;
   if (!attr_set) {
     C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<MODE, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1840,7 +1934,7 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
 }
 
 // CTA pairs for bf16/fp16 GEMMs and convolutions through tc_gemm_kernel with
-// 256-column tiles: B is re-encoded with half-width boxes (each CTA of a pair
+// 256-column tiles (128-column pairs measured no faster): B is re-encoded with half-width boxes (each CTA of a pair
 // loads its half) and tiles are counted in 256 rows.  C3B200_GEMM_PAIR=0 keeps
 // single-CTA tiles (A/B timing).
 static int use_pairs(tc::TmaMaps& maps, tc::TcArgs& a, const void* b, uint64_t K, uint64_t N) {
@@ -1849,7 +1943,13 @@ static int use_pairs(tc::TmaMaps& maps, tc::TcArgs& a, const void* b, uint64_t K
     return !(e && e[0] == '0');
   }();
   a.cg = 1;
-  if (!on || a.block_n != 256 || a.M < 2 * tc::BM) return C3B_OK;
+  static const int min_n = [] {
+    const char* e = getenv("C3B200_GEMM_PAIR_MIN_N");
+    return e ? atoi(e) : 256;
+  }();
+  // (short K: the pair's cross-CTA handshakes cost more than the halved B
+  // traffic saves; ResNet 1x1 shortcuts with K = 128/256 measured slower)
+  if (!on || a.block_n < min_n || a.M < 2 * tc::BM || a.k_blocks < 8) return C3B_OK;
   uint64_t dims[2] = {K, N};
   uint64_t str[1] = {K * 2};
   uint32_t box[2] = {tc::BK, (uint32_t)a.block_n / 2};

@@ -303,7 +303,8 @@ def test_gemm_tc(torch_cuda, M, N, K, act, res):
                                                        (9, 32, 64, 64, 3, 1, 1), (3, 8, 64, 128, 3, 1, 1),
                                                        (5, 4, 128, 64, 3, 1, 0), (33, 16, 128, 128, 3, 1, 0),
                                                        (17, 32, 64, 64, 3, 1, 1), (40, 16, 64, 64, 3, 1, 0),
-                                                       (16, 32, 64, 64, 3, 1, 1)])
+                                                       (16, 32, 64, 64, 3, 1, 1), (8, 16, 64, 128, 3, 2, 1),
+                                                       (12, 16, 64, 128, 1, 2, 0)])
 def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res, mode):
     """mode 0: fastest eligible variant (row ring / halo); 1: one TMA window per tap; 2/3: halo tiles."""
     import torch
@@ -733,9 +734,10 @@ def test_gemm_tc_fp16(torch_cuda, M, N, K, act, res, odt):
 
 @pytest.mark.parametrize("M,N,K,odt,res,act", [(384, 256, 64, "bf16", 0, 0), (2176, 768, 1024, "bf16", 1, 2),
                                               (1000, 512, 256, "f32", 1, 1), (256, 256, 4096, "bf16", 0, 1),
-                                              (640, 256, 192, "f16", 1, 0)])
+                                              (640, 256, 192, "f16", 1, 0), (768, 128, 320, "bf16", 1, 0),
+                                              (1280, 384, 128, "f32", 0, 1)])
 def test_gemm_tc_pairs(torch_cuda, M, N, K, odt, res, act):
-    """256-column tiles run on CTA pairs (tcgen05.mma.cta_group::2, M = 256 per
+    """128- and 256-column tiles run on CTA pairs (tcgen05.mma.cta_group::2, M = 256 per
     pair): odd 128-row tile counts leave the second CTA of the last pair past
     M, ragged M clips inside a CTA, every output / residual format."""
     import torch
