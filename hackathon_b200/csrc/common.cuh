@@ -98,35 +98,51 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 // uses) with the fast reciprocal and exponential — two SFU operations and a
 // handful of FMAs per element instead of the full-precision erff, whose cost
 // made the FFN1 epilogue slower than its MMAs.  The result is rounded to bf16.
+// Written without a sign select: x Phi(x) = 0.5 x + |x| (0.5 - q) with
+// q = Phi(-|x|) = 0.5 erfc(|x| / sqrt 2), and erfc(z) = t P(t) exp(-z^2),
+// t = 1 / (1 + p z), from Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7).  The
+// polynomial coefficients below are A&S's, multiplied by -0.5 (so the
+// polynomial yields -q / exp(-z^2)), and p is divided by sqrt 2 (so t takes |x|);
+// exp(-x^2 / 2) is one ex2.approx of -x^2 log2(e) / 2, 1/d one rcp.approx.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float gelu_as_fast(float x) {
-  const float z = fabsf(x) * 0.70710678118654752f;
-  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
-  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f),
-                                      -0.284496736f), 0.254829592f);
-  const float e = 1.0f - poly * __expf(-z * z);  // erf(|x| / sqrt 2)
-  const float erf_v = x < 0.f ? -e : e;
-  return 0.5f * x * (1.0f + erf_v);
+  const float ax = fabsf(x);
+  const float t = rcp_approx(fmaf(0.23164188826636040f, ax, 1.0f));
+  float p = fmaf(t, -0.5307027145f, 0.7265760135f);
+  p = fmaf(t, p, -0.7107068705f);
+  p = fmaf(t, p, 0.142248368f);
+  p = fmaf(t, p, -0.127414796f);
+  p *= t;                                                  // -q / exp(-x^2/2)
+  const float e = ex2_approx(x * x * -0.72134752044448170f);  // exp(-x^2 / 2)
+  return fmaf(ax, fmaf(p, e, 0.5f), 0.5f * x);
 }
 
-// Two-wide GELU for bf16 outputs: the same A&S 7.1.26 evaluation as
-// gelu_as_fast with the multiply-adds issued as Blackwell's packed fp32 pairs
-// (__ffma2_rn / __fmul2_rn), which halves the FMA-pipe instructions of the
-// epilogues that run it on every output element.
+// Two-wide GELU for 16-bit outputs: the same evaluation with the multiply-adds
+// issued as Blackwell's packed fp32 pairs (__ffma2_rn / __fmul2_rn), which
+// halves the FMA-pipe instructions of the epilogues that run it on every
+// output element.
 __device__ __forceinline__ float2 gelu2_as_fast(float2 x) {
-  const float2 z = make_float2(fabsf(x.x) * 0.70710678118654752f, fabsf(x.y) * 0.70710678118654752f);
-  const float2 d = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), z, make_float2(1.0f, 1.0f));
-  const float2 t = make_float2(__fdividef(1.0f, d.x), __fdividef(1.0f, d.y));
-  float2 p = __ffma2_rn(t, make_float2(1.061405429f, 1.061405429f), make_float2(-1.453152027f, -1.453152027f));
-  p = __ffma2_rn(t, p, make_float2(1.421413741f, 1.421413741f));
-  p = __ffma2_rn(t, p, make_float2(-0.284496736f, -0.284496736f));
-  p = __ffma2_rn(t, p, make_float2(0.254829592f, 0.254829592f));
+  const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 d = __ffma2_rn(make_float2(0.23164188826636040f, 0.23164188826636040f), ax, make_float2(1.0f, 1.0f));
+  const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  float2 p = __ffma2_rn(t, make_float2(-0.5307027145f, -0.5307027145f), make_float2(0.7265760135f, 0.7265760135f));
+  p = __ffma2_rn(t, p, make_float2(-0.7107068705f, -0.7107068705f));
+  p = __ffma2_rn(t, p, make_float2(0.142248368f, 0.142248368f));
+  p = __ffma2_rn(t, p, make_float2(-0.127414796f, -0.127414796f));
   p = __fmul2_rn(t, p);
-  const float2 zz = __fmul2_rn(z, z);
-  const float2 ne = make_float2(-__expf(-zz.x), -__expf(-zz.y));
-  const float2 e = __ffma2_rn(p, ne, make_float2(1.0f, 1.0f));  // erf(|x| / sqrt 2)
-  const float2 er = make_float2(x.x < 0.f ? -e.x : e.x, x.y < 0.f ? -e.y : e.y);
-  const float2 hx = __fmul2_rn(x, make_float2(0.5f, 0.5f));
-  return __ffma2_rn(hx, er, hx);  // 0.5 x (1 + erf)
+  const float2 w = __fmul2_rn(__fmul2_rn(x, x), make_float2(-0.72134752044448170f, -0.72134752044448170f));
+  const float2 e = make_float2(ex2_approx(w.x), ex2_approx(w.y));
+  const float2 r = __ffma2_rn(p, e, make_float2(0.5f, 0.5f));  // 0.5 - q
+  return __ffma2_rn(ax, r, __fmul2_rn(x, make_float2(0.5f, 0.5f)));
 }
 
 // Activation over a register array, chosen once per call (a warp-uniform

@@ -28,7 +28,9 @@ mantissa, fp32 accumulation), convolutions and attention still fp32 SIMT;
 ``kind::f16`` with fp16 operands, fp16 activations, the same fp32
 accumulation, residual stream and logits); ``bf16`` runs contractions on tcgen05 with bf16 operands and
 fp32 accumulation, NHWC bf16 activations for convolutions, an fp32 residual
-stream and fp32 LayerNorm statistics for transformers, fp32 logits; ``fp8``
+stream and fp32 LayerNorm statistics for transformers, fp32 logits (the
+classifier head of ``bf16`` / ``fp16`` runs on ``kind::tf32`` from an f32
+LayerNorm output, as the ResNet classifier stays fp32); ``fp8``
 is ``bf16`` with the linear layers the reference's precision policy marks fp8
 (aligned GEMMs with K, N >= 64: c32/strategy.py:147-157) run as rowwise-scaled
 E4M3 GEMMs — a quantisation step for the activation rows, E4M3 weights with
@@ -449,6 +451,37 @@ def _ln_feeds_f8_linear(st: _State, op: dict, cols: int) -> bool:
     return len(users) == 1 and users[0]["kind"] == "linear" and users[0]["x"] == out and _f8_linear(st, users[0], cols)
 
 
+def _is_output(st: _State, name: str) -> bool:
+    return any(o.name == name for o in st.g.outputs)
+
+
+def _ln_feeds_logits(st: _State, op: dict) -> bool:
+    """True in the bf16 / fp16 profiles when every consumer of the LayerNorm
+    output (directly or through a row select) is a linear layer producing a
+    graph output: the classifier head.  That LayerNorm writes f32 and the head
+    runs on kind::tf32, like the ResNet classifier staying in fp32: rounding
+    the head's input and weights to bf16 was about a third of the Tx-large
+    logit error."""
+    if st.profile not in ("bf16", "fp16"):
+        return False
+
+    def users(name):
+        return [o for o in st.ops if name in (o.get("x"), o.get("res")) or name in (o.get("xs") or [])]
+
+    us = users(op["out"])
+    if not us or _is_output(st, op["out"]):
+        return False
+    for u in us:
+        if u["kind"] == "select" and u["x"] == op["out"]:
+            vs = users(u["out"])
+            if not vs or any(v["kind"] != "linear" or v["x"] != u["out"] or v.get("res") or not _is_output(st, v["out"])
+                             for v in vs):
+                return False
+        elif u["kind"] != "linear" or u["x"] != op["out"] or u.get("res") or not _is_output(st, u["out"]):
+            return False
+    return True
+
+
 def _emit(st: _State, op: dict) -> None:
     P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp16", "fp8", "mixed")
     T16 = st.t16
@@ -594,7 +627,7 @@ def _emit(st: _State, op: dict) -> None:
             st.layout[out] = "rows"
             st.lshape[out] = shp
             return
-        P.add_tensor(out, (rows, cols), T16 if bf else L.F32)
+        P.add_tensor(out, (rows, cols), T16 if bf and not _ln_feeds_logits(st, op) else L.F32)
 
         def build(d, x=x, sname=sname, bname=bname, out=out, lp=lp, rows=rows, cols=cols):
             ins = [d[x].t((rows, cols)), d[sname].t()] + ([d[bname].t()] if bname else [])
@@ -713,8 +746,10 @@ def _emit(st: _State, op: dict) -> None:
                 return [_gemm_tc_launch(d, x, wname, bname, out, M, N, K, act, res)]
             P.add_step("gemm_tc", [x, wname] + ([bname] if bname else []) + ([res] if res else []), [out], build,
                        flops)
-        elif st.profile == "tf32" and N % 32 == 0 and K % 4 == 0 and op.get("alpha", 1.0) == 1.0 \
-                and P.tensors[x].dtype == L.F32:
+        elif (st.profile == "tf32" or (st.profile in ("bf16", "fp16") and _is_output(st, out))) and N % 32 == 0 \
+                and K % 4 == 0 and op.get("alpha", 1.0) == 1.0 and P.tensors[x].dtype == L.F32:
+            # the tf32 profile's linear layers, and the bf16 / fp16 profiles'
+            # classifier head (its input stays f32, see _ln_feeds_logits)
             wname = st.weight("linear", np.ascontiguousarray(w, np.float32), L.F32)
             P.add_tensor(out, (M, N), L.F32)
 

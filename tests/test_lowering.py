@@ -51,7 +51,8 @@ def _check_arena(prog):
     ("resnet18", 64, "fp32", {L.K_CONV: 20, L.K_REDUCE: 1, L.K_GEMM: 1}),
     ("resnet18", 64, "bf16", {L.K_STEM_CONV: 1, L.K_CONV_TC: 19, L.K_GAP_NHWC: 1, L.K_GEMM: 1}),
     ("tx_small", 8, "fp32", {L.K_EMBED: 1, L.K_LAYERNORM: 9, L.K_GEMM: 17, L.K_FLASH_ATTN: 4, L.K_COPY: 1}),
-    ("tx_small", 8, "bf16", {L.K_EMBED: 1, L.K_LAYERNORM: 9, L.K_GEMM_TC: 17, L.K_FLASH_ATTN: 4, L.K_COPY: 1}),
+    ("tx_small", 8, "bf16", {L.K_EMBED: 1, L.K_LAYERNORM: 9, L.K_GEMM_TC: 16, L.K_GEMM_TF32: 1, L.K_FLASH_ATTN: 4,
+                             L.K_COPY: 1}),
 ])
 def test_lowering_fuses_to_expected_kernels(model, batch, profile, kinds):
     g = BUILDERS[model]()
