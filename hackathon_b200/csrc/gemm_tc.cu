@@ -1632,23 +1632,43 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
 constexpr int STEM_THREADS = 416;  // 8 gather warps, 4 epilogue warps, 1 MMA warp
 constexpr int STEM_STAGES = 4;
 
-__global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_constant__ TmaMaps maps,
-                                                                  const float* __restrict__ x,
-                                                                  const float* __restrict__ wt,
-                                                                  const float* __restrict__ bias, c3b_stem_params g,
-                                                                  int act, int64_t M, int n_tiles, int h16) {
+// IMG = true (3x3, stride 1, pad 1, W = 32, C <= 3, C*H*W*4 <= 12 KB): work is
+// whole images.  Warp 17 TMA-loads each image (NCHW f32, 12 KB) into a ring of
+// STEM_IMGS shared-memory slots, and the gather warps build the patch tiles of
+// its H*W/128 tiles from shared memory (no global loads on the gather path);
+// HBM then sees one read of the input and one write of the output.
+constexpr int STEM_IMGS = 3;
+constexpr int STEM_IMG_BYTES = 12288;
+
+// IMG: warps 0-7 gather, 8-15 epilogue (two per TMEM lane quarter, 32
+// channels each), 16 MMA, 17 image loads; otherwise warps 0-7 gather, 8-11
+// epilogue (64 channels each), 12 MMA.
+constexpr int STEM_IMG_THREADS = 576;
+
+template <bool IMG>
+__global__ void __launch_bounds__(IMG ? STEM_IMG_THREADS : STEM_THREADS, 1)
+    tc_stem_kernel(const __grid_constant__ TmaMaps maps, const float* __restrict__ x, const float* __restrict__ wt,
+                   const float* __restrict__ bias, c3b_stem_params g, int act, int64_t M, int n_tiles, int h16,
+                   unsigned long long* prof) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;                                   // STEM_STAGES x 16 KB patch tiles
   uint8_t* sbw = sa + STEM_STAGES * 16384;              // weights [64][64] bf16, 8 KB
-  uint8_t* so = sbw + 8192;                             // 4 epilogue warps x 4 KB output tiles
-  int4* ktab = reinterpret_cast<int4*>(so + 4 * 4096);  // per K index: input offset, row step, col step, valid
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ktab + 32);
+  constexpr int EPI = IMG ? 8 : 4;                      // epilogue warps
+  constexpr int NACC = IMG ? 4 : 2;                     // TMEM accumulators (64 columns each)
+  constexpr int NG = IMG ? 2 : 1;                       // epilogue groups taking alternate tiles
+  constexpr int MMA_WARP = IMG ? 16 : 12;
+  uint8_t* so = sbw + 8192;                             // EPI epilogue warps x 4 KB output tiles
+  float* simg = reinterpret_cast<float*>(so + EPI * 4096);  // IMG: STEM_IMGS image slots (1024-byte aligned)
+  int4* ktab = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(simg) + (IMG ? STEM_IMGS * STEM_IMG_BYTES : 0));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ktab + 32);  // ktab: per K index input offset, row / col step, valid
   uint64_t* afull = bars;
   uint64_t* aempty = afull + STEM_STAGES;
   uint64_t* tfull = aempty + STEM_STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tempty = tfull + NACC;
+  uint64_t* ifull = tempty + NACC;     // IMG: image slot loaded
+  uint64_t* iempty = ifull + STEM_IMGS;  // IMG: image slot gathered (4 arrivals per tile)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(iempty + STEM_IMGS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = g.c * g.g.kh * g.g.kw;
@@ -1676,17 +1696,24 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
       mbar_init(&afull[i], 4);
       mbar_init(&aempty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NACC; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], EPI / NG);
+    }
+    if (IMG) {
+      const int tpi = g.ho * g.wo / 128;
+      for (int i = 0; i < STEM_IMGS; ++i) {
+        mbar_init(&ifull[i], 1);
+        mbar_init(&iempty[i], 4 * tpi);
+      }
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fence_proxy_async();  // the weight rows are read by the MMA (async proxy)
-  if (warp == 12) {
+  if (warp == MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(128));
+                 "r"(NACC * 64));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -1698,6 +1725,14 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
   // activation read and every global write comes after it has completed.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int HW = g.ho * g.wo;
+  long long pc[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // wait profiler (prof != null), per thread
+  // IMG: the CTA's i-th tile is tile i % tpi of its (i / tpi)-th image
+  const int tpi = HW / 128;
+  auto tile_of = [&](int i) -> int {
+    if (!IMG) return blockIdx.x + i * gridDim.x;
+    const int u = blockIdx.x + (i / tpi) * gridDim.x;
+    return u < g.n ? u * tpi + i % tpi : n_tiles;
+  };
 
   if (warp < 8) {
     // ---------------- patch gather: two groups of 4 warps take alternate
@@ -1705,16 +1740,42 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
     const int grp = warp >> 2;
     const int r = (warp & 3) * 32 + lane;
     for (int i = grp;; i += 2) {
-      const int t = blockIdx.x + i * gridDim.x;
+      const int t = tile_of(i);
       if (t >= n_tiles) break;
       const int stage = i % STEM_STAGES;
       const uint32_t phase = (uint32_t)(i / STEM_STAGES) & 1u;
+      long long pt0 = prof ? clock64() : 0;
       if (!mbar_wait(&aempty[stage], phase ^ 1, abort_flag, 51)) break;
+      if (prof) { const long long t1 = clock64(); pc[0] += t1 - pt0; pt0 = t1; }
       const int64_t m = (int64_t)t * 128 + r;
       float v[32];
 #pragma unroll
       for (int k = 0; k < 32; ++k) v[k] = 0.f;
-      if (m < M) {
+      if (IMG) {
+        const int j = i / tpi, slot = j % STEM_IMGS;
+        if (!mbar_wait(&ifull[slot], (uint32_t)(j / STEM_IMGS) & 1u, abort_flag, 55)) break;
+        if (prof) { const long long t1 = clock64(); pc[1] += t1 - pt0; pt0 = t1; }
+        const int oh = (i % tpi) * 4 + (r >> 5), ow = r & 31;
+        const float* sp = simg + slot * (STEM_IMG_BYTES / 4) + (oh - 1) * 32 + ow - 1;
+        bool rok[3], cok[3];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          rok[q] = oh - 1 + q >= 0 && oh - 1 + q < g.h;
+          cok[q] = ow - 1 + q >= 0 && ow - 1 + q < 32;
+        }
+        const int hw = g.h * 32;
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+          if (c < g.c) {
+#pragma unroll
+            for (int rr = 0; rr < 3; ++rr)
+#pragma unroll
+              for (int q = 0; q < 3; ++q)
+                if (rok[rr] && cok[q]) v[c * 9 + rr * 3 + q] = sp[c * hw + rr * 32 + q];
+          }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&iempty[slot]);
+      } else if (m < M) {
         const int img = (int)(m / HW), rem = (int)(m % HW);
         const int oh = rem / g.wo, ow = rem % g.wo;
         const int ih0 = oh * g.g.sh - g.g.ph0, iw0 = ow * g.g.sw - g.g.pw0;
@@ -1754,35 +1815,96 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[stage]);
+      if (prof) pc[2] += clock64() - pt0;
     }
-  } else if (warp < 12) {
-    // ---------------- epilogue: TMEM lane quarter q = warp % 4
+  } else if (warp < 8 + EPI) {
+    // ---------------- epilogue: TMEM lane quarter q = warp % 4, all 64
+    // channels of its 32 pixels.  IMG: two groups of 4 warps take alternate
+    // tiles (two tiles drain at once, four accumulators), each in two
+    // 32-channel passes with 64-byte-swizzled halves of its 4 KB tile.
     const int q = warp & 3;
-    uint8_t* tile = so + (size_t)q * 4096;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    const int grp = (warp - 8) >> 2;
+    constexpr int NC = IMG ? 32 : 64;
+    uint8_t* tile = so + (size_t)(warp - 8) * 4096;
+    for (int i = grp;; i += NG) {
+      const int acc = i % NACC;
+      const uint32_t acc_phase = (uint32_t)(i / NACC) & 1u;
+      const int t = tile_of(i);
+      if (t >= n_tiles) break;
+      long long pt0 = prof ? clock64() : 0;
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 52);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      float v[64];
+      if (prof) { const long long t1 = clock64(); pc[3] += t1 - pt0; pt0 = t1; }
+      if (IMG) {
+        if (lane == 0) bulk_wait_read0();  // the previous stores have read the tile
+        __syncwarp();
+        // four 16-channel chunks; chunk c+1's TMEM load is in flight while
+        // chunk c is finished (the wait names the registers it fills)
+        const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 64);
+        uint32_t ra[16], rb[16];
+        tmem_ld16_nowait(tb, ra);
+        tmem_wait_ld16(ra);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t* cur = (c & 1) ? rb : ra;
+          uint32_t* nxt = (c & 1) ? ra : rb;
+          if (c < 3) tmem_ld16_nowait(tb + (uint32_t)(16 * (c + 1)), nxt);
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(cur[j]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 b = __ldg(reinterpret_cast<const float4*>(bias) + c * 4 + j);
+            v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+          }
+          act_inplace<16>(v, act, true);
+          // chunk c = 16-byte pieces 2(c&1), 2(c&1)+1 of half-tile c>>1
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            *reinterpret_cast<uint4*>(tile + (c >> 1) * 2048 + swz64(lane, 2 * (c & 1) + e)) = pack8h(v + e * 8, h16);
+          if (c < 3) {
+            tmem_wait_ld16(nxt);
+          } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+          }
+        }
+        if (prof) { const long long t1 = clock64(); pc[4] += t1 - pt0; pt0 = t1; }
+        fence_proxy_async();
+        __syncwarp();
+        const int64_t row0 = (int64_t)t * 128 + q * 32;
+        if (lane == 0 && row0 < M) {
+          // maps.b: the output with 32-channel, 64-byte-swizzled boxes
+          tma_store_2d(&maps.b, tile, 0, (int)row0);
+          tma_store_2d(&maps.b, tile + 2048, 32, (int)row0);
+          bulk_commit();
+        }
+        if (prof) { pc[6] += clock64() - pt0; pc[7] += 1; }
+        continue;
+      }
+      float v[NC];
       tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 64), v);
       tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 64 + 32), v + 32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < NC / 4; ++i) {
         const float4 b = __ldg(reinterpret_cast<const float4*>(bias) + i);
         v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
       }
-      act_inplace<64>(v, act, true);
+      act_inplace<NC>(v, act, true);
+      if (prof) { const long long t1 = clock64(); pc[4] += t1 - pt0; pt0 = t1; }
       if (lane == 0) bulk_wait_read0();  // the previous store has read the tile
       __syncwarp();
+      if (prof) { const long long t1 = clock64(); pc[5] += t1 - pt0; pt0 = t1; }
+      {
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(tile + lane * 128 + ((c ^ (lane & 7)) << 4)) = pack8h(v + c * 8, h16);
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(tile + lane * 128 + ((c ^ (lane & 7)) << 4)) = pack8h(v + c * 8, h16);
+      }
       fence_proxy_async();
       __syncwarp();
       const int64_t row0 = (int64_t)t * 128 + q * 32;
@@ -1790,15 +1912,30 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
         tma_store_2d(&maps.out, tile, 0, (int)row0);
         bulk_commit();
       }
+      if (prof) { pc[6] += clock64() - pt0; pc[7] += 1; }
     }
     if (lane == 0) bulk_wait0();
-  } else if (lane == 0) {
+  } else if (IMG && warp == 17) {
+    // ---------------- image loads (IMG)
+    if (lane == 0) {
+      for (int j = 0;; ++j) {
+        const int u = blockIdx.x + j * gridDim.x;
+        if (u >= g.n) break;
+        const int slot = j % STEM_IMGS;
+        if (!mbar_wait(&iempty[slot], ((uint32_t)(j / STEM_IMGS) & 1u) ^ 1u, abort_flag, 56)) break;
+        mbar_arrive_tx(&ifull[slot], (uint32_t)(g.c * g.h * 32 * 4));
+        tma_load_4d(simg + slot * (STEM_IMG_BYTES / 4), &maps.a[0], &ifull[slot], 0, 0, 0, u);
+      }
+    }
+  } else if (warp == MMA_WARP && lane == 0) {
     // ---------------- MMA issue
     const uint32_t idesc = instr_desc_h(BM, 64, h16);
     const uint64_t ad0 = smem_desc(smem_u32(sa)), bd = smem_desc(smem_u32(sbw));
-    int stage = 0, acc = 0;
-    uint32_t phase = 0, acc_phase = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int i = 0; tile_of(i) < n_tiles; ++i) {
+      const int acc = i % NACC;
+      const uint32_t acc_phase = (uint32_t)(i / NACC) & 1u;
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 53)) break;
       if (!mbar_wait(&afull[stage], phase, abort_flag, 54)) break;
       tc_fence_after();
@@ -1809,18 +1946,20 @@ __global__ void __launch_bounds__(STEM_THREADS, 1) tc_stem_kernel(const __grid_c
       mma_commit(&aempty[stage]);
       mma_commit(&tfull[acc]);
       if (++stage == STEM_STAGES) { stage = 0; phase ^= 1; }
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   }
 
+  if (prof && lane == 0)
+    for (int i = 0; i < 8; ++i)
+      if (pc[i]) atomicAdd(&prof[i], (unsigned long long)pc[i]);
   tc_fence_before();
   __syncthreads();
   if (*abort_flag) {
     for (int i = 0; i < 1000; ++i) __nanosleep(1000);
   }
-  if (warp == 12) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(128));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(NACC * 64));
   }
 }
 
@@ -2496,21 +2635,78 @@ bool launch_stem_tc(const c3b_tensor* in, const c3b_tensor& out, const c3b_stem_
   uint64_t str[1] = {128};
   uint32_t box[2] = {64, 32};
   if ((*rc = encode(&maps.out, out.ptr, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return true;
-  const size_t smem = 1024 + tc::STEM_STAGES * 16384 + 8192 + 4 * 4096 + 32 * 16 + (2 * tc::STEM_STAGES + 4) * 8 + 16;
+  // whole images through shared memory (tc_stem_kernel<true>) for the 3x3 /
+  // stride 1 / pad 1 stem of 32-pixel-wide images; C3B200_STEM=gather keeps
+  // the per-pixel global gathers (A/B timing)
+  static const bool img_off = [] {
+    const char* e = getenv("C3B200_STEM");
+    return e && std::string(e) == "gather";
+  }();
+  const bool img = !img_off && g.g.kh == 3 && g.g.kw == 3 && g.g.sh == 1 && g.g.sw == 1 && g.g.ph0 == 1 &&
+                   g.g.pw0 == 1 && g.g.dh == 1 && g.g.dw == 1 && g.w == 32 && g.wo == 32 && g.ho == g.h &&
+                   (g.h * 32) % 128 == 0 && g.c >= 1 && g.c <= 3 && g.c * g.h * 32 * 4 <= tc::STEM_IMG_BYTES &&
+                   ((uintptr_t)in[0].ptr & 15) == 0;
+  if (img) {
+    uint64_t idims[4] = {32, (uint64_t)g.h, (uint64_t)g.c, (uint64_t)g.n};
+    uint64_t istr[3] = {32 * 4, (uint64_t)g.h * 32 * 4, (uint64_t)g.c * g.h * 32 * 4};
+    uint32_t ibox[4] = {32, (uint32_t)g.h, (uint32_t)g.c, 1};
+    if ((*rc = encode(&maps.a[0], in[0].ptr, 4, idims, istr, ibox, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return true;
+    uint32_t hbox[2] = {32, 32};  // 32 channels x 32 pixels per TMA store
+    if ((*rc = encode(&maps.b, out.ptr, 2, dims, str, hbox, CU_TENSOR_MAP_SWIZZLE_64B))) return true;
+  }
+  const size_t smem = 1024 + tc::STEM_STAGES * 16384 + 8192 + (img ? 8 : 4) * 4096 + (img ? tc::STEM_IMGS * tc::STEM_IMG_BYTES : 0) +
+                      32 * 16 + (2 * tc::STEM_STAGES + 8 + 2 * tc::STEM_IMGS) * 8 + 16;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(tc::tc_stem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-      *rc = fail(C3B_E_CUDA, std::string("stem attribute: ") + cudaGetErrorString(e));
-      return true;
+    for (auto k : {tc::tc_stem_kernel<false>, tc::tc_stem_kernel<true>}) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (e != cudaSuccess) {
+        *rc = fail(C3B_E_CUDA, std::string("stem attribute: ") + cudaGetErrorString(e));
+        return true;
+      }
     }
     attr = true;
   }
   const int n_tiles = (int)((M + 127) / 128);
+  // Wait profiler (C3B200_STEM_PROF=1, measurement runs only): cycles summed
+  // over warps, printed after a synchronous launch.
+  static unsigned long long* prof = [] {
+    const char* e = getenv("C3B200_STEM_PROF");
+    unsigned long long* b = nullptr;
+    if (e && e[0] == '1' && cudaMalloc(&b, 8 * sizeof(unsigned long long)) != cudaSuccess) b = nullptr;
+    return b;
+  }();
+  if (prof && cudaMemsetAsync(prof, 0, 8 * sizeof(unsigned long long), s) != cudaSuccess) {
+    *rc = fail(C3B_E_CUDA, "stem profiler reset");
+    return true;
+  }
+  auto report = [&]() {
+    if (!prof) return;
+    unsigned long long h[8];
+    if (cudaStreamSynchronize(s) != cudaSuccess || cudaMemcpy(h, prof, sizeof(h), cudaMemcpyDeviceToHost) != cudaSuccess)
+      return;
+    const double tiles = h[7] ? (double)h[7] / 4.0 : 1.0;  // 4 epilogue warps per tile
+    fprintf(stderr,
+            "[stem prof] img=%d per tile per warp (cycles): gather aempty %.0f ifull %.0f work %.0f | epilogue tfull "
+            "%.0f math %.0f read-wait %.0f store %.0f | tiles %.0f\n",
+            (int)img, h[0] / (tiles * 4), h[1] / (tiles * 4), h[2] / (tiles * 4), h[3] / (tiles * 4), h[4] / (tiles * 4),
+            h[5] / (tiles * 4), h[6] / (tiles * 4), tiles);
+  };
+  if (img) {
+    const int grid = g.n < sm_count() ? g.n : sm_count();
+    *rc = launch_pdl(tc::tc_stem_kernel<true>, grid, tc::STEM_IMG_THREADS, smem, s, maps, (const float*)in[0].ptr,
+                     (const float*)in[1].ptr, (const float*)in[2].ptr, g, p.act, M, n_tiles,
+                     (int)(out.dtype == C3B_F16), prof);
+    report();
+    return true;
+  }
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
-  *rc = launch_pdl(tc::tc_stem_kernel, grid, tc::STEM_THREADS, smem, s, maps, (const float*)in[0].ptr,
+  *rc = launch_pdl(tc::tc_stem_kernel<false>, grid, tc::STEM_THREADS, smem, s, maps, (const float*)in[0].ptr,
                    (const float*)in[1].ptr, (const float*)in[2].ptr, g, p.act, M, n_tiles,
-                   (int)(out.dtype == C3B_F16));
+                   (int)(out.dtype == C3B_F16), prof);
+  report();
   return true;
 }
 

@@ -386,6 +386,33 @@ def test_stem_conv_direct(torch_cuda, n, cout, act):
     assert rel(got, ref) < 8e-3
 
 
+@pytest.mark.parametrize("n,c,h", [(300, 3, 32), (7, 1, 32), (5, 2, 16), (149, 3, 32)])
+def test_stem_conv_images(torch_cuda, n, c, h):
+    """The whole-image stem (3x3 / stride 1 / pad 1, 32-pixel-wide images
+    staged in shared memory by TMA): several images per CTA through the ring
+    of image slots, fewer channels, 16-row images (4 tiles per image)."""
+    import torch
+    from hackathon_b200 import _lib as L
+    cout = 64
+    x, w, b = randn(n, c, h, 32), randn(cout, c, 3, 3) * 0.3, randn(cout)
+    ref = np.maximum(O.conv2d(x, w, b, strides=[1, 1], pads=[1, 1, 1, 1]), 0)
+    wk = np.ascontiguousarray(w.reshape(cout, -1).T)
+    tx, tw, tb = dev(torch, x), dev(torch, wk), dev(torch, b)
+    M = n * h * 32
+    out = torch.empty((M, cout), dtype=torch.bfloat16, device="cuda")
+    sp = L.StemParams()
+    sp.n, sp.c, sp.h, sp.w, sp.ho, sp.wo, sp.kpad = n, c, h, 32, h, 32, 0
+    sp.g = L.ConvGeom(3, 3, 1, 1, 1, 1, 1, 1, 1, 1)
+    L.launch(L.K_STEM_CONV, [L.make_tensor(tx.data_ptr(), L.F32, x.shape), L.make_tensor(tw.data_ptr(), L.F32, wk.shape),
+                             L.make_tensor(tb.data_ptr(), L.F32, b.shape)],
+             [L.make_tensor(out.data_ptr(), L.BF16, (M, cout))], L.StemConvParams(sp, cout, 1),
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    got = out.float().cpu().numpy().reshape(n, h, 32, cout).transpose(0, 3, 1, 2)
+    assert rel(got, ref) < 8e-3
+
+
 def test_skinny_gemm(torch_cuda):
     """N <= 32 GEMMs take the warp-per-row path."""
     t = torch_cuda
