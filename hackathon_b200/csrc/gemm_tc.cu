@@ -2411,9 +2411,22 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
       return e && e[0] == '1';
     }();
     if (p.mode == 0 && !use_ring && p.cin == 64 && p.cout == 64 && a.block_n == 64 && 32 % a.img == 0) {
+      // Segments split each strip's rows across CTAs.  A segment of R rows
+      // issues MMAs for R + 2 input rows, so the choice minimises
+      // waves x (R + 2): whole strips at large batch, shorter segments only
+      // where they fill idle SMs (at 512 images the old rule, four items per
+      // SM, made 4-row segments that cost 1.5x the MMA issue).
       const int strips = ((p.n + a.img - 1) / a.img) * a.wblocks;
       int segs = 1;
-      while (strips * segs < 4 * sm_count() && p.ho % (segs * 2) == 0 && segs * 2 <= p.ho / 2) segs *= 2;
+      long best = -1;
+      for (int sg = 1; sg <= p.ho / 2 && p.ho % sg == 0; sg *= 2) {
+        const long waves = ((long)strips * sg + sm_count() - 1) / sm_count();
+        const long cost = waves * (p.ho / sg + 2);
+        if (best < 0 || cost < best) {
+          best = cost;
+          segs = sg;
+        }
+      }
       a.segs = segs;
       a.seg_rows = p.ho / segs;
       a.n_items = strips * segs;
