@@ -1574,6 +1574,11 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             rv[i] = *reinterpret_cast<const uint4*>(rrow + ((((half * 4 + i) ^ (m & 7))) << 4));
+          // the slot's next content arrives by TMA (async proxy): these
+          // generic reads are ordered before it by a proxy fence, not by the
+          // mbarrier alone (without it a 64-byte-aligned residual showed
+          // rows read after their slot had been refilled)
+          fence_proxy_async();
           __syncwarp();
           if (lane == 0) mbar_arrive(&resempty[slot]);
         }
@@ -1773,6 +1778,7 @@ __global__ void __launch_bounds__(IMG ? STEM_IMG_THREADS : STEM_THREADS, 1)
               for (int q = 0; q < 3; ++q)
                 if (rok[rr] && cok[q]) v[c * 9 + rr * 3 + q] = sp[c * hw + rr * 32 + q];
           }
+        fence_proxy_async();  // generic reads of the slot before its next TMA refill
         __syncwarp();
         if (lane == 0) mbar_arrive(&iempty[slot]);
       } else if (m < M) {

@@ -339,6 +339,48 @@ def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res, mode):
     assert rel(got, ref) < 8e-3
 
 
+@pytest.mark.parametrize("shift", [0, 64])
+def test_conv_tc_rowslide_residual_offsets(torch_cuda, shift):
+    """Stage-1 convolution with a residual (sliding-window kernel) on operands
+    at 64-byte offsets inside one arena, as the reference C3.4 plans place
+    them: three launches agree bit for bit and with the reference conv.  The
+    residual slots are refilled by TMA after the epilogue's generic reads; a
+    missing proxy fence there showed up exactly in this configuration as rows
+    read after their slot had been refilled."""
+    import torch
+    from hackathon_b200 import _lib as L
+    n, h, c = 512, 32, 64
+    x = round_bf16(randn(n, h, h, c))
+    r = round_bf16(randn(n, h, h, c))
+    w = round_bf16(randn(c, 3, 3, c) * 0.05)
+    b = randn(c)
+    nb = n * h * h * c * 2
+    arena = torch.zeros(3 * nb + 8192, dtype=torch.uint8, device="cuda")
+    ox, orr, oo = shift, nb + 2048 + shift, 2 * nb + 4096 + shift
+    arena[ox:ox + nb].copy_(_bf16(torch, x).view(-1).view(torch.uint8))
+    arena[orr:orr + nb].copy_(_bf16(torch, r).view(-1).view(torch.uint8))
+    tw, tb = _bf16(torch, w), dev(torch, b)
+    cp = L.ConvTcParams()
+    cp.n, cp.h, cp.w, cp.cin, cp.cout, cp.ho, cp.wo, cp.k, cp.stride, cp.pad = n, h, h, c, c, h, h, 3, 1, 1
+    cp.has_residual, cp.act, cp.block_n, cp.mode = 1, 1, 0, 0
+    base = arena.data_ptr()
+    ins = [L.make_tensor(base + ox, L.BF16, (n, h, h, c)), L.make_tensor(tw.data_ptr(), L.BF16, (c, 3, 3, c)),
+           L.make_tensor(tb.data_ptr(), L.F32, (c,)), L.make_tensor(base + orr, L.BF16, (n, h, h, c))]
+    outs = []
+    for i in range(3):
+        arena[oo:oo + nb].fill_(i + 1)
+        L.launch(L.K_CONV_TC, ins, [L.make_tensor(base + oo, L.BF16, (n, h, h, c))], cp,
+                 torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        outs.append(arena[oo:oo + nb].clone())
+    assert L.device_status() == 0
+    assert all(bool((o == outs[0]).all()) for o in outs[1:])
+    got = outs[0].view(torch.bfloat16).float().cpu().numpy().reshape(n, h, h, c)[:16].transpose(0, 3, 1, 2)
+    ref = np.maximum(O.conv2d(x[:16].transpose(0, 3, 1, 2), w.transpose(0, 3, 1, 2), b, strides=[1, 1],
+                              pads=[1, 1, 1, 1]) + r[:16].transpose(0, 3, 1, 2), 0)
+    assert rel(got, ref) < 8e-3
+
+
 @pytest.mark.parametrize("dt", ["f32", "bf16"])
 @pytest.mark.parametrize("B,S,H", [(2, 128, 4), (1, 200, 2), (3, 64, 1), (2, 512, 3), (1, 384, 16)])
 def test_flash_attention(torch_cuda, dt, B, S, H):
