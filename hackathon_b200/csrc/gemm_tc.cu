@@ -2094,7 +2094,15 @@ static int use_pairs(tc::TmaMaps& maps, tc::TcArgs& a, const void* b, uint64_t K
   }();
   // (short K: the pair's cross-CTA handshakes cost more than the halved B
   // traffic saves; ResNet 1x1 shortcuts with K = 128/256 measured slower)
-  if (!on || a.block_n < min_n || a.M < 2 * tc::BM || a.k_blocks < 8) return C3B_OK;
+  // (few tiles: pairs halve the tile count, and below two waves of pairs
+  // the coarser quantisation cost more than the shared B saves; ResNet-18 at
+  // 512 images per GPU measured 689K img/s with pairs, 705K without)
+  static const int min_tiles = [] {
+    const char* e = getenv("C3B200_GEMM_PAIR_MIN_TILES");
+    return e ? atoi(e) : sm_count();
+  }();
+  const int64_t pair_tiles = (a.M + 2 * tc::BM - 1) / (2 * tc::BM) * a.n_tiles_n;
+  if (!on || a.block_n < min_n || a.M < 2 * tc::BM || a.k_blocks < 8 || pair_tiles < min_tiles) return C3B_OK;
   uint64_t dims[2] = {K, N};
   uint64_t str[1] = {K * 2};
   uint32_t box[2] = {tc::BK, (uint32_t)a.block_n / 2};
