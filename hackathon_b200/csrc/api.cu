@@ -280,8 +280,8 @@ int dispatch(int kid, const c3b_tensor* in, int n_in, const c3b_tensor* out, int
     case C3B_K_GAP_NHWC: {
       c3b_gap_params p;
       if ((rc = get_params(params, len, p))) return rc;
-      C3B_REQUIRE(n_in == 1 && n_out == 1, "gap: one input, one output");
-      return launch_gap_nhwc(in[0], out[0], p, s);
+      C3B_REQUIRE(n_in >= 1 && n_in <= 3 && n_out == 1, "gap: x [, w [, b]] in, one output");
+      return launch_gap_nhwc(in, n_in, out[0], p, s);
     }
   }
   return fail(C3B_E_UNKNOWN, "unknown kernel id " + std::to_string(kid));

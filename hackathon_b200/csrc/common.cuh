@@ -221,7 +221,8 @@ int launch_embed(const c3b_tensor* in, const c3b_tensor& out, const c3b_embed_pa
 int launch_stem_im2col(const c3b_tensor& in, const c3b_tensor& out, const c3b_stem_params& p, cudaStream_t s);
 int launch_stem_conv(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_stem_conv_params& p,
                      cudaStream_t s);
-int launch_gap_nhwc(const c3b_tensor& in, const c3b_tensor& out, const c3b_gap_params& p, cudaStream_t s);
+int launch_gap_nhwc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gap_params& p,
+                    cudaStream_t s);
 int launch_wait_probe(const c3b_wait_probe_params& p, cudaStream_t s);
 int launch_gemm_tf32(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p, cudaStream_t s);
 bool flash_tc_supported(const c3b_flash_params& p);

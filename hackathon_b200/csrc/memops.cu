@@ -1045,11 +1045,82 @@ __global__ void gap_nhwc_kernel(const void* __restrict__ x, int dt, float* __res
   }
 }
 
-int launch_gap_nhwc(const c3b_tensor& in, const c3b_tensor& out, const c3b_gap_params& p, cudaStream_t s) {
+// GAP followed by the classifier, for the 16-bit convolution profiles:
+// y[n][j] = b[j] + sum_c w[j][c] * mean_p x[n][p][c].  One warp per image;
+// lane l owns the 8-channel chunks l + 32k (16-byte coalesced loads of each
+// pixel row), sums the image's pixels, then takes each classifier row from
+// shared memory and reduces across the warp.  Replaces GlobalAveragePool ->
+// Flatten -> Gemm (c35/engine.py op_global_avgpool, op_gemm) with one launch
+// and one pass over the activation.
+constexpr int GAP_FC_MAX_CHUNKS = 4;  // C <= 1024
+
+__global__ void gap_fc_kernel(const uint4* __restrict__ x, int h16, const float* __restrict__ w,
+                              const float* __restrict__ b, float* __restrict__ y, c3b_gap_params p, int classes) {
+  extern __shared__ float4 sw4[];  // classes x C f32
+  const int c = (int)p.c;
+  for (int i = threadIdx.x; i < classes * c / 4; i += blockDim.x) sw4[i] = reinterpret_cast<const float4*>(w)[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int nch = c / 256;
+  const float inv = 1.0f / (float)p.hw;
+  for (int64_t n = (int64_t)blockIdx.x * wpb + wib; n < p.n; n += (int64_t)gridDim.x * wpb) {
+    float acc[GAP_FC_MAX_CHUNKS * 8];
+#pragma unroll
+    for (int i = 0; i < GAP_FC_MAX_CHUNKS * 8; ++i) acc[i] = 0.f;
+    const uint4* img = x + n * p.hw * (c / 8);
+    for (int64_t px = 0; px < p.hw; ++px) {
+#pragma unroll
+      for (int k = 0; k < GAP_FC_MAX_CHUNKS; ++k)
+        if (k < nch) {
+          float v[8];
+          unpack8h(__ldg(img + px * (c / 8) + lane + 32 * k), v, h16);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[8 * k + e] += v[e];
+        }
+    }
+    for (int j = 0; j < classes; ++j) {
+      float sacc = 0.f;
+#pragma unroll
+      for (int k = 0; k < GAP_FC_MAX_CHUNKS; ++k)
+        if (k < nch) {
+          const float4* wr = sw4 + ((size_t)j * c + (size_t)(lane + 32 * k) * 8) / 4;
+          const float4 w0 = wr[0], w1 = wr[1];
+          sacc += acc[8 * k] * w0.x + acc[8 * k + 1] * w0.y + acc[8 * k + 2] * w0.z + acc[8 * k + 3] * w0.w +
+                  acc[8 * k + 4] * w1.x + acc[8 * k + 5] * w1.y + acc[8 * k + 6] * w1.z + acc[8 * k + 7] * w1.w;
+        }
+      sacc = warp_sum(sacc);
+      if (lane == 0) y[n * classes + j] = sacc * inv + (b ? b[j] : 0.f);
+    }
+  }
+}
+
+int launch_gap_nhwc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gap_params& p, cudaStream_t s) {
   C3B_REQUIRE(out.dtype == C3B_F32, "gap: f32 output");
-  C3B_REQUIRE(numel(in) == p.n * p.hw * p.c && numel(out) >= p.n * p.c, "gap: extents");
-  if (p.n * p.c == 0) return C3B_OK;
-  gap_nhwc_kernel<<<grid_for(p.n * p.c, 256), 256, 0, s>>>(in.ptr, in.dtype, (float*)out.ptr, p);
+  C3B_REQUIRE(numel(in[0]) == p.n * p.hw * p.c, "gap: extents");
+  if (n_in == 1) {
+    C3B_REQUIRE(numel(out) >= p.n * p.c, "gap: output extents");
+    if (p.n * p.c == 0) return C3B_OK;
+    gap_nhwc_kernel<<<grid_for(p.n * p.c, 256), 256, 0, s>>>(in[0].ptr, in[0].dtype, (float*)out.ptr, p);
+    C3B_CHECK_CUDA(cudaGetLastError());
+    return C3B_OK;
+  }
+  // with the classifier: inputs x, w [classes, C] f32, b [classes] f32 (optional)
+  C3B_REQUIRE(in[0].dtype == C3B_BF16 || in[0].dtype == C3B_F16, "gap + classifier: bf16 or fp16 input");
+  C3B_REQUIRE(p.c > 0 && p.c % 256 == 0 && p.c <= 256 * GAP_FC_MAX_CHUNKS,
+              "gap + classifier: C a multiple of 256, at most 1024");
+  C3B_REQUIRE(in[1].dtype == C3B_F32 && numel(in[1]) % p.c == 0, "gap + classifier: w [classes, C] f32");
+  const int classes = (int)(numel(in[1]) / p.c);
+  C3B_REQUIRE(classes >= 1 && classes * p.c * 4 <= 48 * 1024, "gap + classifier: classifier too large");
+  C3B_REQUIRE(n_in == 2 || (in[2].dtype == C3B_F32 && numel(in[2]) == classes), "gap + classifier: b [classes] f32");
+  C3B_REQUIRE(numel(out) >= p.n * classes, "gap + classifier: output extents");
+  C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0, "gap + classifier: alignment");
+  if (p.n == 0) return C3B_OK;
+  const int64_t blocks = (p.n + 7) / 8;
+  const int grid = (int)std::min<int64_t>(blocks, (int64_t)sm_count() * 8);
+  gap_fc_kernel<<<grid, 256, (size_t)classes * p.c * 4, s>>>((const uint4*)in[0].ptr, in[0].dtype == C3B_F16,
+                                                           (const float*)in[1].ptr,
+                                                           n_in > 2 ? (const float*)in[2].ptr : nullptr,
+                                                           (float*)out.ptr, p, classes);
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;
 }

@@ -482,7 +482,28 @@ def _ln_feeds_logits(st: _State, op: dict) -> bool:
     return True
 
 
+def _gap_classifier(st: _State, op: dict, C: int):
+    """The linear op that is the only consumer of a flattened GAP over NHWC
+    16-bit activations, when GAP and it can run as one launch: a classifier
+    without activation or residual, at most 32 classes, C a multiple of 256
+    up to 1024; else None."""
+    if not op.get("flat") or C % 256 or C > 1024 or _is_output(st, op["out"]):
+        return None
+    users = [o for o in st.ops if op["out"] in (o.get("x"), o.get("res")) or op["out"] in (o.get("xs") or [])]
+    if len(users) != 1:
+        return None
+    u = users[0]
+    if u["kind"] != "linear" or u["x"] != op["out"] or u.get("res") or u.get("act", L.ACT_NONE) != L.ACT_NONE:
+        return None
+    w = u["w"]
+    if w.ndim != 2 or w.shape[1] != C or w.shape[0] > 32 or w.shape[0] * C * 4 > 48 * 1024:
+        return None
+    return u
+
+
 def _emit(st: _State, op: dict) -> None:
+    if op.get("fused"):
+        return  # emitted inside the op it was fused into
     P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp16", "fp8", "mixed")
     T16 = st.t16
     k = op["kind"]
@@ -573,6 +594,27 @@ def _emit(st: _State, op: dict) -> None:
         x = st.t(op["x"])
         N, C, H, W = st.lshape[x]
         out = op["out"]
+        head = _gap_classifier(st, op, C) if st.layout[x] == "nhwc" else None
+        if head is not None:
+            # GAP and the classifier in one launch (C3B_K_GAP_NHWC with w, b)
+            head["fused"] = True
+            w = np.ascontiguousarray(head["w"], np.float32) * np.float32(head.get("alpha", 1.0))
+            wname = st.weight("gap_fc", w.astype(np.float32), L.F32)
+            bname = st.weight("gap_fc_bias", (head["b"] * head.get("beta", 1.0)).astype(np.float32), L.F32) \
+                if head["b"] is not None else None
+            hout = head["out"]
+            ncls = w.shape[0]
+            P.add_tensor(hout, (N, ncls), L.F32)
+            gp = L.GapParams(N, H * W, C)
+
+            def build_fc(d, x=x, wname=wname, bname=bname, hout=hout, gp=gp):
+                ins = [d[x].t(), d[wname].t()] + ([d[bname].t()] if bname else [])
+                return [Launch(L.K_GAP_NHWC, ins, [d[hout].t()], gp)]
+            P.add_step("gap_fc", [x, wname] + ([bname] if bname else []), [hout], build_fc,
+                       2.0 * N * ncls * C)
+            st.layout[hout] = "rows"
+            st.lshape[hout] = (N, ncls)
+            return
         P.add_tensor(out, (N, C), L.F32)
         if st.layout[x] == "nhwc":
             gp = L.GapParams(N, H * W, C)

@@ -295,7 +295,10 @@ typedef struct {
  * (c3b_plan_sync / c3b_device_status report C3B_E_DEVICE) without a fault. */
 typedef struct { int32_t code; } c3b_wait_probe_params;
 
-/* --- C3B_K_GAP_NHWC: x [N, HW, C] -> y [N, C] f32 */
+/* --- C3B_K_GAP_NHWC: x [N, HW, C] -> y [N, C] f32.  With two or three inputs
+ * (x bf16/fp16, w [classes, C] f32, optional b [classes] f32; C a multiple of
+ * 256 up to 1024) the classifier follows in the same launch:
+ * y [N, classes] = mean_hw(x) w^T + b (GlobalAveragePool -> Flatten -> Gemm). */
 typedef struct {
   int64_t n, hw, c;
 } c3b_gap_params;

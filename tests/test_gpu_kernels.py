@@ -455,6 +455,31 @@ def test_stem_conv_images(torch_cuda, n, c, h):
     assert rel(got, ref) < 8e-3
 
 
+@pytest.mark.parametrize("n,hw,c,classes,h16,bias", [(4096, 16, 512, 10, 0, 1), (37, 16, 256, 32, 1, 0),
+                                                     (300, 4, 1024, 7, 0, 1)])
+def test_gap_classifier(torch_cuda, n, hw, c, classes, h16, bias):
+    """C3B_K_GAP_NHWC with the classifier: mean over the pixels of NHWC 16-bit
+    rows, then y = mean w^T + b in fp32, in one launch."""
+    import torch
+    from hackathon_b200 import _lib as L
+    x = randn(n, hw, c)
+    x = _round_f16(x) if h16 else round_bf16(x)
+    w, b = randn(classes, c) * 0.05, randn(classes)
+    tx = _f16(torch, x) if h16 else _bf16(torch, x)
+    tw, tb = dev(torch, w), dev(torch, b)
+    out = torch.empty((n, classes), dtype=torch.float32, device="cuda")
+    ins = [L.make_tensor(tx.data_ptr(), L.F16 if h16 else L.BF16, (n, hw, c)),
+           L.make_tensor(tw.data_ptr(), L.F32, (classes, c))]
+    if bias:
+        ins.append(L.make_tensor(tb.data_ptr(), L.F32, (classes,)))
+    L.launch(L.K_GAP_NHWC, ins, [L.make_tensor(out.data_ptr(), L.F32, (n, classes))], L.GapParams(n, hw, c),
+             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    ref = x.astype(np.float64).mean(1) @ w.astype(np.float64).T + (b if bias else 0)
+    assert rel(host(out), ref) < 1e-5
+
+
 def test_skinny_gemm(torch_cuda):
     """N <= 32 GEMMs take the warp-per-row path."""
     t = torch_cuda

@@ -49,7 +49,7 @@ def _check_arena(prog):
 @pytest.mark.parametrize("model,batch,profile,kinds", [
     ("mlp", 256, "fp32", {L.K_GEMM: 3}),
     ("resnet18", 64, "fp32", {L.K_CONV: 20, L.K_REDUCE: 1, L.K_GEMM: 1}),
-    ("resnet18", 64, "bf16", {L.K_STEM_CONV: 1, L.K_CONV_TC: 19, L.K_GAP_NHWC: 1, L.K_GEMM: 1}),
+    ("resnet18", 64, "bf16", {L.K_STEM_CONV: 1, L.K_CONV_TC: 19, L.K_GAP_NHWC: 1}),  # GAP + classifier fused
     ("tx_small", 8, "fp32", {L.K_EMBED: 1, L.K_LAYERNORM: 9, L.K_GEMM: 17, L.K_FLASH_ATTN: 4, L.K_COPY: 1}),
     ("tx_small", 8, "bf16", {L.K_EMBED: 1, L.K_LAYERNORM: 9, L.K_GEMM_TC: 16, L.K_GEMM_TF32: 1, L.K_FLASH_ATTN: 4,
                              L.K_COPY: 1}),
