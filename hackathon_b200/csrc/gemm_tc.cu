@@ -1336,12 +1336,21 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
 // ends).  Every MMA accumulates; the epilogue zeroes a block after draining it
 // (and all blocks at start), which is what lets one instruction start one
 // output row while it continues two others.
-constexpr int SLIDE_NB = 8;
+// Accumulator ring: SLIDE_NL logical output-row blocks of 64 TMEM columns in
+// 8 physical blocks.  Physical blocks 6 and 7 alias logical blocks 0 and 1, so
+// every three-row window (logical b0..b0+2, b0 <= 5) is three consecutive
+// physical blocks and one MMA: a row of logical block 0 or 1 may accumulate
+// partly in its own block and partly in its alias, and the epilogue adds the
+// two.  (A ring of 8 split the windows that wrapped, 2 rows in 8, into two
+// MMAs each.)
+constexpr int SLIDE_NL = 6;
+constexpr int SLIDE_NPHYS = 8;
 constexpr int SLIDE_THREADS = 352;  // producer, MMA, 8 epilogue warps, residual producer
 
 __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(const __grid_constant__ TmaMaps maps,
                                                                           const TcArgs a) {
-  constexpr int NB = SLIDE_NB;
+  constexpr int NB = SLIDE_NL;        // logical blocks: barriers, ring positions
+  constexpr int NPHYS = SLIDE_NPHYS;  // physical 64-column blocks
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NS = a.ring;
@@ -1365,7 +1374,7 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr uint32_t tmem_cols = 64u * NB;
+  constexpr uint32_t tmem_cols = 64u * NPHYS;
   const int SR = a.seg_rows;
 
   if (threadIdx.x == 0) {
@@ -1460,33 +1469,19 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
           const int j0 = i >= 2 ? i - 2 : 0;
           const int j1 = i < SR ? i : SR - 1;
           const int cnt = j1 - j0 + 1;
+          // logical b0 <= 5 and at most 3 blocks: physical b0 .. b0+cnt-1 <= 7
           const int b0 = (int)((G + (uint32_t)j0) % NB);
-          const int n1 = cnt < NB - b0 ? cnt : NB - b0;
-          const int n2 = cnt - n1;
           const int r0 = i - j0;  // tap row of block j0; the next blocks take r0-1, r0-2
           const uint64_t ad = smem_desc(smem_u32(sr + (size_t)slot * rb_al));
           const uint64_t bd = bd0 + (uint64_t)(2 - r0) * WB;
           const uint32_t d1 = tmem_base + (uint32_t)(b0 * 64);
-          const uint32_t id1 = n1 == 3 ? idesc192 : n1 == 2 ? idesc128 : idesc64;
-          if (n2 == 0) {
+          const uint32_t id1 = cnt == 3 ? idesc192 : cnt == 2 ? idesc128 : idesc64;
 #pragma unroll
-            for (int s = 0; s < 3; ++s)
+          for (int s = 0; s < 3; ++s)
 #pragma unroll
-              for (int k = 0; k < BK / 16; ++k)
-                mma_bf16(d1, ad + (uint64_t)s * sstep + (uint64_t)(2 * k), bd + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k),
-                         id1, 1u);
-          } else {
-            const uint32_t id2 = n2 == 2 ? idesc128 : idesc64;
-            const uint64_t bd2 = bd + (uint64_t)n1 * WB;
-#pragma unroll
-            for (int s = 0; s < 3; ++s)
-#pragma unroll
-              for (int k = 0; k < BK / 16; ++k) {
-                const uint64_t aa = ad + (uint64_t)s * sstep + (uint64_t)(2 * k);
-                mma_bf16(d1, aa, bd + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k), id1, 1u);
-                mma_bf16(tmem_base, aa, bd2 + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k), id2, 1u);
-              }
-          }
+            for (int k = 0; k < BK / 16; ++k)
+              mma_bf16(d1, ad + (uint64_t)s * sstep + (uint64_t)(2 * k), bd + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k),
+                       id1, 1u);
           mma_commit(&rempty[slot]);
           if (i >= 2) mma_commit(&tfull[(G + (uint32_t)(i - 2)) % NB]);
         }
@@ -1530,7 +1525,7 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
     const int col0 = half * 32;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)col0;
 #pragma unroll 1
-    for (int b = 0; b < NB; ++b) tmem_st32_zero(lane_base + (uint32_t)(b * 64));
+    for (int b = 0; b < NPHYS; ++b) tmem_st32_zero(lane_base + (uint32_t)(b * 64));
     tmem_st_wait();
     tc_fence_before();
     __syncwarp();
@@ -1564,6 +1559,14 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
         float v[32];
         tmem_ld32(lane_base + blk * 64, v);
         tmem_st32_zero(lane_base + blk * 64);
+        if (blk < (uint32_t)(NPHYS - NB)) {
+          // the part of the row that accumulated in the alias block
+          float va[32];
+          tmem_ld32(lane_base + (blk + NB) * 64, va);
+          tmem_st32_zero(lane_base + (blk + NB) * 64);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] += va[i];
+        }
         const int64_t off = (pix0 + (int64_t)j * a.wo) * 64 + col0;
         uint4 rv[4];
         if (NR) {
@@ -2450,7 +2453,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
       // residual rows (one strip row = IMG x WT pixels x 64 channels) in 3 slots
       a.rring = p.has_residual ? 3 : 0;
       const size_t res_bytes = (size_t)a.img * wt * 64 * 2;
-      const size_t fixed = 1024 + wbytes + a.rring * (res_bytes + 16) + (1 + 2 * tc::SLIDE_NB) * 8 + 16;
+      const size_t fixed = 1024 + wbytes + a.rring * (res_bytes + 16) + (1 + 2 * tc::SLIDE_NL) * 8 + 16;
       int ring = (int)((227 * 1024 - fixed) / (rb + 16));
       if (ring > 8) ring = 8;
       if (ring >= 4) {
