@@ -1345,7 +1345,7 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
 // MMAs each.)
 constexpr int SLIDE_NL = 6;
 constexpr int SLIDE_NPHYS = 8;
-constexpr int SLIDE_THREADS = 352;  // producer, MMA, 8 epilogue warps, residual producer
+constexpr int SLIDE_THREADS = 320;  // producer, MMA, 8 epilogue warps
 
 __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(const __grid_constant__ TmaMaps maps,
                                                                           const TcArgs a) {
@@ -1358,18 +1358,19 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
   constexpr uint32_t b_bytes = 64u * BK * 2;
   uint8_t* sr = smem;
   uint8_t* sb = smem + (size_t)NS * rb_al;
-  const int NR = a.rring;
-  const uint32_t res_bytes = (uint32_t)(a.img * a.wt * 64 * 2);  // one output row of the strip
-  uint8_t* rs = sb + (size_t)9 * b_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(rs + (size_t)NR * res_bytes);
+  // residual layers: every epilogue warp stages its own residual box (32
+  // channels x its 32 pixels, 2 KB) by TMA in two tiles, adds it in place,
+  // writes the output over it and TMA-stores the tile
+  const bool has_res = a.rring != 0;
+  uint8_t* rs = sb + (size_t)9 * b_bytes;  // 8 epilogue warps x 2 x 2 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rs + (has_res ? 8 * 4096 : 0));
   uint64_t* rfull = bars;
   uint64_t* rempty = rfull + NS;
   uint64_t* wfull = rempty + NS;
   uint64_t* tfull = wfull + 1;
   uint64_t* tempty = tfull + NB;
-  uint64_t* resfull = tempty + NB;
-  uint64_t* resempty = resfull + NR;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(resempty + NR);
+  uint64_t* rbar = tempty + NB;  // residual tile landed: 2 per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -1387,10 +1388,7 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 8);
     }
-    for (int i = 0; i < NR; ++i) {
-      mbar_init(&resfull[i], 1);
-      mbar_init(&resempty[i], 8);
-    }
+    for (int i = 0; i < 16; ++i) mbar_init(&rbar[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1398,7 +1396,10 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
   if (warp == 0 && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a[0])));
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)));
-    if (NR) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.res)));
+    if (has_res) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.res)));
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.out)));
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -1494,27 +1495,6 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
         atomicAdd(&a.prof[RP_PAIRS], (unsigned long long)rows);
       }
     }
-  } else if (warp == SLIDE_THREADS / 32 - 1) {
-    // residual producer: output rows of the residual, in epilogue order, into
-    // a ring of NR slots (128-byte swizzled pixel rows of 64 channels)
-    if (lane == 0 && NR) {
-      uint32_t G = 0;
-      for (int u = blockIdx.x; u < a.n_items; u += gridDim.x) {
-        const int seg = u % a.segs;
-        const int strip = u / a.segs;
-        const int wb = strip % a.wblocks, ib = strip / a.wblocks;
-        for (int j = 0; j < SR; ++j) {
-          const uint32_t gj = G + (uint32_t)j;
-          const int slot = (int)(gj % NR);
-          if (!mbar_wait(&resempty[slot], ((gj / NR) & 1) ^ 1, abort_flag, 46)) goto res_done;
-          mbar_arrive_tx(&resfull[slot], res_bytes);
-          tma_load_4d(rs + (size_t)slot * res_bytes, &maps.res, &resfull[slot], 0, ib * a.img, wb * a.wt,
-                      seg * SR + j);
-        }
-        G += (uint32_t)SR;
-      }
-    res_done:;
-    }
   } else {
     // Epilogue: warp (q, half) owns TMEM lanes 32q..32q+31 (pixels) and
     // channels 32*half..+31 of every output row.  It drains a block, zeroes
@@ -1539,6 +1519,28 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
     long long e_tf = 0;
     uint32_t G = 0;
     bool run = true;
+    const int ew = warp - 2;
+    uint8_t* tiles = rs + (size_t)ew * 4096;
+    uint64_t* mybar = rbar + 2 * ew;
+    const int pw = 32 / a.img;  // output columns per warp
+    // TMA coordinates (channel, image, column, row) of this warp's box of
+    // output row j of item u
+    auto box = [&](int u, int j, int* c) {
+      const int seg = u % a.segs;
+      const int strip = u / a.segs;
+      const int wb = strip % a.wblocks, ib = strip / a.wblocks;
+      c[0] = half * 32;
+      c[1] = ib * a.img;
+      c[2] = wb * a.wt + q * pw;
+      c[3] = seg * SR + j;
+    };
+    if (has_res && lane == 0 && (int)blockIdx.x < a.n_items) {
+      int c[4];
+      box(blockIdx.x, 0, c);
+      mbar_arrive_tx(&mybar[0], 2048);
+      tma_load_4d(tiles, &maps.res, &mybar[0], c[0], c[1], c[2], c[3]);
+    }
+    uint32_t g = 0;  // rows this warp has finished (residual tiles alternate)
     for (int u = blockIdx.x; u < a.n_items && run; u += gridDim.x) {
       const int seg = u % a.segs;
       const int strip = u / a.segs;
@@ -1548,9 +1550,22 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
       const int w = wb * a.wt + m / a.img;
       const bool img_ok = img < a.n_img;
       const int64_t pix0 = ((int64_t)img * a.ho + seg * SR) * a.wo + w;  // output row 0 of the segment
-      for (int j = 0; j < SR; ++j) {
+      for (int j = 0; j < SR; ++j, ++g) {
         const uint32_t gj = G + (uint32_t)j;
         const uint32_t blk = gj % NB;
+        const uint32_t tl = g & 1;
+        if (has_res && lane == 0) {
+          // the next row's residual into the other tile, once the store that
+          // last used that tile has read it
+          const int nu = j + 1 < SR ? u : u + (int)gridDim.x;
+          if (nu < a.n_items) {
+            int c[4];
+            box(nu, j + 1 < SR ? j + 1 : 0, c);
+            bulk_wait_read0();
+            mbar_arrive_tx(&mybar[tl ^ 1], 2048);
+            tma_load_4d(tiles + (tl ^ 1) * 2048, &maps.res, &mybar[tl ^ 1], c[0], c[1], c[2], c[3]);
+          }
+        }
         const long long t0 = a.prof ? clock64() : 0;
         const bool ok = mbar_wait(&tfull[blk], (gj / NB) & 1, abort_flag, 45);
         if (!__all_sync(0xffffffffu, ok)) { run = false; break; }
@@ -1567,48 +1582,47 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] += va[i];
         }
-        const int64_t off = (pix0 + (int64_t)j * a.wo) * 64 + col0;
-        uint4 rv[4];
-        if (NR) {
-          const int slot = (int)(gj % NR);
-          const bool rok = mbar_wait(&resfull[slot], (gj / NR) & 1, abort_flag, 47);
-          if (!__all_sync(0xffffffffu, rok)) { run = false; break; }
-          const uint8_t* rrow = rs + (size_t)slot * res_bytes + (size_t)m * 128;
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            rv[i] = *reinterpret_cast<const uint4*>(rrow + ((((half * 4 + i) ^ (m & 7))) << 4));
-          // the slot's next content arrives by TMA (async proxy): these
-          // generic reads are ordered before it by a proxy fence, not by the
-          // mbarrier alone (without it a 64-byte-aligned residual showed
-          // rows read after their slot had been refilled)
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&resempty[slot]);
-        }
-        if (img_ok) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += bias[i];
-          if (NR) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              float rr[8];
-              unpack8h(rv[i], rr, a.h16);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[8 * i + e] += rr[e];
-            }
-          }
-          act_inplace<32>(v, a.act, true);
-          uint4* op = reinterpret_cast<uint4*>(out + off);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) op[i] = pack8h(v + 8 * i, a.h16);
-        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[blk]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += bias[i];
+        if (has_res) {
+          const bool rok = mbar_wait(&mybar[tl], (g >> 1) & 1, abort_flag, 47);
+          if (!__all_sync(0xffffffffu, rok)) { run = false; break; }
+          uint8_t* tile = tiles + tl * 2048;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4* cp = reinterpret_cast<uint4*>(tile + swz64(lane, c));
+            float rr[8];
+            unpack8h(*cp, rr, a.h16);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[8 * c + e] += rr[e];
+            act_inplace<8>(v + 8 * c, a.act, true);
+            *cp = pack8h(v + 8 * c, a.h16);
+          }
+          // one proxy fence orders both the residual reads (before the tile's
+          // next TMA load) and the result writes (before this TMA store)
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            int c[4];
+            box(u, j, c);
+            tma_store_4d(&maps.out, tile, c[0], c[1], c[2], c[3]);
+            bulk_commit();
+          }
+        } else if (img_ok) {
+          act_inplace<32>(v, a.act, true);
+          const int64_t off = (pix0 + (int64_t)j * a.wo) * 64 + col0;
+          uint4* op = reinterpret_cast<uint4*>(out + off);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) op[i] = pack8h(v + 8 * i, a.h16);
+        }
       }
       G += (uint32_t)SR;
     }
+    if (has_res && lane == 0) bulk_wait0();
     tmem_st_wait();  // (an aborted row may leave its zeroing store unwaited)
     if (a.prof && lane == 0) {
       atomicAdd(&a.prof[RP_EPI_TOTAL], (unsigned long long)(clock64() - et0));
@@ -2450,10 +2464,9 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
       a.row_bytes = 64 * a.img * (wt + 2) * 2;
       const size_t rb = ((size_t)a.row_bytes + 1023) & ~(size_t)1023;
       const size_t wbytes = (size_t)9 * 64 * tc::BK * 2;
-      // residual rows (one strip row = IMG x WT pixels x 64 channels) in 3 slots
-      a.rring = p.has_residual ? 3 : 0;
-      const size_t res_bytes = (size_t)a.img * wt * 64 * 2;
-      const size_t fixed = 1024 + wbytes + a.rring * (res_bytes + 16) + (1 + 2 * tc::SLIDE_NL) * 8 + 16;
+      // residual layers: per-warp 2 x 2 KB residual / output tiles
+      a.rring = p.has_residual ? 1 : 0;
+      const size_t fixed = 1024 + wbytes + (a.rring ? 8 * 4096 : 0) + (1 + 2 * tc::SLIDE_NL + 16) * 8 + 16;
       int ring = (int)((227 * 1024 - fixed) / (rb + 16));
       if (ring > 8) ring = 8;
       if (ring >= 4) {
@@ -2463,10 +2476,13 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
         uint32_t box[4] = {64, (uint32_t)a.img, (uint32_t)(wt + 2), 1};
         if ((rc = encode(&maps.a[0], x, 4, dims, str, box))) return rc;
         if (a.rring) {
+          // residual and output: NHWC [n, ho, wo, 64]; one warp's 32 channels x 32 pixels per box
           uint64_t rdims[4] = {64, (uint64_t)p.n, (uint64_t)p.wo, (uint64_t)p.ho};
           uint64_t rstr[3] = {(uint64_t)p.ho * p.wo * 64 * 2, 64 * 2, (uint64_t)p.wo * 64 * 2};
-          uint32_t rbox[4] = {64, (uint32_t)a.img, (uint32_t)wt, 1};
-          if ((rc = encode(&maps.res, const_cast<void*>(a.res), 4, rdims, rstr, rbox))) return rc;
+          uint32_t rbox[4] = {32, (uint32_t)a.img, (uint32_t)(32 / a.img), 1};
+          if ((rc = encode(&maps.res, const_cast<void*>(a.res), 4, rdims, rstr, rbox, CU_TENSOR_MAP_SWIZZLE_64B)))
+            return rc;
+          if ((rc = encode(&maps.out, out.ptr, 4, rdims, rstr, rbox, CU_TENSOR_MAP_SWIZZLE_64B))) return rc;
         }
         const size_t smem = fixed + ring * (rb + 16);
         static bool attr_slide = false;
