@@ -1361,9 +1361,10 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
   // residual layers: every epilogue warp stages its own residual box (32
   // channels x its 32 pixels, 2 KB) by TMA in two tiles, adds it in place,
   // writes the output over it and TMA-stores the tile
-  const bool has_res = a.rring != 0;
+  const bool has_res = a.rring == 1;
+  const bool tiles_out = a.rring != 0;     // output through the per-warp tiles and TMA stores
   uint8_t* rs = sb + (size_t)9 * b_bytes;  // 8 epilogue warps x 2 x 2 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(rs + (has_res ? 8 * 4096 : 0));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rs + (tiles_out ? 8 * 4096 : 0));
   uint64_t* rfull = bars;
   uint64_t* rempty = rfull + NS;
   uint64_t* wfull = rempty + NS;
@@ -1396,10 +1397,8 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
   if (warp == 0 && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a[0])));
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)));
-    if (has_res) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.res)));
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.out)));
-    }
+    if (has_res) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.res)));
+    if (tiles_out) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.out)));
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -1559,6 +1558,7 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
           // last used that tile has read it
           const int nu = j + 1 < SR ? u : u + (int)gridDim.x;
           if (nu < a.n_items) {
+            // (every residual row is loaded; this also runs only for residual layers)
             int c[4];
             box(nu, j + 1 < SR ? j + 1 : 0, c);
             bulk_wait_read0();
@@ -1588,17 +1588,24 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
         if (lane == 0) mbar_arrive(&tempty[blk]);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += bias[i];
-        if (has_res) {
-          const bool rok = mbar_wait(&mybar[tl], (g >> 1) & 1, abort_flag, 47);
-          if (!__all_sync(0xffffffffu, rok)) { run = false; break; }
+        if (tiles_out) {
           uint8_t* tile = tiles + tl * 2048;
+          if (has_res) {
+            const bool rok = mbar_wait(&mybar[tl], (g >> 1) & 1, abort_flag, 47);
+            if (!__all_sync(0xffffffffu, rok)) { run = false; break; }
+          } else {
+            if (lane == 0) bulk_wait_read1();  // the store two rows back has read this tile
+            __syncwarp();
+          }
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint4* cp = reinterpret_cast<uint4*>(tile + swz64(lane, c));
-            float rr[8];
-            unpack8h(*cp, rr, a.h16);
+            if (has_res) {
+              float rr[8];
+              unpack8h(*cp, rr, a.h16);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[8 * c + e] += rr[e];
+              for (int e = 0; e < 8; ++e) v[8 * c + e] += rr[e];
+            }
             act_inplace<8>(v + 8 * c, a.act, true);
             *cp = pack8h(v + 8 * c, a.h16);
           }
@@ -1622,7 +1629,7 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
       }
       G += (uint32_t)SR;
     }
-    if (has_res && lane == 0) bulk_wait0();
+    if (tiles_out && lane == 0) bulk_wait0();
     tmem_st_wait();  // (an aborted row may leave its zeroing store unwaited)
     if (a.prof && lane == 0) {
       atomicAdd(&a.prof[RP_EPI_TOTAL], (unsigned long long)(clock64() - et0));
@@ -2465,7 +2472,11 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
       const size_t rb = ((size_t)a.row_bytes + 1023) & ~(size_t)1023;
       const size_t wbytes = (size_t)9 * 64 * tc::BK * 2;
       // residual layers: per-warp 2 x 2 KB residual / output tiles
-      a.rring = p.has_residual ? 1 : 0;
+      static const bool tiles_nores = [] {
+        const char* e = getenv("C3B200_SLIDE_TILES");
+        return e && e[0] == '1';
+      }();
+      a.rring = p.has_residual ? 1 : tiles_nores ? 2 : 0;
       const size_t fixed = 1024 + wbytes + (a.rring ? 8 * 4096 : 0) + (1 + 2 * tc::SLIDE_NL + 16) * 8 + 16;
       int ring = (int)((227 * 1024 - fixed) / (rb + 16));
       if (ring > 8) ring = 8;
@@ -2477,10 +2488,12 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
         if ((rc = encode(&maps.a[0], x, 4, dims, str, box))) return rc;
         if (a.rring) {
           // residual and output: NHWC [n, ho, wo, 64]; one warp's 32 channels x 32 pixels per box
+          // (rring 2: output tiles only, no residual)
           uint64_t rdims[4] = {64, (uint64_t)p.n, (uint64_t)p.wo, (uint64_t)p.ho};
           uint64_t rstr[3] = {(uint64_t)p.ho * p.wo * 64 * 2, 64 * 2, (uint64_t)p.wo * 64 * 2};
           uint32_t rbox[4] = {32, (uint32_t)a.img, (uint32_t)(32 / a.img), 1};
-          if ((rc = encode(&maps.res, const_cast<void*>(a.res), 4, rdims, rstr, rbox, CU_TENSOR_MAP_SWIZZLE_64B)))
+          if (a.res &&
+              (rc = encode(&maps.res, const_cast<void*>(a.res), 4, rdims, rstr, rbox, CU_TENSOR_MAP_SWIZZLE_64B)))
             return rc;
           if ((rc = encode(&maps.out, out.ptr, 4, rdims, rstr, rbox, CU_TENSOR_MAP_SWIZZLE_64B))) return rc;
         }
