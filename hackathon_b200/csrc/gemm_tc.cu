@@ -1336,21 +1336,21 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
 // ends).  Every MMA accumulates; the epilogue zeroes a block after draining it
 // (and all blocks at start), which is what lets one instruction start one
 // output row while it continues two others.
-// Accumulator ring: SLIDE_NL logical output-row blocks of 64 TMEM columns in
-// 8 physical blocks.  Physical blocks 6 and 7 alias logical blocks 0 and 1, so
-// every three-row window (logical b0..b0+2, b0 <= 5) is three consecutive
-// physical blocks and one MMA: a row of logical block 0 or 1 may accumulate
-// partly in its own block and partly in its alias, and the epilogue adds the
-// two.  (A ring of 8 split the windows that wrapped, 2 rows in 8, into two
-// MMAs each.)
-constexpr int SLIDE_NL = 6;
+// Accumulator ring: SLIDE_NL output-row blocks of 64 TMEM columns.  A window
+// of three rows that wraps around the ring is issued as two MMAs (N=128 +
+// N=64), so every output row accumulates in one block and its result does not
+// depend on where the ring stands.  (Aliasing blocks 0 and 1 into two spare
+// blocks, which kept every window one MMA, split those rows' sums in two and
+// made their bits depend on the schedule, i.e. on the batch size.)
+constexpr int SLIDE_NL = 8;
 constexpr int SLIDE_NPHYS = 8;
 constexpr int SLIDE_THREADS = 320;  // producer, MMA, 8 epilogue warps
 
 __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(const __grid_constant__ TmaMaps maps,
                                                                           const TcArgs a) {
-  constexpr int NB = SLIDE_NL;        // logical blocks: barriers, ring positions
-  constexpr int NPHYS = SLIDE_NPHYS;  // physical 64-column blocks
+  constexpr int NB = SLIDE_NL;        // accumulator blocks (one output row each)
+  constexpr int NPHYS = SLIDE_NPHYS;  // TMEM blocks allocated
+  static_assert(NPHYS == NB, "every row accumulates in its own block");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NS = a.ring;
@@ -1469,19 +1469,33 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
           const int j0 = i >= 2 ? i - 2 : 0;
           const int j1 = i < SR ? i : SR - 1;
           const int cnt = j1 - j0 + 1;
-          // logical b0 <= 5 and at most 3 blocks: physical b0 .. b0+cnt-1 <= 7
           const int b0 = (int)((G + (uint32_t)j0) % NB);
+          const int n1 = cnt < NB - b0 ? cnt : NB - b0;  // blocks before the ring wraps
+          const int n2 = cnt - n1;
           const int r0 = i - j0;  // tap row of block j0; the next blocks take r0-1, r0-2
           const uint64_t ad = smem_desc(smem_u32(sr + (size_t)slot * rb_al));
           const uint64_t bd = bd0 + (uint64_t)(2 - r0) * WB;
           const uint32_t d1 = tmem_base + (uint32_t)(b0 * 64);
-          const uint32_t id1 = cnt == 3 ? idesc192 : cnt == 2 ? idesc128 : idesc64;
+          const uint32_t id1 = n1 == 3 ? idesc192 : n1 == 2 ? idesc128 : idesc64;
+          if (n2 == 0) {
 #pragma unroll
-          for (int s = 0; s < 3; ++s)
+            for (int s = 0; s < 3; ++s)
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k)
-              mma_bf16(d1, ad + (uint64_t)s * sstep + (uint64_t)(2 * k), bd + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k),
-                       id1, 1u);
+              for (int k = 0; k < BK / 16; ++k)
+                mma_bf16(d1, ad + (uint64_t)s * sstep + (uint64_t)(2 * k), bd + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k),
+                         id1, 1u);
+          } else {
+            const uint32_t id2 = n2 == 2 ? idesc128 : idesc64;
+            const uint64_t bd2 = bd + (uint64_t)n1 * WB;
+#pragma unroll
+            for (int s = 0; s < 3; ++s)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k) {
+                const uint64_t aa = ad + (uint64_t)s * sstep + (uint64_t)(2 * k);
+                mma_bf16(d1, aa, bd + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k), id1, 1u);
+                mma_bf16(tmem_base, aa, bd2 + (uint64_t)(s * 3) * WB + (uint64_t)(2 * k), id2, 1u);
+              }
+          }
           mma_commit(&rempty[slot]);
           if (i >= 2) mma_commit(&tfull[(G + (uint32_t)(i - 2)) % NB]);
         }
@@ -1574,14 +1588,6 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
         float v[32];
         tmem_ld32(lane_base + blk * 64, v);
         tmem_st32_zero(lane_base + blk * 64);
-        if (blk < (uint32_t)(NPHYS - NB)) {
-          // the part of the row that accumulated in the alias block
-          float va[32];
-          tmem_ld32(lane_base + (blk + NB) * 64, va);
-          tmem_st32_zero(lane_base + (blk + NB) * 64);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += va[i];
-        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
