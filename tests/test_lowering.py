@@ -66,7 +66,7 @@ def test_lowering_fuses_to_expected_kernels(model, batch, profile, kinds):
     assert prog.tensors["logits"].dtype == L.F32
 
 
-def test_flop_accounting_matches_survey():
+def test_flop_accounting_per_image():
     """ResNet-18 conv GEMMs: 1.1108 GFLOP per image (the figure roofline.achieved uses)."""
     p = lower(BUILDERS["resnet18"](), 16, "bf16")
     conv = sum(s.flops for s in p.steps if s.label.startswith("conv") or s.label == "stem_conv")
