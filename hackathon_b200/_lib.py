@@ -106,7 +106,7 @@ class GemmTcParams(C.Structure):
 
 class ConvTcParams(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("n", "h", "w", "cin", "cout", "ho", "wo", "k", "stride", "pad",
-                                         "has_residual", "act", "block_n", "mode")]
+                                         "has_residual", "act", "block_n", "mode", "has_shortcut")]
 
 
 class FlashParams(C.Structure):

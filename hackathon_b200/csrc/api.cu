@@ -208,8 +208,8 @@ int dispatch(int kid, const c3b_tensor* in, int n_in, const c3b_tensor* out, int
     case C3B_K_CONV_TC: {
       c3b_conv_tc_params p;
       if ((rc = get_params(params, len, p))) return rc;
-      C3B_REQUIRE(n_out == 1, "tc conv: one output");
-      return launch_conv_tc(in, n_in, out[0], p, s);
+      C3B_REQUIRE(n_out == (p.has_shortcut ? 2 : 1), "tc conv: one output, two with the fused shortcut");
+      return launch_conv_tc(in, n_in, out, p, s);
     }
     case C3B_K_FLASH_ATTN: {
       c3b_flash_params p;

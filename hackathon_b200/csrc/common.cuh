@@ -230,7 +230,8 @@ int launch_flash_tc(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_flas
 int launch_gemm_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_params& p, cudaStream_t s);
 int launch_conv_simt(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_params& p, cudaStream_t s);
 int launch_gemm_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_gemm_tc_params& p, cudaStream_t s);
-int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_tc_params& p, cudaStream_t s);
+int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor* outs, const c3b_conv_tc_params& p,
+                   cudaStream_t s);
 int launch_flash_attn(const c3b_tensor& qkv, const c3b_tensor& out, const c3b_flash_params& p, cudaStream_t s);
 int launch_quant_e4m3(const c3b_tensor& x, const c3b_tensor& q, const c3b_tensor& scale, const c3b_quant_params& p,
                       cudaStream_t s);

@@ -77,6 +77,14 @@ struct TcArgs {
   // tc_gemm_kernel: bf16 output through per-warp shared-memory tiles and TMA
   // stores (maps.out: 16 columns x 32 rows, 32-byte swizzle)
   int tma_out;
+  // fused 1x1 stride-2 shortcut (tc_gemm_kernel<0, 1>, convolutions): aux_n
+  // more accumulator columns per tile, fed by the centre tap's K blocks
+  // [aux_kb0, aux_kb0 + cblocks) against aux_w [aux_n][cin] (resident in
+  // shared memory); output aux_out [M][aux_n] = acc + aux_bias, no activation
+  int aux_n, aux_kb0;
+  const uint16_t* aux_w;
+  const float* aux_bias;
+  uint16_t* aux_out;
   // 16-bit format of A, B and every 16-bit output / residual: 0 bf16, 1 fp16
   int h16;
   // optional wait counters of the row-ring kernel (C3B200_CONV_PROF=1), else null
@@ -281,7 +289,7 @@ constexpr int W4_GROUP = 16;  // K elements per FP4 scale
 // its own 128 A rows and half of the tile's B columns, CTA 0 issues
 // tcgen05.mma.cta_group::2 for both, and each CTA drains its own 128 rows.
 // Per SM that halves the B bytes staged and read per MMA.  bf16/fp16 only.
-template <int MODE, int CG = 1>
+template <int MODE, int CG = 1, bool AUX = false>
 __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TmaMaps maps, const TcArgs a) {
   constexpr bool F8 = MODE == 1, W4 = MODE == 2, TF = MODE == 3;
   static_assert(CG == 1 || MODE == 0, "CTA pairs: bf16/fp16 operands only");
@@ -297,15 +305,23 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   const uint32_t b_bytes = (uint32_t)(a.block_n / CG) * BK * 2;  // this CTA's share of B
   const uint32_t raw_bytes = W4 ? (uint32_t)a.block_n * (BK / 2) : 0u;                 // packed FP4
   const uint32_t scl_bytes = W4 ? (uint32_t)a.block_n * (BK / W4_GROUP) * 4u : 0u;     // fp32 scales
+  // Resident B (bres, single CTAs, bf16/fp16): the CTA's whole B column block
+  // (k_blocks x b_bytes) is loaded once; only A streams through the stages.
+  const bool bres = MODE == 0 && CG == 1 && a.bres != 0;
   uint8_t* sa = smem;
   uint8_t* sb = smem + (size_t)stages * a_bytes;
-  uint8_t* sraw = sb + (size_t)stages * b_bytes;
+  uint8_t* sraw = sb + (size_t)(bres ? a.k_blocks : stages) * b_bytes;
   uint8_t* sscl = sraw + (size_t)stages * raw_bytes;
+  // fused shortcut weights: cblocks x [aux_n rows x 128 bytes], 128-byte swizzle
+  constexpr bool aux = AUX;  // fused 1x1 shortcut (conv launches with has_shortcut)
+  static_assert(!AUX || (MODE == 0 && CG == 1), "fused shortcut: single bf16/fp16 tiles");
+  uint8_t* saux = sscl + (size_t)stages * scl_bytes;  // 1024-byte aligned: every region above is
+  const uint32_t aux_kb_bytes = (uint32_t)a.aux_n * 128u;
   // per-warp output tiles (2 per epilogue warp: 1 KB for 16-bit output, 2 KB
   // for f32 output; 1024-byte aligned)
   const uint32_t tile_bytes = a.tma_out == 2 ? 2048u : 1024u;
   uint8_t* stg = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(sscl + (size_t)stages * scl_bytes) + 1023) & ~uintptr_t(1023));
+      (reinterpret_cast<uintptr_t>(saux + (aux ? (size_t)a.cblocks * aux_kb_bytes : 0)) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(stg + (a.tma_out ? (size_t)EPIW * 2 * tile_bytes : 0));
   uint64_t* full = bars;
   uint64_t* empty = bars + stages;
@@ -318,13 +334,27 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t tmem_cols = (uint32_t)a.block_n * 2;
+  // one accumulator buffer: block_n columns (+ aux_n); recomputed where used
+  // from the kernel parameters, which costs no register
+#define ACC_COLS ((uint32_t)(a.block_n + (aux ? a.aux_n : 0)))
+  const uint32_t tmem_cols = ACC_COLS * 2;
 
+  if (aux) {
+    // constant weights: read before the dependency wait, made visible to the
+    // MMA (async proxy) by the fence before the barrier below
+    const int chunks = a.aux_n * a.cblocks * 8;  // 16-byte chunks
+    for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
+      const int c = i & 7, n = (i >> 3) % a.aux_n, cb = (i >> 3) / a.aux_n;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.aux_w + (size_t)n * a.cin + cb * BK + c * 8));
+      *reinterpret_cast<uint4*>(saux + (size_t)cb * aux_kb_bytes + n * 128 + ((c ^ (n & 7)) << 4)) = v;
+    }
+    fence_proxy_async();
+  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
-      mbar_init(&bready[i], 8);
+      mbar_init(&bready[i], bres ? 1 : 8);  // bres: bready[0] = B resident
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
@@ -366,6 +396,16 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      const long long gp0 = a.prof ? clock64() : 0;
+      long long gp_empty = 0;
+      if (bres && cid < a.n_tiles) {
+        // every tile of this CTA has column block cid % n_tiles_n (the grid is
+        // a multiple of n_tiles_n)
+        const int n0 = (cid % a.n_tiles_n) * a.block_n;
+        mbar_arrive_tx(&bready[0], (uint32_t)a.k_blocks * b_bytes);
+        for (int kb = 0; kb < a.k_blocks; ++kb)
+          tma_load_2d(sb + (size_t)kb * b_bytes, &maps.b, &bready[0], kb * BK, n0);
+      }
       for (int t = cid; t < a.n_tiles; t += ncl) {
         const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
         const int m0 = (mb * CG + (int)rank) * BM, n0 = nb * a.block_n + (int)rank * (a.block_n / CG);
@@ -375,7 +415,9 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
           oh0 = (m0 % a.pix) / a.wo;
         }
         for (int kb = 0; kb < a.k_blocks; ++kb) {
+          const long long gw = a.prof ? clock64() : 0;
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 11)) goto producer_done;
+          if (a.prof) gp_empty += clock64() - gw;
           uint8_t* dA = sa + (size_t)stage * a_bytes;
           uint8_t* dB = sb + (size_t)stage * b_bytes;
           if (W4) {
@@ -407,11 +449,11 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
             }
             tma_load_2d_pair(dB, &maps.b, fb, kb * KEL, n0);
           } else if (!a.conv) {
-            mbar_arrive_tx(&full[stage], a_bytes + b_bytes);
+            mbar_arrive_tx(&full[stage], bres ? a_bytes : a_bytes + b_bytes);
             tma_load_2d(dA, &maps.a[0], &full[stage], kb * KEL, m0);
-            tma_load_2d(dB, &maps.b, &full[stage], kb * KEL, n0);
+            if (!bres) tma_load_2d(dB, &maps.b, &full[stage], kb * KEL, n0);
           } else {
-            mbar_arrive_tx(&full[stage], a_bytes + b_bytes);
+            mbar_arrive_tx(&full[stage], bres ? a_bytes : a_bytes + b_bytes);
             const int tap = kb / a.cblocks, cb = kb % a.cblocks;
             const int r = tap / a.ksz, s = tap % a.ksz;
             int map = 0, ro, so;
@@ -426,10 +468,14 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
               map = pr * 2 + ps;
             }
             tma_load_4d(dA, &maps.a[map], &full[stage], cb * BK, so, oh0 + ro, img0);
-            tma_load_2d(dB, &maps.b, &full[stage], kb * BK, n0);
+            if (!bres) tma_load_2d(dB, &maps.b, &full[stage], kb * BK, n0);
           }
           if (++stage == stages) { stage = 0; phase ^= 1; }
         }
+      }
+      if (a.prof) {
+        atomicAdd(&a.prof[RP_PROD_TOTAL], (unsigned long long)(clock64() - gp0));
+        atomicAdd(&a.prof[RP_PROD_EMPTY], (unsigned long long)gp_empty);
       }
     producer_done:;
     }
@@ -439,24 +485,33 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
       const uint32_t idesc = F8   ? instr_desc_e4m3(BM, a.block_n)
                              : TF ? instr_desc_tf32(BM, a.block_n)
                                   : instr_desc_h(BM * CG, a.block_n, a.h16);
+      const uint32_t idesc_aux = aux ? instr_desc_h(BM, a.aux_n, a.h16) : 0u;
+      const uint64_t xd0 = smem_desc(smem_u32(saux));
       // stage descriptors = base descriptor + offset in 16-byte units
       const uint64_t ad0 = smem_desc(smem_u32(sa)), bd0 = smem_desc(smem_u32(sb));
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = cid; t < a.n_tiles; t += ncl) {
+      const long long gm0 = a.prof ? clock64() : 0;
+      long long gm_te = 0, gm_full = 0;
+      bool b_ok = !bres || cid >= a.n_tiles || mbar_wait(&bready[0], 0, abort_flag, 17);
+      for (int t = cid; t < a.n_tiles && b_ok; t += ncl) {
+        long long gw = a.prof ? clock64() : 0;
         if (!(CG == 2 ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, abort_flag, 12)
                       : mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 12)))
           break;
+        if (a.prof) gm_te += clock64() - gw;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * a.block_n);
+        const uint32_t d_tmem = tmem_base + (uint32_t)acc * ACC_COLS;
         bool ok = true;
         for (int kb = 0; kb < a.k_blocks; ++kb) {
+          gw = a.prof ? clock64() : 0;
           if (!mbar_wait(W4 ? &bready[stage] : &full[stage], phase, abort_flag, 13)) { ok = false; break; }
+          if (a.prof) gm_full += clock64() - gw;
           tc_fence_after();
           const uint64_t ad = ad0 + (uint64_t)stage * (a_bytes >> 4);
-          const uint64_t bd = bd0 + (uint64_t)stage * (b_bytes >> 4);
+          const uint64_t bd = bd0 + (uint64_t)(bres ? kb : stage) * (b_bytes >> 4);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // four 32-byte K steps per 128-byte row
             if (CG == 2)
@@ -467,6 +522,15 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
               mma_tf32(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
             else
               mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          if (aux && kb >= a.aux_kb0 && kb < a.aux_kb0 + a.cblocks) {
+            // the centre tap's A block is the shortcut's A: its N columns go
+            // to the accumulator block after the tile's own
+            const uint64_t xd = xd0 + (uint64_t)(((uint32_t)(kb - a.aux_kb0) * aux_kb_bytes) >> 4);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_bf16(d_tmem + (uint32_t)a.block_n, ad + (uint64_t)(2 * k), xd + (uint64_t)(2 * k), idesc_aux,
+                       (kb > a.aux_kb0 || k > 0) ? 1u : 0u);
           }
           if (CG == 2)
             mma_commit_pair(&empty[stage]);
@@ -480,6 +544,11 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
         else
           mma_commit(&tfull[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      if (a.prof) {
+        atomicAdd(&a.prof[RP_MMA_TOTAL], (unsigned long long)(clock64() - gm0));
+        atomicAdd(&a.prof[RP_MMA_RFULL], (unsigned long long)gm_full);
+        atomicAdd(&a.prof[RP_MMA_TEMPTY], (unsigned long long)gm_te);
       }
     }
   } else if (W4 && warp >= 2 + EPIW) {
@@ -574,7 +643,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 14);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.block_n + part * cols);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)acc * ACC_COLS + (uint32_t)(part * cols);
 #pragma unroll 1
       for (int c0 = 0; f32_tma && c0 < cols; c0 += 16) {
         float v[16];
@@ -656,6 +725,27 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
           for (int i = 0; i < 4; ++i) rc[i] = rn[i];
         }
       }
+      if (aux) {
+        // fused shortcut: this warp's quarter of the aux_n columns, + bias,
+        // no activation, 16-bit rows straight from registers
+        const int acols = a.aux_n / (EPIW / 4);
+#pragma unroll 1
+        for (int c0 = 0; c0 < acols; c0 += 16) {
+          float v[16];
+          tmem_ld16(tbase - (uint32_t)(part * cols) + (uint32_t)(a.block_n + part * acols + c0), v);
+          if (row < a.M) {
+            const float4* bp = reinterpret_cast<const float4*>(a.aux_bias + part * acols + c0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float4 b = __ldg(bp + i);
+              v[4 * i] += b.x; v[4 * i + 1] += b.y; v[4 * i + 2] += b.z; v[4 * i + 3] += b.w;
+            }
+            uint4* op = reinterpret_cast<uint4*>(a.aux_out + row * a.aux_n + part * acols + c0);
+            op[0] = pack8h(v, a.h16);
+            op[1] = pack8h(v + 8, a.h16);
+          }
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -685,6 +775,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     else
       asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
   }
+#undef ACC_COLS
 }
 
 // Epilogue for one 16-column chunk of one output row: +bias [+residual] -> act -> store.
@@ -2050,24 +2141,69 @@ static int enable_tma_out(tc::TmaMaps& maps, tc::TcArgs& a) {
   return C3B_OK;
 }
 
-template <int MODE, int CG = 1>
+// Wait profiler of tc_gemm_kernel (C3B200_GEMM_PROF=1, measurement runs only):
+// cycles summed over CTAs, printed after a synchronous launch.
+static unsigned long long* gemm_prof_buf() {
+  static unsigned long long* buf = [] {
+    const char* e = getenv("C3B200_GEMM_PROF");
+    unsigned long long* b = nullptr;
+    if (e && e[0] == '1' && cudaMalloc(&b, tc::RP_COUNT * sizeof(unsigned long long)) != cudaSuccess) b = nullptr;
+    return b;
+  }();
+  return buf;
+}
+
+static int gemm_prof_report(const tc::TcArgs& a, int ctas, cudaStream_t s) {
+  unsigned long long h[tc::RP_COUNT];
+  C3B_CHECK_CUDA(cudaStreamSynchronize(s));
+  C3B_CHECK_CUDA(cudaMemcpy(h, a.prof, sizeof(h), cudaMemcpyDeviceToHost));
+  const int issuers = a.cg == 2 ? ctas / 2 : ctas;
+  const double tiles = (double)a.n_tiles / issuers;
+  fprintf(stderr,
+          "[gemm prof] M %lld N %lld K %lld block_n %d cg %d stages %d | per CTA: prod %.0f (empty-wait %.0f) | "
+          "mma %.0f (full-wait %.0f tempty-wait %.0f) | epi tfull-wait per warp %.0f | tiles/issuer %.1f | "
+          "per k-block: mma %.0f full-wait %.0f\n",
+          (long long)a.M, (long long)a.N, (long long)a.K, a.block_n, a.cg, a.stages, (double)h[tc::RP_PROD_TOTAL] / ctas,
+          (double)h[tc::RP_PROD_EMPTY] / ctas, (double)h[tc::RP_MMA_TOTAL] / issuers,
+          (double)h[tc::RP_MMA_RFULL] / issuers, (double)h[tc::RP_MMA_TEMPTY] / issuers,
+          (double)h[tc::RP_EPI_TFULL] / (16.0 * ctas), tiles, (double)h[tc::RP_MMA_TOTAL] / issuers / (tiles * a.k_blocks),
+          (double)h[tc::RP_MMA_RFULL] / issuers / (tiles * a.k_blocks));
+  return C3B_OK;
+}
+
+template <int MODE, int CG = 1, bool AUX = false>
 static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s) {
+  if (unsigned long long* pb = gemm_prof_buf()) {
+    C3B_CHECK_CUDA(cudaMemsetAsync(pb, 0, tc::RP_COUNT * sizeof(unsigned long long), s));
+    a.prof = pb;
+  }
   // one 128-byte K row per operand row; MODE 2 adds the packed FP4 tile and its scales
-  size_t stage_bytes = (size_t)tc::BM * 128 + (size_t)(a.block_n / CG) * 128;
+  const size_t b_stage = (size_t)(a.block_n / CG) * 128;
+  if (MODE != 0 || CG != 1) a.bres = 0;
+  const size_t b_res = a.bres ? (size_t)a.k_blocks * b_stage : 0;  // resident B (single CTAs)
+  if ((a.aux_n != 0) != AUX) return fail(C3B_E_INVALID, "tc gemm: fused shortcut needs its kernel variant");
+  const size_t aux_bytes = AUX ? (size_t)a.cblocks * a.aux_n * 128 : 0;  // fused shortcut weights
+  size_t stage_bytes = (size_t)tc::BM * 128 + (a.bres ? 0 : b_stage);
   if (MODE == 2) stage_bytes += (size_t)a.block_n * (tc::BK / 2) + (size_t)a.block_n * (tc::BK / tc::W4_GROUP) * 4;
-  const size_t out_tiles =
+  size_t out_tiles =
       a.tma_out ? (size_t)(MODE == 2 ? 8 : 16) * (a.tma_out == 2 ? 4096 : 2048) + 1024 : 0;  // + alignment
   // with output tiles the stage ring takes what the opt-in maximum leaves, so
   // long-K convolutions keep their pipeline depth
-  const size_t budget = a.tma_out ? 227 * 1024 - 2048 - out_tiles : 200 * 1024;
+  size_t budget = a.tma_out ? 227 * 1024 - 2048 - out_tiles - b_res - aux_bytes : 200 * 1024 - b_res - aux_bytes;
+  if (a.bres && a.tma_out && budget / stage_bytes < 4) {
+    // resident B and output tiles leave under four A stages: per-lane stores
+    a.tma_out = 0;
+    out_tiles = 0;
+    budget = 227 * 1024 - 2048 - b_res - aux_bytes;
+  }
   int stages = (int)(budget / stage_bytes);
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(C3B_E_INVALID, "tc gemm: tile does not fit in shared memory");
   a.stages = stages;
-  const size_t smem = 1024 + stages * stage_bytes + out_tiles + (3 * stages + 4 + 32) * 8 + 16;
+  const size_t smem = 1024 + stages * stage_bytes + b_res + aux_bytes + out_tiles + (3 * stages + 4 + 32) * 8 + 16;
   static bool attr_set = false;
   if (!attr_set) {
-    C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<MODE, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    C3B_CHECK_CUDA(cudaFuncSetAttribute(tc::tc_gemm_kernel<MODE, CG, AUX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         227 * 1024));
     attr_set = true;
   }
@@ -2087,7 +2223,7 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
       cfg.attrs = at;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, tc::tc_gemm_kernel<MODE, CG>, &cfg) != cudaSuccess || n < 1) {
+      if (cudaOccupancyMaxActiveClusters(&n, tc::tc_gemm_kernel<MODE, CG, AUX>, &cfg) != cudaSuccess || n < 1) {
         (void)cudaGetLastError();
         n = sm_count() / 2;
       }
@@ -2095,17 +2231,17 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
     }
     const int clusters = a.n_tiles < max_clusters ? a.n_tiles : max_clusters;
     if (clusters < 1) return C3B_OK;
-    if (int rc = launch_pdl_cluster(tc::tc_gemm_kernel<MODE, CG>, 2 * clusters, 2, tc::HALO16_THREADS, smem, s, maps,
+    if (int rc = launch_pdl_cluster(tc::tc_gemm_kernel<MODE, CG, AUX>, 2 * clusters, 2, tc::HALO16_THREADS, smem, s, maps,
                                     a))
       return rc;
     C3B_CHECK_CUDA(cudaGetLastError());
-    return C3B_OK;
+    return a.prof ? gemm_prof_report(a, 2 * clusters, s) : C3B_OK;
   }
   int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
   if (grid < 1) return C3B_OK;
-  if (int rc = launch_pdl(tc::tc_gemm_kernel<MODE, CG>, grid, tc::HALO16_THREADS, smem, s, maps, a)) return rc;
+  if (int rc = launch_pdl(tc::tc_gemm_kernel<MODE, CG, AUX>, grid, tc::HALO16_THREADS, smem, s, maps, a)) return rc;
   C3B_CHECK_CUDA(cudaGetLastError());
-  return C3B_OK;
+  return a.prof ? gemm_prof_report(a, grid, s) : C3B_OK;
 }
 
 // CTA pairs for bf16/fp16 GEMMs and convolutions through tc_gemm_kernel with
@@ -2142,8 +2278,28 @@ static int use_pairs(tc::TmaMaps& maps, tc::TcArgs& a, const void* b, uint64_t K
   return C3B_OK;
 }
 
+// Resident B for single-CTA bf16/fp16 convolutions whose B column block fits
+// in shared memory beside four A stages: the weights are staged once per CTA
+// instead of once per tile, which halves the shared-memory fill of each K
+// block (N = 128 tiles are bound by shared-memory bandwidth: TMA fill plus
+// the MMA operand reads).  A CTA's tiles all share one column block when the
+// grid (the SM count) is a multiple of the column-block count.
+// C3B200_GEMM_BRES=0 restages B per K block (A/B timing).
+static void use_resident_b(tc::TcArgs& a) {
+  static const bool on = [] {
+    const char* e = getenv("C3B200_GEMM_BRES");
+    return !(e && e[0] == '0');
+  }();
+  a.bres = 0;
+  const size_t b_res = (size_t)a.k_blocks * a.block_n * 128;
+  if (!on || a.cg != 1 || sm_count() % a.n_tiles_n != 0 || a.n_tiles < 2 * sm_count()) return;
+  if (b_res + 4 * (size_t)tc::BM * 128 + 4096 > 227 * 1024) return;
+  a.bres = 1;
+}
+
 static int launch_tc(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s, int mode = 0) {
   if (mode == 0 && a.cg == 2) return launch_tc_mode<0, 2>(maps, a, s);
+  if (mode == 0 && a.aux_n) return launch_tc_mode<0, 1, true>(maps, a, s);
   if (mode == 3) return launch_tc_mode<3>(maps, a, s);
   if (mode == 1) return launch_tc_mode<1>(maps, a, s);
   if (mode == 2) return launch_tc_mode<2>(maps, a, s);
@@ -2387,9 +2543,12 @@ int launch_gemm_w4a16(const c3b_tensor* in, int n_in, const c3b_tensor& out, con
   return launch_tc(maps, a, s, 2);
 }
 
-int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const c3b_conv_tc_params& p,
+int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor* outs, const c3b_conv_tc_params& p,
                    cudaStream_t s) {
-  C3B_REQUIRE(n_in == 3 + (p.has_residual ? 1 : 0), "tc conv: inputs x, w, bias [, residual]");
+  const c3b_tensor& out = outs[0];
+  const int n_main = 3 + (p.has_residual ? 1 : 0);
+  C3B_REQUIRE(n_in == n_main + (p.has_shortcut ? 2 : 0),
+              "tc conv: inputs x, w, bias [, residual] [, shortcut w, shortcut bias]");
   C3B_REQUIRE((in[0].dtype == C3B_BF16 || in[0].dtype == C3B_F16) && in[1].dtype == in[0].dtype,
               "tc conv: activations and weights both bf16 or both fp16");
   C3B_REQUIRE(p.cin % 64 == 0, "tc conv: Cin must be a multiple of 64");
@@ -2411,7 +2570,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
   tc::TcArgs a;
   memset(&a, 0, sizeof(a));
   a.h16 = in[0].dtype == C3B_F16;
-  int rc = fill_epilogue(a, in, n_in, 2, C3B_BIAS_COL, p.has_residual, M, p.cout, out);
+  int rc = fill_epilogue(a, in, n_main, 2, C3B_BIAS_COL, p.has_residual, M, p.cout, out);
   if (rc) return rc;
   if (M == 0) return C3B_OK;
   const int64_t K = (int64_t)p.k * p.k * p.cin;
@@ -2675,8 +2834,28 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const 
         if ((rc = encode(&maps.a[pr * 2 + ps], base, 4, dims, str, box))) return rc;
       }
   }
-  if ((rc = use_pairs(maps, a, in[1].ptr, (uint64_t)K, (uint64_t)p.cout))) return rc;
+  if (p.has_shortcut) {
+    // the 1x1 stride-2 shortcut samples the centre tap's pixels: its A blocks
+    // are the centre tap's, and it becomes aux_n more columns of each tile
+    const c3b_tensor &ws = in[n_main], &bs = in[n_main + 1], &ys = outs[1];
+    C3B_REQUIRE(p.stride == 2 && p.k % 2 == 1 && p.pad == p.k / 2, "tc conv shortcut: stride 2, pad k/2");
+    C3B_REQUIRE(a.n_tiles_n == 1 && a.block_n == p.cout && (p.cout == 64 || p.cout == 128),
+                "tc conv shortcut: Cout 64 or 128 (one column block)");
+    C3B_REQUIRE(ws.dtype == in[0].dtype && numel(ws) == (int64_t)p.cout * p.cin, "tc conv shortcut: ws [Cout, Cin]");
+    C3B_REQUIRE(bs.dtype == C3B_F32 && numel(bs) == p.cout, "tc conv shortcut: bs [Cout] f32");
+    C3B_REQUIRE(ys.dtype == in[0].dtype && numel(ys) == M * p.cout, "tc conv shortcut: ys [N, Ho, Wo, Cout] 16-bit");
+    C3B_REQUIRE(((uintptr_t)ws.ptr & 15) == 0 && ((uintptr_t)bs.ptr & 15) == 0 && ((uintptr_t)ys.ptr & 15) == 0,
+                "tc conv shortcut: 16-byte alignment");
+    a.aux_n = p.cout;
+    a.aux_kb0 = (p.pad * p.k + p.pad) * a.cblocks;
+    a.aux_w = static_cast<const uint16_t*>(ws.ptr);
+    a.aux_bias = static_cast<const float*>(bs.ptr);
+    a.aux_out = static_cast<uint16_t*>(ys.ptr);
+  } else if ((rc = use_pairs(maps, a, in[1].ptr, (uint64_t)K, (uint64_t)p.cout))) {
+    return rc;
+  }
   if ((rc = enable_tma_out(maps, a))) return rc;
+  use_resident_b(a);
   return launch_tc(maps, a, s);
 }
 

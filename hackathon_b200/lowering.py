@@ -501,9 +501,33 @@ def _gap_classifier(st: _State, op: dict, C: int):
     return u
 
 
+def _conv_shortcut(st: _State, op: dict, H: int, W: int, geo, O: int):
+    """The 1x1 stride-2 convolution on this 3x3 (k odd, pad k/2) stride-2
+    convolution's input, when one launch can compute both: the residual
+    block's downsampling shortcut samples exactly the centre tap's pixels.
+    It must not have been emitted yet, and has the same Cout (64 or 128), no
+    activation and no residual.  C3B200_CONV_SHORTCUT=0 keeps two launches."""
+    if os.environ.get("C3B200_CONV_SHORTCUT", "1") == "0" or op["res"] or O not in (64, 128):
+        return None
+    kh = op["w"].shape[2]
+    if kh % 2 == 0 or op["w"].shape[3] != kh or geo.sh != 2 or geo.sw != 2 or geo.ph0 != kh // 2:
+        return None
+    for u in st.ops:
+        if u is op or u["kind"] != "conv" or u.get("fused") or u.get("_emitted") or st.t(u["x"]) != st.t(op["x"]):
+            continue
+        w = u["w"]
+        if w.shape != (O, op["w"].shape[1], 1, 1) or u["res"] or u["act"] != L.ACT_NONE:
+            continue
+        g1, _, _ = conv_geometry(u["attrs"], H, W, 1, 1)
+        if g1.sh == 2 and g1.sw == 2 and g1.ph0 == g1.ph1 == g1.pw0 == g1.pw1 == 0 and g1.dh == 1:
+            return u
+    return None
+
+
 def _emit(st: _State, op: dict) -> None:
     if op.get("fused"):
         return  # emitted inside the op it was fused into
+    op["_emitted"] = True
     P, B, bf = st.prog, st.batch, st.profile in ("bf16", "fp16", "fp8", "mixed")
     T16 = st.t16
     k = op["kind"]
@@ -583,11 +607,25 @@ def _emit(st: _State, op: dict) -> None:
             cp.has_residual, cp.act, cp.block_n = int(res is not None), op["act"], 0
             # C3B200_CONV_MODE=1 forces one TMA window per tap (A/B comparisons)
             cp.mode = int(os.environ.get("C3B200_CONV_MODE", "0"))
+            sc = _conv_shortcut(st, op, H, W, geo, O)
+            extra_in, extra_out = [], []
+            if sc is not None:
+                # the downsampling shortcut rides along: ws [O, C], bs, output [N*Ho*Wo, O]
+                sc["fused"] = True
+                cp.has_shortcut = 1
+                wsn = st.weight("conv", st.bits16(np.ascontiguousarray(sc["w"].reshape(O, C))), T16)
+                bsn = st.weight("bias", sc["b"].astype(np.float32), L.F32)
+                P.add_tensor(sc["out"], (N * Ho * Wo, O), T16)
+                st.layout[sc["out"]] = "nhwc"
+                st.lshape[sc["out"]] = (N, O, Ho, Wo)
+                extra_in, extra_out = [wsn, bsn], [sc["out"]]
+                flops += 2.0 * N * Ho * Wo * O * C
 
-            def build(d, x=x, wname=wname, bname=bname, res=res, out=out, cp=cp):
-                ins = [d[x].t(), d[wname].t(), d[bname].t()] + ([d[res].t()] if res else [])
-                return [Launch(L.K_CONV_TC, ins, [d[out].t()], cp)]
-            P.add_step("conv_tc", [x, wname, bname] + ([res] if res else []), [out], build, flops)
+            def build(d, x=x, wname=wname, bname=bname, res=res, out=out, cp=cp, ei=extra_in, eo=extra_out):
+                ins = [d[x].t(), d[wname].t(), d[bname].t()] + ([d[res].t()] if res else []) + [d[e].t() for e in ei]
+                return [Launch(L.K_CONV_TC, ins, [d[out].t()] + [d[e].t() for e in eo], cp)]
+            P.add_step("conv_tc", [x, wname, bname] + ([res] if res else []) + extra_in, [out] + extra_out, build,
+                       flops)
             st.layout[out] = "nhwc"
         st.lshape[out] = (N, O, Ho, Wo)
     elif k == "gap":

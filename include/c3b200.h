@@ -207,7 +207,12 @@ typedef struct {
  * inputs: x [N,H,W,Cin] bf16, w [Cout, kh, kw, Cin] bf16, bias f32 [Cout],
  * [residual [N,Ho,Wo,Cout] bf16] ; output y [N,Ho,Wo,Cout] bf16.
  * Cin % 64 == 0, Cout % 32 == 0, stride 1 or 2 (H, W even for stride 2),
- * square kernel, symmetric padding. */
+ * square kernel, symmetric padding.
+ * has_shortcut = 1 (stride 2, pad = k / 2, Cout 64 or 128): the launch also
+ * computes the 1x1 stride-2 convolution of the same input (a residual block's
+ * downsampling shortcut), which samples exactly the pixels of the centre tap.
+ * Two more inputs follow: ws [Cout, Cin] bf16, bs [Cout] f32; and a second
+ * output ys [N,Ho,Wo,Cout] bf16 = conv1x1(x) + bs with no activation. */
 typedef struct {
   int32_t n, h, w, cin, cout, ho, wo, k, stride, pad;
   int32_t has_residual, act, block_n;
@@ -215,6 +220,7 @@ typedef struct {
                    tiles (3x3 s1 p1, Cout <= 128, weights resident when they fit), else one TMA
                    window per tap; 1: one TMA window per tap; 2: halo tiles, streamed weights;
                    3: halo tiles, resident weights, no row ring */
+  int32_t has_shortcut;
 } c3b_conv_tc_params;
 
 /* --- C3B_K_FLASH_ATTN: qkv [B, S, 3, H, D] (f32 or bf16) -> out [B, S, H*D].

@@ -339,6 +339,62 @@ def test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res, mode):
     assert rel(got, ref) < 8e-3
 
 
+@pytest.mark.parametrize("n,h,cin,cout,k,stride,res", [(160, 32, 64, 128, 3, 2, 0), (160, 32, 64, 128, 1, 2, 1),
+                                                       (300, 16, 256, 512, 1, 2, 0), (150, 16, 128, 256, 1, 2, 1)])
+def test_conv_tc_resident_weights(torch_cuda, n, h, cin, cout, k, stride, res):
+    """Stride-2 convolutions with at least two tiles per SM: tc_gemm_kernel
+    stages the whole weight block once per CTA (one or two column blocks)."""
+    test_conv_tc(torch_cuda, n, h, cin, cout, k, stride, res, 0)
+
+
+@pytest.mark.parametrize("n,h,cin,cout,h16", [(8, 32, 64, 128, 0), (160, 32, 64, 128, 0), (6, 16, 128, 64, 0),
+                                               (5, 8, 64, 128, 1)])
+def test_conv_tc_fused_shortcut(torch_cuda, n, h, cin, cout, h16):
+    """3x3 stride-2 conv + ReLU with the block's 1x1 stride-2 shortcut in the
+    same launch (has_shortcut): both outputs against the oracle's two convs."""
+    import torch
+    from hackathon_b200 import _lib as L
+    rnd = _round_f16 if h16 else round_bf16
+    t16, conv = (L.F16, lambda a: _f16(torch, a)) if h16 else (L.BF16, lambda a: _bf16(torch, a))
+    x = rnd(randn(n, cin, h, h))
+    w = rnd(randn(cout, cin, 3, 3) * 0.05)
+    ws = rnd(randn(cout, cin, 1, 1) * 0.1)
+    b, bs = randn(cout), randn(cout)
+    ref = np.maximum(O.conv2d(x, w, b, strides=[2, 2], pads=[1] * 4), 0)
+    ref_s = O.conv2d(x, ws, bs, strides=[2, 2], pads=[0] * 4)
+    ho = h // 2
+    xn, wn = conv(x.transpose(0, 2, 3, 1)), conv(w.transpose(0, 2, 3, 1))
+    wsn = conv(ws.reshape(cout, cin))
+    tb, tbs = dev(torch, b), dev(torch, bs)
+    dt = torch.float16 if h16 else torch.bfloat16
+    out = torch.empty((n, ho, ho, cout), dtype=dt, device="cuda")
+    out_s = torch.full((n, ho, ho, cout), float("nan"), dtype=dt, device="cuda")
+    cp = L.ConvTcParams()
+    cp.n, cp.h, cp.w, cp.cin, cp.cout, cp.ho, cp.wo, cp.k, cp.stride, cp.pad = n, h, h, cin, cout, ho, ho, 3, 2, 1
+    cp.has_residual, cp.act, cp.block_n, cp.mode, cp.has_shortcut = 0, 1, 0, 0, 1
+    ins = [L.make_tensor(xn.data_ptr(), t16, (n, h, h, cin)), L.make_tensor(wn.data_ptr(), t16, (cout, 3, 3, cin)),
+           L.make_tensor(tb.data_ptr(), L.F32, (cout,)), L.make_tensor(wsn.data_ptr(), t16, (cout, cin)),
+           L.make_tensor(tbs.data_ptr(), L.F32, (cout,))]
+    outs = [L.make_tensor(out.data_ptr(), t16, (n, ho, ho, cout)), L.make_tensor(out_s.data_ptr(), t16, (n, ho, ho, cout))]
+    L.launch(L.K_CONV_TC, ins, outs, cp, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    got = out.float().cpu().numpy().transpose(0, 3, 1, 2)
+    got_s = out_s.float().cpu().numpy().transpose(0, 3, 1, 2)
+    assert rel(got, ref) < 8e-3
+    assert rel(got_s, ref_s) < 8e-3
+    # the same shortcut as its own launch gives the same bits (one K block of
+    # four MMAs either way)
+    cp1 = L.ConvTcParams()
+    cp1.n, cp1.h, cp1.w, cp1.cin, cp1.cout, cp1.ho, cp1.wo, cp1.k, cp1.stride, cp1.pad = n, h, h, cin, cout, ho, ho, 1, 2, 0
+    cp1.has_residual, cp1.act, cp1.block_n, cp1.mode = 0, 0, 0, 0
+    alone = torch.empty_like(out_s)
+    L.launch(L.K_CONV_TC, [ins[0], L.make_tensor(wsn.data_ptr(), t16, (cout, 1, 1, cin)), ins[4]],
+             [L.make_tensor(alone.data_ptr(), t16, (n, ho, ho, cout))], cp1, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(alone, out_s)
+
+
 @pytest.mark.parametrize("shift", [0, 64])
 def test_conv_tc_rowslide_residual_offsets(torch_cuda, shift):
     """Stage-1 convolution with a residual (sliding-window kernel) on operands

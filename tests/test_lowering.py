@@ -49,7 +49,8 @@ def _check_arena(prog):
 @pytest.mark.parametrize("model,batch,profile,kinds", [
     ("mlp", 256, "fp32", {L.K_GEMM: 3}),
     ("resnet18", 64, "fp32", {L.K_CONV: 20, L.K_REDUCE: 1, L.K_GEMM: 1}),
-    ("resnet18", 64, "bf16", {L.K_STEM_CONV: 1, L.K_CONV_TC: 19, L.K_GAP_NHWC: 1}),  # GAP + classifier fused
+    # GAP + classifier fused; the stage-2 downsampling shortcut rides in its 3x3 stride-2 conv
+    ("resnet18", 64, "bf16", {L.K_STEM_CONV: 1, L.K_CONV_TC: 18, L.K_GAP_NHWC: 1}),
     ("tx_small", 8, "fp32", {L.K_EMBED: 1, L.K_LAYERNORM: 9, L.K_GEMM: 17, L.K_FLASH_ATTN: 4, L.K_COPY: 1}),
     ("tx_small", 8, "bf16", {L.K_EMBED: 1, L.K_LAYERNORM: 9, L.K_GEMM_TC: 16, L.K_GEMM_TF32: 1, L.K_FLASH_ATTN: 4,
                              L.K_COPY: 1}),
@@ -64,6 +65,18 @@ def test_lowering_fuses_to_expected_kernels(model, batch, profile, kinds):
     _check_arena(prog)
     assert prog.outputs == ["logits"]
     assert prog.tensors["logits"].dtype == L.F32
+
+
+def test_shortcut_fused_into_stride2_conv():
+    """The 64->128 stride-2 stage entry launches once with both outputs; the
+    128- and 256-channel entries (CTA pairs) keep their own shortcut launch."""
+    prog = lower(BUILDERS["resnet18"](), 8, "bf16")
+    fused = [ln for ln in _launches(prog) if ln.kid == L.K_CONV_TC and ln.params.has_shortcut]
+    assert len(fused) == 1
+    (ln,) = fused
+    assert ln.params.stride == 2 and ln.params.k == 3 and ln.params.cout == 128
+    assert len(ln.ins) == 5 and len(ln.outs) == 2
+    assert [ln.ins[3].shape[i] for i in range(2)] == [128, 64]
 
 
 def test_flop_accounting_per_image():
