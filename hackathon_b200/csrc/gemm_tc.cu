@@ -77,6 +77,12 @@ struct TcArgs {
   // tc_gemm_kernel: bf16 output through per-warp shared-memory tiles and TMA
   // stores (maps.out: 16 columns x 32 rows, 32-byte swizzle)
   int tma_out;
+  // 16-bit format of A, B and every 16-bit output / residual: 0 bf16, 1 fp16
+  int h16;
+  // optional wait counters of the row-ring kernel (C3B200_CONV_PROF=1), else null
+  unsigned long long* prof;
+  // (the fields below sit last: placed earlier they changed the register
+  // allocation of the other tc_gemm_kernel variants into spills)
   // fused 1x1 stride-2 shortcut (tc_gemm_kernel<0, 1>, convolutions): aux_n
   // more accumulator columns per tile, fed by the centre tap's K blocks
   // [aux_kb0, aux_kb0 + cblocks) against aux_w [aux_n][cin] (resident in
@@ -85,10 +91,6 @@ struct TcArgs {
   const uint16_t* aux_w;
   const float* aux_bias;
   uint16_t* aux_out;
-  // 16-bit format of A, B and every 16-bit output / residual: 0 bf16, 1 fp16
-  int h16;
-  // optional wait counters of the row-ring kernel (C3B200_CONV_PROF=1), else null
-  unsigned long long* prof;
 };
 
 // Row-ring wait-profiler slots (cycles summed over CTAs; epilogue slots over warps).
@@ -396,8 +398,6 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      const long long gp0 = a.prof ? clock64() : 0;
-      long long gp_empty = 0;
       if (bres && cid < a.n_tiles) {
         // every tile of this CTA has column block cid % n_tiles_n (the grid is
         // a multiple of n_tiles_n)
@@ -415,9 +415,7 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
           oh0 = (m0 % a.pix) / a.wo;
         }
         for (int kb = 0; kb < a.k_blocks; ++kb) {
-          const long long gw = a.prof ? clock64() : 0;
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 11)) goto producer_done;
-          if (a.prof) gp_empty += clock64() - gw;
           uint8_t* dA = sa + (size_t)stage * a_bytes;
           uint8_t* dB = sb + (size_t)stage * b_bytes;
           if (W4) {
@@ -473,10 +471,6 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
           if (++stage == stages) { stage = 0; phase ^= 1; }
         }
       }
-      if (a.prof) {
-        atomicAdd(&a.prof[RP_PROD_TOTAL], (unsigned long long)(clock64() - gp0));
-        atomicAdd(&a.prof[RP_PROD_EMPTY], (unsigned long long)gp_empty);
-      }
     producer_done:;
     }
   } else if (warp == 1) {
@@ -493,22 +487,16 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      const long long gm0 = a.prof ? clock64() : 0;
-      long long gm_te = 0, gm_full = 0;
       bool b_ok = !bres || cid >= a.n_tiles || mbar_wait(&bready[0], 0, abort_flag, 17);
       for (int t = cid; t < a.n_tiles && b_ok; t += ncl) {
-        long long gw = a.prof ? clock64() : 0;
         if (!(CG == 2 ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, abort_flag, 12)
                       : mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 12)))
           break;
-        if (a.prof) gm_te += clock64() - gw;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)acc * ACC_COLS;
         bool ok = true;
         for (int kb = 0; kb < a.k_blocks; ++kb) {
-          gw = a.prof ? clock64() : 0;
           if (!mbar_wait(W4 ? &bready[stage] : &full[stage], phase, abort_flag, 13)) { ok = false; break; }
-          if (a.prof) gm_full += clock64() - gw;
           tc_fence_after();
           const uint64_t ad = ad0 + (uint64_t)stage * (a_bytes >> 4);
           const uint64_t bd = bd0 + (uint64_t)(bres ? kb : stage) * (b_bytes >> 4);
@@ -544,11 +532,6 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
         else
           mma_commit(&tfull[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-      }
-      if (a.prof) {
-        atomicAdd(&a.prof[RP_MMA_TOTAL], (unsigned long long)(clock64() - gm0));
-        atomicAdd(&a.prof[RP_MMA_RFULL], (unsigned long long)gm_full);
-        atomicAdd(&a.prof[RP_MMA_TEMPTY], (unsigned long long)gm_te);
       }
     }
   } else if (W4 && warp >= 2 + EPIW) {
@@ -2141,42 +2124,8 @@ static int enable_tma_out(tc::TmaMaps& maps, tc::TcArgs& a) {
   return C3B_OK;
 }
 
-// Wait profiler of tc_gemm_kernel (C3B200_GEMM_PROF=1, measurement runs only):
-// cycles summed over CTAs, printed after a synchronous launch.
-static unsigned long long* gemm_prof_buf() {
-  static unsigned long long* buf = [] {
-    const char* e = getenv("C3B200_GEMM_PROF");
-    unsigned long long* b = nullptr;
-    if (e && e[0] == '1' && cudaMalloc(&b, tc::RP_COUNT * sizeof(unsigned long long)) != cudaSuccess) b = nullptr;
-    return b;
-  }();
-  return buf;
-}
-
-static int gemm_prof_report(const tc::TcArgs& a, int ctas, cudaStream_t s) {
-  unsigned long long h[tc::RP_COUNT];
-  C3B_CHECK_CUDA(cudaStreamSynchronize(s));
-  C3B_CHECK_CUDA(cudaMemcpy(h, a.prof, sizeof(h), cudaMemcpyDeviceToHost));
-  const int issuers = a.cg == 2 ? ctas / 2 : ctas;
-  const double tiles = (double)a.n_tiles / issuers;
-  fprintf(stderr,
-          "[gemm prof] M %lld N %lld K %lld block_n %d cg %d stages %d | per CTA: prod %.0f (empty-wait %.0f) | "
-          "mma %.0f (full-wait %.0f tempty-wait %.0f) | epi tfull-wait per warp %.0f | tiles/issuer %.1f | "
-          "per k-block: mma %.0f full-wait %.0f\n",
-          (long long)a.M, (long long)a.N, (long long)a.K, a.block_n, a.cg, a.stages, (double)h[tc::RP_PROD_TOTAL] / ctas,
-          (double)h[tc::RP_PROD_EMPTY] / ctas, (double)h[tc::RP_MMA_TOTAL] / issuers,
-          (double)h[tc::RP_MMA_RFULL] / issuers, (double)h[tc::RP_MMA_TEMPTY] / issuers,
-          (double)h[tc::RP_EPI_TFULL] / (16.0 * ctas), tiles, (double)h[tc::RP_MMA_TOTAL] / issuers / (tiles * a.k_blocks),
-          (double)h[tc::RP_MMA_RFULL] / issuers / (tiles * a.k_blocks));
-  return C3B_OK;
-}
-
 template <int MODE, int CG = 1, bool AUX = false>
 static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s) {
-  if (unsigned long long* pb = gemm_prof_buf()) {
-    C3B_CHECK_CUDA(cudaMemsetAsync(pb, 0, tc::RP_COUNT * sizeof(unsigned long long), s));
-    a.prof = pb;
-  }
   // one 128-byte K row per operand row; MODE 2 adds the packed FP4 tile and its scales
   const size_t b_stage = (size_t)(a.block_n / CG) * 128;
   if (MODE != 0 || CG != 1) a.bres = 0;
@@ -2235,13 +2184,13 @@ static int launch_tc_mode(const tc::TmaMaps& maps, tc::TcArgs& a, cudaStream_t s
                                     a))
       return rc;
     C3B_CHECK_CUDA(cudaGetLastError());
-    return a.prof ? gemm_prof_report(a, 2 * clusters, s) : C3B_OK;
+    return C3B_OK;
   }
   int grid = a.n_tiles < sm_count() ? a.n_tiles : sm_count();
   if (grid < 1) return C3B_OK;
   if (int rc = launch_pdl(tc::tc_gemm_kernel<MODE, CG, AUX>, grid, tc::HALO16_THREADS, smem, s, maps, a)) return rc;
   C3B_CHECK_CUDA(cudaGetLastError());
-  return a.prof ? gemm_prof_report(a, grid, s) : C3B_OK;
+  return C3B_OK;
 }
 
 // CTA pairs for bf16/fp16 GEMMs and convolutions through tc_gemm_kernel with
