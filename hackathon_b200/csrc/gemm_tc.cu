@@ -2788,6 +2788,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor* outs, const
     // are the centre tap's, and it becomes aux_n more columns of each tile
     const c3b_tensor &ws = in[n_main], &bs = in[n_main + 1], &ys = outs[1];
     C3B_REQUIRE(p.stride == 2 && p.k % 2 == 1 && p.pad == p.k / 2, "tc conv shortcut: stride 2, pad k/2");
+    C3B_REQUIRE(!p.has_residual, "tc conv shortcut: the main convolution takes no residual");
     C3B_REQUIRE(a.n_tiles_n == 1 && a.block_n == p.cout && (p.cout == 64 || p.cout == 128),
                 "tc conv shortcut: Cout 64 or 128 (one column block)");
     C3B_REQUIRE(ws.dtype == in[0].dtype && numel(ws) == (int64_t)p.cout * p.cin, "tc conv shortcut: ws [Cout, Cin]");

@@ -1046,30 +1046,31 @@ __global__ void gap_nhwc_kernel(const void* __restrict__ x, int dt, float* __res
 }
 
 // GAP followed by the classifier, for the 16-bit convolution profiles:
-// y[n][j] = b[j] + sum_c w[j][c] * mean_p x[n][p][c].  One warp per image
-// (every warp of a launch resident at once up to ~9k images); lane l owns the
-// 8-channel chunks l + 32k.  The pixel rows are read in batches of 16
-// independent 16-byte loads per lane (two DRAM round trips for a 4x4x512 map
-// instead of one per pixel), summed in registers, and each classifier row
-// (staged in shared memory) is reduced across the warp.  Replaces
-// GlobalAveragePool -> Flatten -> Gemm (c35/engine.py op_global_avgpool,
-// op_gemm) with one launch and one pass over the activation.
+// y[n][j] = b[j] + sum_c w[j][c] * mean_p x[n][p][c].  One warp per image,
+// four per block (every warp of a launch resident at once up to ~9k images);
+// lane l owns the 8-channel chunks l + 32k.  The pixel rows are read in
+// batches of 16 independent 16-byte loads per lane (two DRAM round trips for
+// a 4x4x512 map instead of one per pixel), summed in registers, and each
+// classifier row (read through L1, shared by all warps of the SM) is reduced
+// across the warp.  Replaces GlobalAveragePool -> Flatten -> Gemm
+// (c35/engine.py op_global_avgpool, op_gemm) with one launch and one pass
+// over the activation.
 constexpr int GAP_FC_MAX_CHUNKS = 4;  // C <= 1024
 constexpr int GAP_FC_BATCH = 16;      // 16-byte loads in flight per lane
+constexpr int GAP_FC_WARPS = 4;       // warps (images) per block
 
 template <int NCH>
-__global__ void __launch_bounds__(256) gap_fc_kernel(const uint4* __restrict__ x, int h16, const float* __restrict__ w,
-                                                     const float* __restrict__ b, float* __restrict__ y,
-                                                     c3b_gap_params p, int classes) {
-  extern __shared__ float4 sw4[];  // classes x C f32
-  constexpr int C8 = NCH * 32;     // 16-byte chunks per pixel row
+__global__ void __launch_bounds__(GAP_FC_WARPS * 32) gap_fc_kernel(const uint4* __restrict__ x, int h16,
+                                                                   const float* __restrict__ w,
+                                                                   const float* __restrict__ b,
+                                                                   float* __restrict__ y, c3b_gap_params p,
+                                                                   int classes) {
+  constexpr int C8 = NCH * 32;             // 16-byte chunks per pixel row
   constexpr int PXB = GAP_FC_BATCH / NCH;  // pixels per load batch
-  for (int i = threadIdx.x; i < classes * C8 * 2; i += blockDim.x) sw4[i] = reinterpret_cast<const float4*>(w)[i];
-  __syncthreads();
-  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int hw = (int)p.hw;
   const float inv = 1.0f / (float)p.hw;
-  for (int64_t n = (int64_t)blockIdx.x * wpb + wib; n < p.n; n += (int64_t)gridDim.x * wpb) {
+  for (int64_t n = (int64_t)blockIdx.x * GAP_FC_WARPS + wib; n < p.n; n += (int64_t)gridDim.x * GAP_FC_WARPS) {
     float acc[NCH * 8];
 #pragma unroll
     for (int i = 0; i < NCH * 8; ++i) acc[i] = 0.f;
@@ -1095,8 +1096,8 @@ __global__ void __launch_bounds__(256) gap_fc_kernel(const uint4* __restrict__ x
       float sacc = 0.f;
 #pragma unroll
       for (int k = 0; k < NCH; ++k) {
-        const float4* wr = sw4 + ((size_t)j * C8 * 8 + (size_t)(lane + 32 * k) * 8) / 4;
-        const float4 w0 = wr[0], w1 = wr[1];
+        const float4* wr = reinterpret_cast<const float4*>(w + (size_t)j * C8 * 8 + (size_t)(lane + 32 * k) * 8);
+        const float4 w0 = __ldg(wr), w1 = __ldg(wr + 1);
         sacc += acc[8 * k] * w0.x + acc[8 * k + 1] * w0.y + acc[8 * k + 2] * w0.z + acc[8 * k + 3] * w0.w +
                 acc[8 * k + 4] * w1.x + acc[8 * k + 5] * w1.y + acc[8 * k + 6] * w1.z + acc[8 * k + 7] * w1.w;
       }
@@ -1127,17 +1128,16 @@ int launch_gap_nhwc(const c3b_tensor* in, int n_in, const c3b_tensor& out, const
   C3B_REQUIRE(numel(out) >= p.n * classes, "gap + classifier: output extents");
   C3B_REQUIRE(((uintptr_t)in[0].ptr & 15) == 0 && ((uintptr_t)in[1].ptr & 15) == 0, "gap + classifier: alignment");
   if (p.n == 0) return C3B_OK;
-  const int grid = (int)std::min<int64_t>((p.n + 7) / 8, (int64_t)sm_count() * 8);
-  const size_t smem = (size_t)classes * p.c * 4;
+  const int grid = (int)std::min<int64_t>((p.n + GAP_FC_WARPS - 1) / GAP_FC_WARPS, (int64_t)sm_count() * 16);
   const uint4* xp = (const uint4*)in[0].ptr;
   const float *wp = (const float*)in[1].ptr, *bp = n_in > 2 ? (const float*)in[2].ptr : nullptr;
   const int h16 = in[0].dtype == C3B_F16;
   float* yp = (float*)out.ptr;
   switch (p.c / 256) {
-    case 1: gap_fc_kernel<1><<<grid, 256, smem, s>>>(xp, h16, wp, bp, yp, p, classes); break;
-    case 2: gap_fc_kernel<2><<<grid, 256, smem, s>>>(xp, h16, wp, bp, yp, p, classes); break;
-    case 3: gap_fc_kernel<3><<<grid, 256, smem, s>>>(xp, h16, wp, bp, yp, p, classes); break;
-    default: gap_fc_kernel<4><<<grid, 256, smem, s>>>(xp, h16, wp, bp, yp, p, classes); break;
+    case 1: gap_fc_kernel<1><<<grid, GAP_FC_WARPS * 32, 0, s>>>(xp, h16, wp, bp, yp, p, classes); break;
+    case 2: gap_fc_kernel<2><<<grid, GAP_FC_WARPS * 32, 0, s>>>(xp, h16, wp, bp, yp, p, classes); break;
+    case 3: gap_fc_kernel<3><<<grid, GAP_FC_WARPS * 32, 0, s>>>(xp, h16, wp, bp, yp, p, classes); break;
+    default: gap_fc_kernel<4><<<grid, GAP_FC_WARPS * 32, 0, s>>>(xp, h16, wp, bp, yp, p, classes); break;
   }
   C3B_CHECK_CUDA(cudaGetLastError());
   return C3B_OK;

@@ -208,7 +208,7 @@ typedef struct {
  * [residual [N,Ho,Wo,Cout] bf16] ; output y [N,Ho,Wo,Cout] bf16.
  * Cin % 64 == 0, Cout % 32 == 0, stride 1 or 2 (H, W even for stride 2),
  * square kernel, symmetric padding.
- * has_shortcut = 1 (stride 2, pad = k / 2, Cout 64 or 128): the launch also
+ * has_shortcut = 1 (stride 2, pad = k / 2, Cout 64 or 128, no residual): the launch also
  * computes the 1x1 stride-2 convolution of the same input (a residual block's
  * downsampling shortcut), which samples exactly the pixels of the centre tap.
  * Two more inputs follow: ws [Cout, Cin] bf16, bs [Cout] f32; and a second
