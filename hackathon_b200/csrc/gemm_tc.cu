@@ -2530,6 +2530,26 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor* outs, const
   a.k_blocks = (int)(K / tc::BK);
   a.conv = 1; a.cblocks = p.cin / 64; a.ksz = p.k; a.stride = p.stride; a.pad = p.pad;
   a.pix = pix; a.wo = p.wo; a.cin = p.cin;
+  if (p.has_shortcut) {
+    // The 1x1 stride-2 shortcut samples the centre tap's pixels: its A blocks
+    // are the centre tap's, and it becomes aux_n more columns of each tile
+    // (checked here, before any CUDA call).
+    const c3b_tensor &ws = in[n_main], &bs = in[n_main + 1], &ys = outs[1];
+    C3B_REQUIRE(p.stride == 2 && p.k % 2 == 1 && p.pad == p.k / 2, "tc conv shortcut: stride 2, pad k/2");
+    C3B_REQUIRE(!p.has_residual, "tc conv shortcut: the main convolution takes no residual");
+    C3B_REQUIRE(a.n_tiles_n == 1 && a.block_n == p.cout && (p.cout == 64 || p.cout == 128),
+                "tc conv shortcut: Cout 64 or 128 (one column block)");
+    C3B_REQUIRE(ws.dtype == in[0].dtype && numel(ws) == (int64_t)p.cout * p.cin, "tc conv shortcut: ws [Cout, Cin]");
+    C3B_REQUIRE(bs.dtype == C3B_F32 && numel(bs) == p.cout, "tc conv shortcut: bs [Cout] f32");
+    C3B_REQUIRE(ys.dtype == in[0].dtype && numel(ys) == M * p.cout, "tc conv shortcut: ys [N, Ho, Wo, Cout] 16-bit");
+    C3B_REQUIRE(((uintptr_t)ws.ptr & 15) == 0 && ((uintptr_t)bs.ptr & 15) == 0 && ((uintptr_t)ys.ptr & 15) == 0,
+                "tc conv shortcut: 16-byte alignment");
+    a.aux_n = p.cout;
+    a.aux_kb0 = (p.pad * p.k + p.pad) * a.cblocks;
+    a.aux_w = static_cast<const uint16_t*>(ws.ptr);
+    a.aux_bias = static_cast<const float*>(bs.ptr);
+    a.aux_out = static_cast<uint16_t*>(ys.ptr);
+  }
   const uint32_t bw = (uint32_t)p.wo;
   const uint32_t bh = pix >= 128 ? 128u / bw : (uint32_t)p.ho;
   const uint32_t bn = pix >= 128 ? 1u : 128u / (uint32_t)pix;
@@ -2783,27 +2803,7 @@ int launch_conv_tc(const c3b_tensor* in, int n_in, const c3b_tensor* outs, const
         if ((rc = encode(&maps.a[pr * 2 + ps], base, 4, dims, str, box))) return rc;
       }
   }
-  if (p.has_shortcut) {
-    // the 1x1 stride-2 shortcut samples the centre tap's pixels: its A blocks
-    // are the centre tap's, and it becomes aux_n more columns of each tile
-    const c3b_tensor &ws = in[n_main], &bs = in[n_main + 1], &ys = outs[1];
-    C3B_REQUIRE(p.stride == 2 && p.k % 2 == 1 && p.pad == p.k / 2, "tc conv shortcut: stride 2, pad k/2");
-    C3B_REQUIRE(!p.has_residual, "tc conv shortcut: the main convolution takes no residual");
-    C3B_REQUIRE(a.n_tiles_n == 1 && a.block_n == p.cout && (p.cout == 64 || p.cout == 128),
-                "tc conv shortcut: Cout 64 or 128 (one column block)");
-    C3B_REQUIRE(ws.dtype == in[0].dtype && numel(ws) == (int64_t)p.cout * p.cin, "tc conv shortcut: ws [Cout, Cin]");
-    C3B_REQUIRE(bs.dtype == C3B_F32 && numel(bs) == p.cout, "tc conv shortcut: bs [Cout] f32");
-    C3B_REQUIRE(ys.dtype == in[0].dtype && numel(ys) == M * p.cout, "tc conv shortcut: ys [N, Ho, Wo, Cout] 16-bit");
-    C3B_REQUIRE(((uintptr_t)ws.ptr & 15) == 0 && ((uintptr_t)bs.ptr & 15) == 0 && ((uintptr_t)ys.ptr & 15) == 0,
-                "tc conv shortcut: 16-byte alignment");
-    a.aux_n = p.cout;
-    a.aux_kb0 = (p.pad * p.k + p.pad) * a.cblocks;
-    a.aux_w = static_cast<const uint16_t*>(ws.ptr);
-    a.aux_bias = static_cast<const float*>(bs.ptr);
-    a.aux_out = static_cast<uint16_t*>(ys.ptr);
-  } else if ((rc = use_pairs(maps, a, in[1].ptr, (uint64_t)K, (uint64_t)p.cout))) {
-    return rc;
-  }
+  if (!p.has_shortcut && (rc = use_pairs(maps, a, in[1].ptr, (uint64_t)K, (uint64_t)p.cout))) return rc;
   if ((rc = enable_tma_out(maps, a))) return rc;
   use_resident_b(a);
   return launch_tc(maps, a, s);

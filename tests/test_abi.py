@@ -106,3 +106,32 @@ def test_invalid_launch_reports_error_without_gpu_work():
     size returns C3B_E_INVALID with a message."""
     with pytest.raises(RuntimeError, match="parameter block size"):
         L.launch(L.K_EW, [L.make_tensor(1, L.F32, (4,))], [L.make_tensor(1, L.F32, (4,))], L.CopyParams())
+
+
+@pytest.mark.parametrize("change,match", [
+    ({"has_residual": 1}, "takes no residual"),
+    ({"stride": 1, "ho": 32, "wo": 32}, "stride 2, pad k/2"),
+    ({"cout": 256}, "Cout 64 or 128"),
+    ({"ws_shape": (128, 32)}, r"ws \[Cout, Cin\]"),
+])
+def test_fused_shortcut_arguments_checked_without_gpu_work(change, match):
+    """C3B_K_CONV_TC with has_shortcut: the shortcut's conditions (stride 2, no
+    residual, one column block of Cout 64 or 128, ws [Cout, Cin]) are checked
+    before any CUDA call; the pointers are never dereferenced."""
+    c = {"n": 2, "h": 32, "cin": 64, "cout": 128, "stride": 2, "ho": 16, "wo": 16, "has_residual": 0,
+         "ws_shape": None}
+    c.update(change)
+    n, h, cin, cout, ho = c["n"], c["h"], c["cin"], c["cout"], c["ho"]
+    cp = L.ConvTcParams()
+    cp.n, cp.h, cp.w, cp.cin, cp.cout, cp.ho, cp.wo = n, h, h, cin, cout, ho, c["wo"]
+    cp.k, cp.stride, cp.pad = 3, c["stride"], 1
+    cp.has_residual, cp.act, cp.block_n, cp.mode, cp.has_shortcut = c["has_residual"], 1, 0, 0, 1
+    ptr = iter(range(1 << 20, 64 << 20, 1 << 20))  # 16-byte aligned, never dereferenced
+    t = lambda dt, shape: L.make_tensor(next(ptr), dt, shape)  # noqa: E731
+    ins = [t(L.BF16, (n, h, h, cin)), t(L.BF16, (cout, 3, 3, cin)), t(L.F32, (cout,))]
+    if c["has_residual"]:
+        ins.append(t(L.BF16, (n, ho, ho, cout)))
+    ins += [t(L.BF16, c["ws_shape"] or (cout, cin)), t(L.F32, (cout,))]
+    outs = [t(L.BF16, (n, ho, ho, cout)), t(L.BF16, (n, ho, ho, cout))]
+    with pytest.raises(RuntimeError, match=match):
+        L.launch(L.K_CONV_TC, ins, outs, cp)
