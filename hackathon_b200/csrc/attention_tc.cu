@@ -212,6 +212,9 @@ __global__ void __launch_bounds__(THREADS, CTAS_PER_SM) flash_tc_kernel(const __
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // every CTA of this persistent grid is resident: the next kernel may launch
+  // onto SMs as they free up (it waits on griddepcontrol before its activations)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int H = a.heads;
   if (warp == 0) {

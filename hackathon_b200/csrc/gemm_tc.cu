@@ -392,6 +392,9 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   // maps, constant weights) may overlap the previous kernel's tail; every
   // activation read and every global write comes after it has completed.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // every CTA of this persistent grid is resident: the next kernel may launch
+  // onto SMs as they free up (it waits on griddepcontrol before its activations)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -870,6 +873,9 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_conv_halo_kernel(const _
   // maps, constant weights) may overlap the previous kernel's tail; every
   // activation read and every global write comes after it has completed.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // every CTA of this persistent grid is resident: the next kernel may launch
+  // onto SMs as they free up (it waits on griddepcontrol before its activations)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1145,6 +1151,9 @@ __global__ void __launch_bounds__(HALO_THREADS, 1) tc_conv_rowring_kernel(const 
   // maps, constant weights) may overlap the previous kernel's tail; every
   // activation read and every global write comes after it has completed.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // every CTA of this persistent grid is resident: the next kernel may launch
+  // onto SMs as they free up (it waits on griddepcontrol before its activations)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1484,6 +1493,9 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // every CTA of this persistent grid is resident: the next kernel may launch
+  // onto SMs as they free up (it waits on griddepcontrol before its activations)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1833,6 +1845,9 @@ __global__ void __launch_bounds__(IMG ? STEM_IMG_THREADS : STEM_THREADS, 1)
   // maps, constant weights) may overlap the previous kernel's tail; every
   // activation read and every global write comes after it has completed.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // every CTA of this persistent grid is resident: the next kernel may launch
+  // onto SMs as they free up (it waits on griddepcontrol before its activations)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int HW = g.ho * g.wo;
   long long pc[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // wait profiler (prof != null), per thread
   // IMG: the CTA's i-th tile is tile i % tpi of its (i / tpi)-th image
