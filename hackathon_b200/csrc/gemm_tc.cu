@@ -388,6 +388,15 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
   if (CG == 2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (bres && warp == 0 && lane == 0 && cid < a.n_tiles) {
+    // resident B (constant weights, so before the dependency wait): every tile
+    // of this CTA has column block cid % n_tiles_n (the grid is a multiple of
+    // n_tiles_n)
+    const int n0 = (cid % a.n_tiles_n) * a.block_n;
+    mbar_arrive_tx(&bready[0], (uint32_t)a.k_blocks * b_bytes);
+    for (int kb = 0; kb < a.k_blocks; ++kb)
+      tma_load_2d(sb + (size_t)kb * b_bytes, &maps.b, &bready[0], kb * BK, n0);
+  }
   // Programmatic dependent launch: the prologue above (barriers, TMEM, tensor
   // maps, constant weights) may overlap the previous kernel's tail; every
   // activation read and every global write comes after it has completed.
@@ -401,14 +410,6 @@ __global__ void __launch_bounds__(HALO16_THREADS, 1) tc_gemm_kernel(const __grid
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      if (bres && cid < a.n_tiles) {
-        // every tile of this CTA has column block cid % n_tiles_n (the grid is
-        // a multiple of n_tiles_n)
-        const int n0 = (cid % a.n_tiles_n) * a.block_n;
-        mbar_arrive_tx(&bready[0], (uint32_t)a.k_blocks * b_bytes);
-        for (int kb = 0; kb < a.k_blocks; ++kb)
-          tma_load_2d(sb + (size_t)kb * b_bytes, &maps.b, &bready[0], kb * BK, n0);
-      }
       for (int t = cid; t < a.n_tiles; t += ncl) {
         const int mb = t / a.n_tiles_n, nb = t % a.n_tiles_n;
         const int m0 = (mb * CG + (int)rank) * BM, n0 = nb * a.block_n + (int)rank * (a.block_n / CG);
@@ -1492,6 +1493,12 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (warp == 0 && lane == 0) {
+    // the 9 weight taps are constants: loaded before the dependency wait
+    mbar_arrive_tx(&wfull[0], 9u * b_bytes);
+    for (int tap = 0; tap < 9; ++tap)
+      tma_load_2d(sb + (size_t)((tap % 3) * 3 + 2 - tap / 3) * b_bytes, &maps.b, &wfull[0], tap * a.cin, 0);
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // every CTA of this persistent grid is resident: the next kernel may launch
   // onto SMs as they free up (it waits on griddepcontrol before its activations)
@@ -1499,9 +1506,6 @@ __global__ void __launch_bounds__(SLIDE_THREADS, 1) tc_conv_rowslide_kernel(cons
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_tx(&wfull[0], 9u * b_bytes);
-      for (int tap = 0; tap < 9; ++tap)
-        tma_load_2d(sb + (size_t)((tap % 3) * 3 + 2 - tap / 3) * b_bytes, &maps.b, &wfull[0], tap * a.cin, 0);
       uint32_t c = 0;
       const long long pt0 = a.prof ? clock64() : 0;
       long long pw = 0;
