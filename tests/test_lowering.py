@@ -79,6 +79,19 @@ def test_shortcut_fused_into_stride2_conv():
     assert [ln.ins[3].shape[i] for i in range(2)] == [128, 64]
 
 
+def test_shortcut_fusion_switch(monkeypatch):
+    """C3B200_CONV_SHORTCUT=0 keeps the 64->128 shortcut as its own launch:
+    19 tcgen05 conv launches, none with a second output, the same FLOPs."""
+    fused = lower(BUILDERS["resnet18"](), 8, "bf16")
+    monkeypatch.setenv("C3B200_CONV_SHORTCUT", "0")
+    prog = lower(BUILDERS["resnet18"](), 8, "bf16")
+    lns = [ln for ln in _launches(prog) if ln.kid == L.K_CONV_TC]
+    assert len(lns) == 19 and not any(ln.params.has_shortcut for ln in lns)
+    assert all(len(ln.outs) == 1 for ln in lns)
+    assert abs(sum(s.flops for s in prog.steps) - sum(s.flops for s in fused.steps)) < 1.0
+    _check_arena(prog)
+
+
 def test_flop_accounting_per_image():
     """ResNet-18 conv GEMMs: 1.1108 GFLOP per image (the figure roofline.achieved uses)."""
     p = lower(BUILDERS["resnet18"](), 16, "bf16")
